@@ -1,0 +1,347 @@
+#!/usr/bin/env python
+"""bench.py — the headline measurement: one DiffusionGemma W4A16 MoE layer on a 256-token canvas
+(configs[1]: fused RMSNorm -> router with the Zipf bias -> 128-expert top-8 MoE) in microseconds
+and HBM GB/s, plus the configs[2] sampler step in microseconds.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints ONE JSON line on rank 0.  `value` is microseconds per canvas-layer for the whole job (lower
+is better); for N > 1 every rank runs its own canvas through its own copy of the layer (replicas),
+so value = max-over-ranks time / (N * K).  Inputs are synthetic (workloads.py) with the BASELINE
+shapes and distributions; four distinct weight sets (4 x 416 MB) rotate between steps so every
+step streams its weights from HBM, not L2.
+
+--impl reference times the reference algorithm's CPU implementation (the oracle restatement of the
+reference's torch path) on the host cores, rank 0 only, on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+REPO = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "knivesysl-diffusion-xe_b200" / "kernels"))
+sys.path.insert(0, str(REPO))
+
+import torch  # noqa: E402
+
+METRIC = json.loads((REPO / "BASELINE.json").read_text())["metric"]
+T, H, I, E, TOPK = 256, 2816, 704, 128, 8
+V_SAMPLER = 262144
+NSETS = 4
+# DRAM bytes per launch of the dominant kernel (gate_up+GELU GEMM) from one ncu capture of the
+# configs[1] layer (see profiles/); None until a capture exists for the current kernel.
+GEMM1_NCU_TRAFFIC = None
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# --------------------------------------------------------------------------------- clocks
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(index), f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.15)
+        self.p.terminate()
+        self.p.wait()
+        self.f.flush()
+        rows = [ln.split(",") for ln in open(self.f.name).read().splitlines() if ln.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for n, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(n)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------------- workloads
+def build_layer(dev):
+    import workloads
+    sets = []
+    for i in range(NSETS):
+        sets.append(workloads.moe_weights(E, H, I, seed=100 + i, device=dev))
+    inp = workloads.moe_inputs(T, H, E, seed=0, device=dev)
+    return sets, inp
+
+
+def layer_step(W, inp, xn, xp):
+    """configs[1] step: fused RMSNorm (also writes the MoE K-interleave copy) -> router -> MoE."""
+    import fused_moe_w4_v2
+    import fused_rmsnorm
+    import moe_router
+    y_norm = fused_rmsnorm.fused_rmsnorm(inp["hidden"], inp["norm_w"], 1e-6, xperm=xp)
+    ids, w, _ = moe_router.route_topk(y_norm, inp["router_w"], TOPK, bias=inp["bias"],
+                                      want_logits=False)
+    return fused_moe_w4_v2.moe_forward(y_norm, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"],
+                                       W["dn_s"], W["dn_z"], ids, w, hidden_perm=xp), ids
+
+
+LAUNCHES_PER_LAYER = 7  # rmsnorm, router logits, router top-k, align, gate_up, down, combine
+
+
+def time_layer(dev, steps, warmup, dist):
+    import _knx
+    sets, inp = build_layer(dev)
+    xp = torch.empty(T, H, dtype=torch.float16, device=dev)
+    for i in range(warmup):
+        layer_step(sets[i % NSETS], inp, None, xp)
+    torch.cuda.synchronize(dev)
+    _, ids = layer_step(sets[0], inp, None, xp)
+    counts = torch.bincount(ids.flatten().long(), minlength=E).cpu()
+    if dist:
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    clk = Clocks(dev.index)
+    time.sleep(0.3)
+    _knx.prof_start(steps)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(steps):
+        layer_step(sets[i % NSETS], inp, None, xp)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    clocks = clk.stop()
+    stages, ncalls = _knx.prof_stop()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    return ms, {k: v / max(ncalls, 1) for k, v in stages.items()}, counts, clocks
+
+
+def time_layer_e2e(dev, steps, warmup):
+    """Through the public API with host buffers: H2D of the canvas hidden states from pinned
+    memory, the layer, D2H of the layer output, every step."""
+    sets, inp = build_layer(dev)
+    host_in = inp["hidden"].cpu().pin_memory()
+    host_out = torch.empty(T, H, dtype=torch.float16).pin_memory()
+    xp = torch.empty(T, H, dtype=torch.float16, device=dev)
+    dev_in = torch.empty_like(inp["hidden"])
+
+    def step(i):
+        dev_in.copy_(host_in, non_blocking=True)
+        inp2 = dict(inp, hidden=dev_in)
+        y, _ = layer_step(sets[i % NSETS], inp2, None, xp)
+        host_out.copy_(y, non_blocking=True)
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(steps):
+        step(i)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    return ev0.elapsed_time(ev1), host_in.numel() * 2, host_out.numel() * 2
+
+
+def time_sampler(dev, reps=1):
+    """48 denoising steps with the temperature schedule; per step one fused pass
+    (entropy + Gumbel-max + argmax) and one acceptance/stop launch."""
+    import accept_ops
+    import fused_sampler_ops
+    import workloads
+    xs = [workloads.sampler_logits(256, V_SAMPLER, seed=s, device=dev) for s in (0, 1)]
+    canvas = torch.zeros(1, 256, dtype=torch.int64, device=dev)
+    hist = torch.full((2, 1, 256), -1, dtype=torch.int64, device=dev)
+
+    def run(step, x):
+        Tm = workloads.temperature(step)
+        h, s, a = fused_sampler_ops.sample_step(x, workloads.step_seed(1234, step), Tm)
+        accept_ops.accept_and_stop(h.view(1, 256), canvas, s.view(1, 256), 0.1, a.view(1, 256),
+                                   hist, 0.005)
+    for i in range(3):
+        run(i, xs[i % 2])
+    torch.cuda.synchronize(dev)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kern_ms = 0.0
+    e0.record()
+    n = 0
+    for _ in range(reps):
+        for step in range(48):
+            x = xs[step % 2]
+            k0.record()
+            fused_sampler_ops.sample_step(x, workloads.step_seed(1234, step),
+                                          workloads.temperature(step))
+            k1.record()
+            torch.cuda.synchronize(dev)
+            kern_ms += k0.elapsed_time(k1)
+            n += 1
+    e1.record()
+    torch.cuda.synchronize(dev)
+    # full step (fused pass + acceptance/stop), back to back
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for step in range(48):
+        run(step, xs[step % 2])
+    f1.record()
+    torch.cuda.synchronize(dev)
+    return f0.elapsed_time(f1) / 48.0, kern_ms / n
+
+
+# --------------------------------------------------------------------------------- CPU arms
+def cpu_layer_sample(nthreads, expert_stride=16):
+    """The reference algorithm on the host (oracle restatement of the reference torch path:
+    per-expert F.linear on dequant_w4 weights + tanh-GELU + fixed-order combine), on a bounded
+    sample: the experts e with e % expert_stride == 0 and all their tokens, dequant inside the
+    timed region; the layer time is scaled by expert_stride.  RMSNorm + router run in full."""
+    import workloads
+    from oracle import ref
+    torch.set_num_threads(nthreads)
+    W = workloads.moe_weights(E, H, I, seed=100)
+    inp = workloads.moe_inputs(T, H, E, seed=0)
+    t0 = time.perf_counter()
+    xn = ref.rmsnorm(inp["hidden"], inp["norm_w"], 1e-6)
+    ids, w, _ = ref.router_topk(xn, inp["router_w"], inp["bias"], TOPK)
+    t_route = time.perf_counter() - t0
+    keep = torch.arange(E) % expert_stride == 0
+    sel = keep[ids.long()]
+    ids_s = torch.where(sel, ids.long(), torch.full_like(ids.long(), E))
+    t1 = time.perf_counter()
+    ref.moe_layer(xn, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"], W["dn_z"], ids_s, w)
+    t_moe = time.perf_counter() - t1
+    return (t_route + t_moe * expert_stride) * 1e6
+
+
+def reference_arm(args, rank):
+    if rank != 0:
+        return
+    ncores = len(os.sched_getaffinity(0))
+    vals = []
+    for i in range(args.warmup + args.steps):
+        us = cpu_layer_sample(ncores)
+        if i >= args.warmup:
+            vals.append(us)
+    v = statistics.median(vals)
+    line = {"metric": METRIC, "value": v, "unit": "us", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": v / 1000.0, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": "configs[1]: RMSNorm -> router (Zipf bias) -> W4A16 MoE layer, "
+                                   "T=256 H=2816 I=704 E=128 top-8", "device": "cpu"},
+            "cpu_baseline": {"value": v, "unit": "us", "cores": ncores, "kind": "port",
+                             "sample": "per step: RMSNorm+router on all 256 tokens, MoE on the 8 "
+                                       "experts e%16==0 (dequant inside) scaled x16"},
+            "e2e": {"value": v, "unit": "us", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    dist = world > 1
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if dist:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=dev)
+    ms, stages, counts, clocks = time_layer(dev, args.steps, args.warmup, dist)
+    ms_step = ms / args.steps
+    value = ms * 1000.0 / (args.steps * world)
+    import workloads
+    peak, peak_kind = peaks()
+    touched = int((counts > 0).sum())
+    bytes_layer = workloads.moe_layer_bytes(counts.numpy())
+    gemm1_bytes = touched * (2 * I * H // 2 + 2 * I * (H // 128) * 4) + T * H * 2
+    gemm1_ms = stages["gate_up_gelu"]
+    e2e_ms, h2d, d2h = time_layer_e2e(dev, args.steps, args.warmup)
+    samp_step_ms, samp_kern_ms = time_sampler(dev)
+    if dist:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return
+    cpu = None
+    if not args.no_cpu_baseline:
+        ncores = len(os.sched_getaffinity(0))
+        us = cpu_layer_sample(ncores)
+        cpu = {"value": us, "unit": "us", "cores": ncores, "kind": "port",
+               "sample": "one layer: RMSNorm+router on all 256 tokens, MoE on experts e%16==0 "
+                         "(dequant inside the timed region) scaled x16"}
+    achieved = gemm1_bytes / (gemm1_ms * 1e-3) / 1e9
+    line = {
+        "metric": METRIC, "value": value, "unit": "us", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "configs[1]: RMSNorm -> router (Zipf bias) -> W4A16 MoE layer, "
+                               "T=256 H=2816 I=704 E=128 top-8, gate_up gs128 / down gs64",
+                   "l2": f"{NSETS} rotating weight sets ({NSETS} x 416 MB) > 126 MB L2",
+                   "parallelism": f"replicas x{world}", "touched_experts": touched,
+                   "max_tokens_per_expert": int(counts.max())},
+        "layer_hbm_gbs": bytes_layer / (ms_step * 1e-3) / 1e9,
+        "layer_hbm_frac": bytes_layer / (ms_step * 1e-3) / 1e9 / peak,
+        "layer_bytes": bytes_layer,
+        "stages_us": {k: v * 1000.0 for k, v in stages.items()},
+        "roofline": {"kernel": "gateup_gelu_kernel", "bound": "hbm", "achieved": achieved,
+                     "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak_kind": peak_kind, "traffic": GEMM1_NCU_TRAFFIC,
+                     "algorithmic_bytes": gemm1_bytes},
+        "sampler_step_us": samp_step_ms * 1000.0,
+        "sampler_roofline": {"kernel": "sampler_kernel", "bound": "hbm",
+                             "achieved": 256 * V_SAMPLER * 4 / (samp_kern_ms * 1e-3) / 1e9,
+                             "peak": peak, "unit": "GB/s",
+                             "frac": 256 * V_SAMPLER * 4 / (samp_kern_ms * 1e-3) / 1e9 / peak,
+                             "kernel_us": samp_kern_ms * 1000.0},
+        "e2e": {"value": e2e_ms * 1000.0 / args.steps, "unit": "us", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": LAUNCHES_PER_LAYER * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,176 @@
+/*
+ * knx.h — C ABI of the B200 (sm_100a) kernels for the DiffusionGemma W4A16 MoE layer and the
+ * block-diffusion sampler step.
+ *
+ * Every entry point takes plain device pointers, element counts and a CUDA stream handle
+ * (`cudaStream_t` passed as `void*`; NULL = legacy default stream). Nothing here allocates
+ * device memory: callers pass outputs and, where a function needs scratch space, a workspace
+ * whose size the matching `*_workspace_size` function reports. Every call is stream-ordered,
+ * never synchronises the host and is safe to capture in a CUDA graph.
+ *
+ * Return value: KNX_OK (0) or a negative KNX_E* status for host-detectable contract violations
+ * (bad sizes, misaligned pointers, launch failures). Data-dependent problems found on the
+ * device (for example an expert id outside [0, E]) are OR-ed as KNX_DEV_* bits into the
+ * optional `err` device word; pass NULL to skip that reporting. Kernels never trap.
+ *
+ * Each declaration names the reference interface it replaces, as `file:line` inside the
+ * reference project (SRSWTI/knivesysl-diffusion-xe, directory `kernels/`).
+ */
+#ifndef KNX_H_
+#define KNX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define KNX_API __attribute__((visibility("default")))
+#else
+#define KNX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---------------------------------------------------------------------- */
+#define KNX_OK 0
+#define KNX_E_INVALID (-1)      /* bad size / dtype / flag combination                     */
+#define KNX_E_ALIGN (-2)        /* pointer or stride violates the documented alignment      */
+#define KNX_E_WORKSPACE (-3)    /* workspace NULL or smaller than *_workspace_size()        */
+#define KNX_E_LAUNCH (-4)       /* cudaGetLastError() after a launch was not cudaSuccess     */
+#define KNX_E_UNSUPPORTED (-5)  /* shape outside what the kernels were built for            */
+#define KNX_E_DEVICE (-6)       /* device is not sm_100 or CUDA call failed                  */
+
+/* device error bits (OR-ed into *err when err != NULL) */
+#define KNX_DEV_BAD_EXPERT_ID 0x1 /* topk id < 0 or > E (id == E is the "dropped" sentinel) */
+#define KNX_DEV_CAPACITY 0x2      /* a per-launch capacity bound was exceeded                */
+
+/* ---- dtypes ----------------------------------------------------------------------------- */
+#define KNX_F16 0
+#define KNX_BF16 1
+#define KNX_F32 2
+#define KNX_I32 3
+#define KNX_I64 4
+
+KNX_API int knx_version(void);
+/* 1 when the current device is a compute-capability 10.0 part (the only target). */
+KNX_API int knx_device_ok(void);
+KNX_API const char* knx_status_string(int status);
+
+/* ---- RMSNorm ----------------------------------------------------------------------------
+ * Replaces fused_rmsnorm (fused_rmsnorm.py:24-32, kernel fused_rmsnorm.py:10-21).
+ * y[r,:] = x[r,:] * rsqrt(mean(x[r,:]^2) + eps) * w   (fp32 math; w may be NULL = no scale)
+ * x, y: [rows, cols] contiguous in `dtype` (F16/BF16); w: [cols] in `w_dtype`.
+ * flags & KNX_RMS_ROUND_BF16: round the fp32 result to bf16 before the final store in
+ *   `dtype`, reproducing the reference kernel's bf16 store + .to(x.dtype) (fused_rmsnorm.py:21,32).
+ * xperm (optional, F16 only): also writes y with the K-interleave used by the MoE GEMMs
+ *   (see knx_moe_w4); pass NULL to skip. */
+#define KNX_RMS_ROUND_BF16 0x1
+KNX_API int knx_rmsnorm(const void* x, const void* w, int w_dtype, void* y, void* xperm, int64_t rows,
+                int64_t cols, float eps, int dtype, int flags, void* stream);
+
+/* ---- router ------------------------------------------------------------------------------
+ * DiffusionGemma router (transformers, not vendored; consumer signature pack_experts.py:44,65):
+ * logits = x . Wr^T (+ bias), p = softmax(logits), top-k by logit (ties -> lower expert id),
+ * weights renormalised over the selected k.  x: f16 [T,H]; wr: f16 [E,H]; bias: f32 [E] or
+ * NULL; logits_out: f32 [T,E] or NULL; ids: i32 [T,topk]; weights: f32 [T,topk].
+ * Requires H % 256 == 0, E % 32 == 0, E <= 256, topk <= min(16, E).
+ * workspace: >= knx_router_workspace_size(T, E) bytes (K-split partial logits). */
+KNX_API size_t knx_router_workspace_size(int64_t T, int E);
+KNX_API int knx_router_topk(const void* x, const void* wr, const float* bias, int64_t T, int64_t H, int E,
+                    int topk, float* logits_out, int32_t* ids, float* weights, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* ---- permutation (moe_align) ------------------------------------------------------------
+ * Replaces moe_align (fused_moe_w4.py:15-51) and moe_align_cuda/_align_finalize
+ * (fused_moe_w4_v2.py:32-74): a deterministic counting sort of the flat (token, slot) pairs
+ * p = t*topk + k by expert, stable in p.  Outputs, all int32:
+ *   counts[E]        pairs per expert (ids outside [0,E) are dropped and not counted)
+ *   offsets[E+1]     exclusive prefix of counts (unpadded slot start per expert)
+ *   sorted_pair[N]   pair index at each unpadded slot, N = T*topk (tail = N for dropped)
+ *   inv[N]           unpadded slot of pair p (-1 for dropped pairs)
+ * With block_m > 0 it also writes the reference's BM-padded form:
+ *   sorted_rows[cap] (pad = N), expert_ids[max_blocks] (pad = E), padded_inv[N];
+ *   cap = max_blocks*block_m, max_blocks = ceil(N/block_m) + E (fused_moe_w4.py:36-37).
+ * Pass NULL for any output not wanted.  ids_dtype is KNX_I32 or KNX_I64. */
+KNX_API int knx_moe_align(const void* topk_ids, int ids_dtype, int64_t T, int topk, int E, int block_m,
+                  int32_t* counts, int32_t* offsets, int32_t* sorted_pair, int32_t* inv,
+                  int32_t* sorted_rows, int32_t* expert_ids, int32_t* padded_inv, int32_t* err,
+                  void* stream);
+
+/* ---- one W4A16 MoE layer ------------------------------------------------------------------
+ * Replaces fused_moe_w4_v2 (fused_moe_w4_v2.py:319-371) and fused_moe_w4 (fused_moe_w4.py:104-128).
+ * Weight buffers are the pack_experts layout, read unchanged (pack_experts.py:34-41, 87-106):
+ *   gu_q u8 [E, 2I, H/2]   gu_s, gu_z f16 [E, 2I, H/gs_gu]   (rows [0,I) gate, [I,2I) up)
+ *   dn_q u8 [E, H, I/2]    dn_s, dn_z f16 [E, H, I/gs_dn]
+ *   nibble j of a row: byte j/2, low nibble for even j; w = (q - z) * s.
+ * out[t,:] = sum_{k=0..topk-1, fixed order} w[t,k] * down_e(gelu_tanh(gate_e(x_t)) * up_e(x_t)),
+ *   each pair's down output rounded to f16 before the fp32 weighted sum (fused_moe_w4_v2.py:248-263).
+ * hidden/out: [T,H] in hidden_dtype (F16/BF16; hidden is used as f16 like the reference);
+ * topk_ids: [T,topk] i32/i64; topk_w: [T,topk] F16/BF16/F32.
+ * hidden_perm: optional f16 [T,H] copy of hidden already in the MoE K-interleave (as written by
+ *   knx_rmsnorm's xperm); NULL = the layer builds it in its workspace.
+ * Contracts (fused_moe_w4_v2.py:325-328): H % 256 == 0, I % 64 == 0, gs_gu % 32 == 0 and
+ *   divides H, gs_dn % 32 == 0 and divides I, topk <= 16, E <= 1024.
+ * workspace: >= knx_moe_w4_workspace_size(T, H, I, E, topk) bytes, 256-byte aligned. */
+KNX_API size_t knx_moe_w4_workspace_size(int64_t T, int64_t H, int64_t I, int E, int topk);
+KNX_API int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidden_dtype, const void* topk_ids,
+               int ids_dtype, const void* topk_w, int w_dtype, const uint8_t* gu_q,
+               const void* gu_s, const void* gu_z, const uint8_t* dn_q, const void* dn_s,
+               const void* dn_z, int64_t T, int64_t H, int64_t I, int E, int topk, int gs_gu,
+               int gs_dn, void* workspace, size_t workspace_bytes, void* out, int32_t* err,
+               void* stream);
+
+/* ---- dense W4A16 linear -------------------------------------------------------------------
+ * Replaces w4a16_linear (w4a16.py:96-108):  Y[M,N] = X[M,K] . dequant(q,s,z)^T, f16 out.
+ * X: f16 [M,K] row-major; q u8 [N,K/2]; s,z f16 [N,K/gs].  K % 64 == 0, gs % 32 == 0, gs | K.
+ * workspace: >= knx_w4a16_workspace_size(M, K) bytes. */
+KNX_API size_t knx_w4a16_workspace_size(int64_t M, int64_t K);
+KNX_API int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, const void* z, int64_t M,
+                     int64_t N, int64_t K, int gs, void* Y, void* workspace,
+                     size_t workspace_bytes, void* stream);
+
+/* ---- sampler ------------------------------------------------------------------------------
+ * One streaming pass over fp32 logits [rows, V] that fuses, per row r:
+ *   q = x / temperature (IEEE-rounded division; temperature == 1 leaves x unchanged)
+ *   entropy[r] = logsumexp(q) - sum(q*exp(q-m))/sum(exp(q-m))  (fused_sampler_ops.py:22-40)
+ *   samp[r]    = first argmax_c (q_c + g_c), g_c = -log(-log(clamp(u_c, 1e-10, 1-1e-7))),
+ *                u_c = uniform(Philox4x32-10(key = seed + r, counter = (c,0,0,0)) word 0)
+ *                exactly as Triton's tl.rand(seed + r, c) (fused_sampler_ops.py:54-81)
+ *   amax[r]    = first argmax_c q_c
+ * Any of entropy/samp/amax may be NULL.  V <= 2^31 - 1.
+ * workspace: >= knx_sampler_workspace_size(rows, V) bytes. */
+KNX_API size_t knx_sampler_workspace_size(int64_t rows, int64_t V);
+KNX_API int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, float temperature,
+                      int64_t seed, float* entropy, int64_t* samp, int64_t* amax,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Entropy-bound acceptance and the stable-and-confident stop test, one launch per batch.
+ * Replaces _accept_canvas (fast_sampler.py:32-42) and _stop_call (fast_sampler.py:45-65).
+ * entropy f32 [B,L]; cur, proposal, out i64 [B,L]; mask u8 [B,L] (1 = accepted):
+ *   order = stable ascending sort of entropy; cum = running fp64 sum rounded to fp32;
+ *   accepted = (cum - sorted_entropy) <= entropy_bound;  out = accepted ? proposal : cur.
+ * Stop test (when finished != NULL): history i64 [S,B,L] of the last S argmax canvases
+ *   (initialised to -1 by the caller), argmax i64 [B,L]:
+ *   stable = S == 0 || all(history[s] == argmax); history rolls by one and stores argmax;
+ *   confident = (fp64 sum of entropy / L, rounded to fp32) < confidence_threshold;
+ *   finished[b] = stable && confident (u8).  L <= 1024. */
+KNX_API int knx_accept_stop(const float* entropy, const int64_t* cur, const int64_t* proposal, int64_t B,
+                    int64_t L, float entropy_bound, uint8_t* mask, int64_t* out,
+                    const int64_t* argmax, int64_t* history, int stability_threshold,
+                    float confidence_threshold, uint8_t* finished, void* stream);
+
+/* ---- stage profiling (benchmarks) --------------------------------------------------------
+ * knx_prof_start(max_calls): from now on knx_moe_w4 records a CUDA event at each of its stage
+ * boundaries (prep = K-interleave copy + align, gate_up+GELU GEMM, down GEMM, combine) for up to
+ * max_calls calls, without synchronising.  knx_prof_stop(stage_ms, n_stages, ncalls) waits for the
+ * recorded events, writes the per-stage device time summed over the recorded calls and the number
+ * of calls, and turns recording off.  Not thread-safe; meant for single-threaded benchmarks. */
+#define KNX_PROF_STAGES 4
+KNX_API int knx_prof_start(int max_calls);
+KNX_API int knx_prof_stop(float* stage_ms, int n_stages, int* ncalls);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KNX_H_ */

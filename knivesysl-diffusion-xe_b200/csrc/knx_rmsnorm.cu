@@ -1,0 +1,144 @@
+// knx_rmsnorm.cu — single-launch RMSNorm (replaces fused_rmsnorm.py:10-32).
+//
+// One warp per row.  A row is read once with 16-byte loads and kept in registers (up to
+// RMS_MAX_VEC vectors per lane, 4096 16-bit elements per row); wider rows are re-read from L2
+// for the second pass.  Math is fp32: ms = sum(x^2)/cols + eps, y = x * (1/sqrt(ms)) * w.
+// HBM-bound: 2 * rows * cols * 2 bytes + cols * 2 bytes of weight per launch.
+#include "knx_common.cuh"
+
+namespace knx {
+namespace {
+
+constexpr int RMS_WARPS = 8;
+constexpr int RMS_MAX_VEC = 16;  // 16 lanes-vectors * 8 elements * 32 lanes = 4096 elements
+
+template <typename T>
+KNX_DEVINL void unpack8(const uint4& v, float (&f)[8]);
+template <>
+KNX_DEVINL void unpack8<__half>(const uint4& v, float (&f)[8]) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __half22float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+template <>
+KNX_DEVINL void unpack8<__nv_bfloat16>(const uint4& v, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+template <typename T>
+KNX_DEVINL T from_f32(float v, bool round_bf16) {
+  if (round_bf16) v = __bfloat162float(__float2bfloat16_rn(v));
+  if constexpr (std::is_same<T, __half>::value) {
+    return __float2half_rn(v);
+  } else {
+    return __float2bfloat16_rn(v);
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(RMS_WARPS * 32)
+    rmsnorm_kernel(const T* __restrict__ x, const void* __restrict__ w, int w_dtype,
+                   T* __restrict__ y, __half* __restrict__ xperm, int64_t rows, int cols,
+                   float eps, bool round_bf16) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * RMS_WARPS + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int nvec = cols >> 3;  // 8 elements per 16-byte vector
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * cols);
+  uint4 cache[RMS_MAX_VEC];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < RMS_MAX_VEC; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nvec) {
+      cache[i] = ldg_nc_v4(xr + v);
+      float f[8];
+      unpack8<T>(cache[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    }
+  }
+  for (int v = lane + 32 * RMS_MAX_VEC; v < nvec; v += 32) {
+    float f[8];
+    unpack8<T>(xr[v], f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+  }
+  ss = warp_sum(ss);
+  const float ms = __fadd_rn(__fdiv_rn(ss, static_cast<float>(cols)), eps);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(ms));
+
+  uint4* yr = reinterpret_cast<uint4*>(y + row * cols);
+  uint4* pr = xperm ? reinterpret_cast<uint4*>(xperm + row * cols) : nullptr;
+  auto emit = [&](int v, const uint4& c) {
+    float f[8];
+    unpack8<T>(c, f);
+    T out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float t = __fmul_rn(f[j], inv);
+      if (w != nullptr) t = __fmul_rn(t, load_as_float(w, w_dtype, static_cast<int64_t>(v) * 8 + j));
+      out[j] = from_f32<T>(t, round_bf16);
+    }
+    yr[v] = *reinterpret_cast<uint4*>(out);
+    if (pr) {
+      // MoE K-interleave inside each 8-group: position p(i) = 2*(i%4) + i/4 holds element i.
+      __half hp[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float t;
+        if constexpr (std::is_same<T, __half>::value) {
+          t = __half2float(out[j]);
+        } else {
+          t = __bfloat162float(out[j]);
+        }
+        hp[2 * (j & 3) + (j >> 2)] = __float2half_rn(t);
+      }
+      pr[v] = *reinterpret_cast<uint4*>(hp);
+    }
+  };
+#pragma unroll
+  for (int i = 0; i < RMS_MAX_VEC; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nvec) emit(v, cache[i]);
+  }
+  for (int v = lane + 32 * RMS_MAX_VEC; v < nvec; v += 32) emit(v, xr[v]);
+}
+
+}  // namespace
+}  // namespace knx
+
+extern "C" int knx_rmsnorm(const void* x, const void* w, int w_dtype, void* y, void* xperm,
+                           int64_t rows, int64_t cols, float eps, int dtype, int flags,
+                           void* stream) {
+  using namespace knx;
+  if (rows < 0 || cols <= 0 || (cols % 8) != 0 || cols > (1 << 24)) return KNX_E_INVALID;
+  if (dtype != KNX_F16 && dtype != KNX_BF16) return KNX_E_INVALID;
+  if (w != nullptr && w_dtype != KNX_F16 && w_dtype != KNX_BF16 && w_dtype != KNX_F32)
+    return KNX_E_INVALID;
+  if (!aligned(x, 16) || !aligned(y, 16) || (xperm && !aligned(xperm, 16))) return KNX_E_ALIGN;
+  if (rows == 0) return KNX_OK;
+  const bool rb = (flags & KNX_RMS_ROUND_BF16) != 0;
+  const dim3 grid(static_cast<unsigned>((rows + RMS_WARPS - 1) / RMS_WARPS));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == KNX_F16) {
+    rmsnorm_kernel<__half><<<grid, RMS_WARPS * 32, 0, s>>>(
+        static_cast<const __half*>(x), w, w_dtype, static_cast<__half*>(y),
+        static_cast<__half*>(xperm), rows, static_cast<int>(cols), eps, rb);
+  } else {
+    rmsnorm_kernel<__nv_bfloat16><<<grid, RMS_WARPS * 32, 0, s>>>(
+        static_cast<const __nv_bfloat16*>(x), w, w_dtype, static_cast<__nv_bfloat16*>(y),
+        static_cast<__half*>(xperm), rows, static_cast<int>(cols), eps, rb);
+  }
+  return launch_status();
+}

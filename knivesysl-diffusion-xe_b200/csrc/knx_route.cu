@@ -1,0 +1,475 @@
+// knx_route.cu — router (logits, softmax, top-k, renormalise) and the token->expert
+// permutation (deterministic counting sort), plus the activation K-interleave copy.
+//
+// Reference behaviour followed:
+//   * moe_align (fused_moe_w4.py:15-51): stable sort of flat pairs p = t*topk + k by expert,
+//     ids == E are "dropped" and sort to the end; BM-padded block layout with pad sentinels
+//     Nexp (rows) and E (blocks); inv[p] = padded slot (0 for dropped pairs).
+//   * router (DiffusionGemma, not vendored; specified as softmax -> top-k -> renormalise).
+#include "knx_common.cuh"
+#include "knx_internal.cuh"
+
+namespace knx {
+namespace {
+
+// ------------------------------------------------------------------------------------------
+// Router logits: grid (ceil(T/32), E/32, RT_KSPLIT); each CTA computes a [32 token x 32 expert]
+// partial over one K split with m16n8k16 MMAs from a cp.async double buffer.  Partials go to
+// part[split][T][E]; the top-k kernel sums the splits in fixed order (deterministic).
+constexpr int RT_TOK = 32, RT_EXP = 32, RT_BK = 64, RT_KSPLIT = 4;
+constexpr int RT_ROWB = RT_BK * 2 + 16;  // 144-byte padded smem rows: conflict-free u32 loads
+
+__global__ void __launch_bounds__(128)
+    router_logits_kernel(const __half* __restrict__ x, const __half* __restrict__ wr, int T,
+                         int H, int E, float* __restrict__ part) {
+  __shared__ __align__(16) uint8_t sx[2][RT_TOK * RT_ROWB];
+  __shared__ __align__(16) uint8_t sw[2][RT_EXP * RT_ROWB];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const int t0 = blockIdx.x * RT_TOK, e0 = blockIdx.y * RT_EXP;
+  const int kper = H / RT_KSPLIT;  // multiple of RT_BK (host checks H % 256 == 0)
+  const int kbeg = blockIdx.z * kper;
+  const int nchunk = kper / RT_BK;
+
+  auto load = [&](int c, int buf) {
+    const int k0 = kbeg + c * RT_BK;
+    for (int i = tid; i < (RT_TOK + RT_EXP) * 8; i += 128) {
+      const int r = i >> 3, ch = i & 7;
+      if (r < RT_TOK) {
+        const int t = t0 + r;
+        cp_async16(&sx[buf][r * RT_ROWB + ch * 16],
+                   x + static_cast<int64_t>(t < T ? t : T - 1) * H + k0 + ch * 8);
+      } else {
+        const int e = e0 + r - RT_TOK;
+        cp_async16(&sw[buf][(r - RT_TOK) * RT_ROWB + ch * 16],
+                   wr + static_cast<int64_t>(e) * H + k0 + ch * 8);
+      }
+    }
+    cp_async_commit();
+  };
+
+  // warp tile: tokens [16*(warp&1), +16) as MMA rows, experts [16*(warp>>1), +16) as 2 n8 tiles
+  const int tm = 16 * (warp & 1), en = 16 * (warp >> 1);
+  float acc[2][4] = {};
+  load(0, 0);
+  for (int c = 0; c < nchunk; ++c) {
+    if (c + 1 < nchunk) {
+      load(c + 1, (c + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const uint32_t bx = smem_u32(sx[c & 1]), bw = smem_u32(sw[c & 1]);
+#pragma unroll
+    for (int ks = 0; ks < RT_BK / 16; ++ks) {
+      const int kb = ks * 32 + q * 4;  // byte offset of k = 16*ks + 2q
+      const uint32_t a0 = lds32(bx + (tm + g) * RT_ROWB + kb);
+      const uint32_t a1 = lds32(bx + (tm + g + 8) * RT_ROWB + kb);
+      const uint32_t a2 = lds32(bx + (tm + g) * RT_ROWB + kb + 16);
+      const uint32_t a3 = lds32(bx + (tm + g + 8) * RT_ROWB + kb + 16);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint32_t b0 = lds32(bw + (en + 8 * nt + g) * RT_ROWB + kb);
+        const uint32_t b1 = lds32(bw + (en + 8 * nt + g) * RT_ROWB + kb + 16);
+        mma_16816(acc[nt], a0, a1, a2, a3, b0, b1);
+      }
+    }
+    __syncthreads();
+  }
+  float* out = part + static_cast<int64_t>(blockIdx.z) * T * E;
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int e = e0 + en + 8 * nt + 2 * q;
+    const int ta = t0 + tm + g, tb = ta + 8;
+    if (ta < T) {
+      out[static_cast<int64_t>(ta) * E + e] = acc[nt][0];
+      out[static_cast<int64_t>(ta) * E + e + 1] = acc[nt][1];
+    }
+    if (tb < T) {
+      out[static_cast<int64_t>(tb) * E + e] = acc[nt][2];
+      out[static_cast<int64_t>(tb) * E + e + 1] = acc[nt][3];
+    }
+  }
+}
+
+// One warp per token: sum the K-split partials in order, add bias, softmax, top-k by logit
+// (ties -> lower expert id), renormalise the selected probabilities.
+constexpr int TK_MAXE = 256;
+__global__ void __launch_bounds__(256)
+    router_topk_kernel(const float* __restrict__ part, const float* __restrict__ bias, int T,
+                       int E, int topk, float* __restrict__ logits_out, int32_t* __restrict__ ids,
+                       float* __restrict__ weights) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (t >= T) return;
+  constexpr int PER = TK_MAXE / 32;
+  float l[PER];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    float v = -INFINITY;
+    if (e < E) {
+      v = 0.f;
+      for (int s = 0; s < RT_KSPLIT; ++s) v += part[(static_cast<int64_t>(s) * T + t) * E + e];
+      if (bias) v += bias[e];
+      if (logits_out) logits_out[static_cast<int64_t>(t) * E + e] = v;
+    }
+    l[i] = v;
+    mx = fmaxf(mx, v);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float den = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) den += (lane + 32 * i < E) ? expf(l[i] - mx) : 0.f;
+  den = warp_sum(den);
+  // top-k selection: k rounds of a warp-wide (max value, min index) reduction
+  float psel[16];
+  int isel[16];
+  float psum = 0.f;
+  for (int k = 0; k < topk; ++k) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E && (l[i] > bv || (l[i] == bv && e < bi))) {
+        bv = l[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (lane + 32 * i == bi) l[i] = -INFINITY;  // remove the winner
+    const float p = expf(bv - mx) / den;
+    psel[k] = p;
+    isel[k] = bi;
+    psum += p;
+  }
+  if (lane == 0) {
+    for (int k = 0; k < topk; ++k) {
+      ids[static_cast<int64_t>(t) * topk + k] = isel[k];
+      weights[static_cast<int64_t>(t) * topk + k] = psel[k] / psum;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Counting sort (one CTA, 1024 threads).  Each warp ranks a contiguous run of pairs with
+// __match_any_sync, so the rank of pair p inside its expert is
+//   (pairs of that expert in earlier warps) + (earlier pairs in the same warp),
+// which is exactly the stable order.  Also builds the GEMM task list (expert token chunks of at
+// most m_max, ordered by chunk size descending, then expert, then chunk) and zeroes the GEMMs'
+// dynamic work counters.
+constexpr int AL_THREADS = 1024;
+
+__device__ __forceinline__ int* scnt_buf(int* whist, int) { return whist; }
+
+__device__ int block_excl_scan(int v, int* sbuf, int* total) {
+  // sbuf: >= 32 ints.  Exclusive scan over blockDim.x threads in thread order.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) sbuf[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int wv = lane < nw ? sbuf[lane] : 0;
+    int wi = wv;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    if (lane < nw) sbuf[lane] = wi - wv;
+    if (lane == 31) sbuf[32] = wi;
+  }
+  __syncthreads();
+  const int res = sbuf[warp] + incl - v;
+  if (total) *total = sbuf[32];
+  __syncthreads();
+  return res;
+}
+
+__global__ void __launch_bounds__(AL_THREADS)
+    align_kernel(const void* __restrict__ ids, int ids_dtype, int T, int topk, int E, int block_m,
+                 int m_max, int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
+                 int32_t* __restrict__ sorted_pair, int32_t* __restrict__ inv,
+                 int32_t* __restrict__ sorted_rows, int32_t* __restrict__ expert_ids,
+                 int32_t* __restrict__ padded_inv, int4* __restrict__ tasks,
+                 int32_t* __restrict__ ntasks, int32_t* __restrict__ work_counters,
+                 int n_work_counters, int32_t* __restrict__ err) {
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  const int N = T * topk;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int per_warp = ((N + AL_THREADS - 1) / AL_THREADS) * 32;
+  const int npad = (N + 7) & ~7;
+  int16_t* sid = reinterpret_cast<int16_t*>(sm_raw);
+  int16_t* srank = sid + npad;
+  int* whist = reinterpret_cast<int*>(srank + npad);  // [32][E]
+  int* soff = whist + 32 * E;                          // [E+1]
+  int* spblk = soff + E + 1;                           // [E+1]
+  int* scan_buf = spblk + E + 1;                       // [33]
+  int* size_hist = scan_buf + 40;                      // [m_max+1]
+
+  for (int i = tid; i < 32 * E; i += AL_THREADS) whist[i] = 0;
+  for (int i = tid; i <= m_max; i += AL_THREADS) size_hist[i] = 0;
+  if (tid < n_work_counters) work_counters[tid] = 0;
+  int bad = 0;
+  for (int p = tid; p < N; p += AL_THREADS) {
+    int64_t v = load_as_i64(ids, ids_dtype, p);
+    if (v < 0 || v > E) {
+      bad = 1;
+      v = E;
+    }
+    sid[p] = static_cast<int16_t>(v);
+  }
+  if (bad && err) atomicOr(err, KNX_DEV_BAD_EXPERT_ID);
+  __syncthreads();
+
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int p0 = warp * per_warp;
+  for (int r = 0; r < per_warp; r += 32) {
+    const int p = p0 + r + lane;
+    const bool valid = p < N;
+    const int e = valid ? sid[p] : E;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int before = __popc(peers & lt_mask);
+    const int leader = __ffs(peers) - 1;
+    const int prev = (e < E) ? whist[warp * E + e] : 0;
+    __syncwarp();
+    if (e < E && lane == leader) whist[warp * E + e] = prev + __popc(peers);
+    __syncwarp();
+    if (valid) srank[p] = static_cast<int16_t>(e < E ? prev + before : -1);
+  }
+  __syncthreads();
+
+  // per expert: exclusive prefix over warps (in place) and the expert's total count
+  int cnt = 0, nblk = 0, nfull = 0, rem = 0;
+  const int e_me = tid;  // E <= AL_THREADS
+  if (e_me < E) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = whist[w * E + e_me];
+      whist[w * E + e_me] = run;
+      run += c;
+    }
+    cnt = run;
+    nblk = block_m > 0 ? (cnt + block_m - 1) / block_m : 0;
+    nfull = cnt / m_max;
+    rem = cnt % m_max;
+  }
+  int total_valid = 0, total_blk = 0, total_full = 0;
+  const int off = block_excl_scan(cnt, scan_buf, &total_valid);
+  const int pblk = block_excl_scan(nblk, scan_buf, &total_blk);
+  const int fpre = block_excl_scan(nfull, scan_buf, &total_full);
+  if (e_me < E) {
+    soff[e_me] = off;
+    spblk[e_me] = pblk;
+    if (counts) counts[e_me] = cnt;
+    if (offsets) offsets[e_me] = off;
+    if (rem > 0) atomicAdd(&size_hist[rem], 1);
+  }
+  if (tid == 0) {
+    soff[E] = total_valid;
+    spblk[E] = total_blk;
+    if (offsets) offsets[E] = total_valid;
+    size_hist[m_max] = total_full;
+  }
+  const int max_blocks = block_m > 0 ? (N + block_m - 1) / block_m + E : 0;
+  const int cap = max_blocks * block_m;
+  if (block_m > 0 && sorted_rows) {
+    for (int i = tid; i < cap; i += AL_THREADS) sorted_rows[i] = N;
+  }
+  __syncthreads();
+
+  for (int p = tid; p < N; p += AL_THREADS) {
+    const int e = sid[p];
+    if (e < E) {
+      const int w = p / per_warp;
+      const int rank = whist[w * E + e] + srank[p];
+      const int slot = soff[e] + rank;
+      if (sorted_pair) sorted_pair[slot] = p;
+      if (inv) inv[p] = slot;
+      if (block_m > 0) {
+        const int ps = spblk[e] * block_m + rank;
+        if (sorted_rows) sorted_rows[ps] = p;
+        if (padded_inv) padded_inv[p] = ps;
+      }
+    } else {
+      if (inv) inv[p] = -1;
+      if (block_m > 0 && padded_inv) padded_inv[p] = 0;
+    }
+  }
+  if (sorted_pair)
+    for (int s = total_valid + tid; s < N; s += AL_THREADS) sorted_pair[s] = N;
+  if (block_m > 0 && expert_ids) {
+    for (int b = tid; b < max_blocks; b += AL_THREADS) {
+      // expert e with spblk[e] <= b < spblk[e+1]; b >= total -> E (upper_bound search)
+      int lo = 0, hi = E;  // find first e in [0,E] with spblk[e] > b, answer = that - 1
+      while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (spblk[mid + 1] > b) hi = mid; else lo = mid + 1;
+      }
+      expert_ids[b] = (b < total_blk) ? lo : E;
+    }
+  }
+
+  // task list: sizes descending; size_hist[s] becomes the number of tasks with size > s
+  if (tasks) {
+    __syncthreads();  // placement above still reads whist
+    if (tid == 0) {
+      int run = 0;
+      for (int s = m_max; s >= 1; --s) {
+        const int h = size_hist[s];
+        size_hist[s] = run;
+        run += h;
+      }
+      *ntasks = run;
+    }
+    if (e_me < E) scnt_buf(whist, E)[e_me] = cnt;  // whist is free again: reuse as count table
+    __syncthreads();
+    if (e_me < E && cnt > 0) {
+      for (int j = 0; j < nfull; ++j)
+        tasks[size_hist[m_max] + fpre + j] = make_int4(e_me, j * m_max, m_max, 0);
+      if (rem > 0) {
+        const int* sc = scnt_buf(whist, E);
+        int before_same = 0;
+        for (int e2 = 0; e2 < e_me; ++e2) before_same += (sc[e2] % m_max) == rem;
+        tasks[size_hist[rem] + before_same] = make_int4(e_me, nfull * m_max, rem, 0);
+      }
+    }
+  }
+}
+
+// Activation copy into the MoE K-interleave (f16 out; f16 or bf16 in).  One thread per 16 bytes.
+template <typename T>
+__global__ void permute_act_kernel(const T* __restrict__ x, __half* __restrict__ xp, int64_t nvec) {
+  const int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (v >= nvec) return;
+  const uint4 raw = ldg_nc_v4(reinterpret_cast<const uint4*>(x) + v);
+  const T* e = reinterpret_cast<const T*>(&raw);
+  __half hp[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float f;
+    if constexpr (std::is_same<T, __half>::value) {
+      f = __half2float(e[j]);
+    } else {
+      f = __bfloat162float(e[j]);
+    }
+    hp[2 * (j & 3) + (j >> 2)] = __float2half_rn(f);
+  }
+  reinterpret_cast<uint4*>(xp)[v] = *reinterpret_cast<uint4*>(hp);
+}
+
+}  // namespace
+
+constexpr int RT_KSPLIT_PUBLIC = RT_KSPLIT;
+
+size_t align_smem_bytes(int N, int E, int m_max) {
+  const int npad = (N + 7) & ~7;
+  return static_cast<size_t>(npad) * 4 + static_cast<size_t>(32 * E + 2 * (E + 1) + 40 + m_max + 1) * 4;
+}
+
+bool align_supported(int64_t N, int E) {
+  return N <= ALIGN_MAX_PAIRS && E >= 1 && E <= ALIGN_MAX_EXPERTS;
+}
+
+int launch_align(const void* ids, int ids_dtype, int T, int topk, int E, int block_m, int m_max,
+                 int32_t* counts, int32_t* offsets, int32_t* sorted_pair, int32_t* inv,
+                 int32_t* sorted_rows, int32_t* expert_ids, int32_t* padded_inv, int4* tasks,
+                 int32_t* ntasks, int32_t* work_counters, int n_work_counters, int32_t* err,
+                 cudaStream_t stream) {
+  const int N = T * topk;
+  const size_t smem = align_smem_bytes(N, E, m_max);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    attr_set[dev & 63] = true;
+  }
+  align_kernel<<<1, AL_THREADS, smem, stream>>>(ids, ids_dtype, T, topk, E, block_m, m_max, counts,
+                                                offsets, sorted_pair, inv, sorted_rows, expert_ids,
+                                                padded_inv, tasks, ntasks, work_counters,
+                                                n_work_counters, err);
+  return launch_status();
+}
+
+int launch_permute(const void* x, int dtype, __half* xp, int64_t elems, cudaStream_t stream) {
+  const int64_t nvec = elems / 8;
+  if (nvec == 0) return KNX_OK;
+  const int threads = 256;
+  const unsigned blocks = static_cast<unsigned>((nvec + threads - 1) / threads);
+  if (dtype == KNX_F16) {
+    permute_act_kernel<__half><<<blocks, threads, 0, stream>>>(static_cast<const __half*>(x), xp, nvec);
+  } else {
+    permute_act_kernel<__nv_bfloat16>
+        <<<blocks, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), xp, nvec);
+  }
+  return launch_status();
+}
+
+}  // namespace knx
+
+// ------------------------------------------------------------------------------------------
+extern "C" size_t knx_router_workspace_size(int64_t T, int E) {
+  return static_cast<size_t>(knx::RT_KSPLIT_PUBLIC) * static_cast<size_t>(T > 0 ? T : 0) *
+             static_cast<size_t>(E > 0 ? E : 0) * sizeof(float) + 256;
+}
+
+extern "C" int knx_router_topk(const void* x, const void* wr, const float* bias, int64_t T,
+                               int64_t H, int E, int topk, float* logits_out, int32_t* ids,
+                               float* weights, void* workspace, size_t workspace_bytes,
+                               void* stream) {
+  using namespace knx;
+  if (T < 0 || H <= 0 || (H % 256) != 0 || E < 32 || (E % 32) != 0 || E > 256 || topk < 1 ||
+      topk > 16 || topk > E || H > (1 << 24) || T > (1 << 24))
+    return KNX_E_INVALID;
+  if (!aligned(x, 16) || !aligned(wr, 16)) return KNX_E_ALIGN;
+  if (T == 0) return KNX_OK;
+  if (workspace == nullptr || workspace_bytes < knx_router_workspace_size(T, E))
+    return KNX_E_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  float* part = static_cast<float*>(workspace);
+  const dim3 g1(static_cast<unsigned>((T + RT_TOK - 1) / RT_TOK), E / RT_EXP, RT_KSPLIT);
+  router_logits_kernel<<<g1, 128, 0, s>>>(static_cast<const __half*>(x),
+                                          static_cast<const __half*>(wr), static_cast<int>(T),
+                                          static_cast<int>(H), E, part);
+  int st = launch_status();
+  if (st != KNX_OK) return st;
+  router_topk_kernel<<<static_cast<unsigned>((T + 7) / 8), 256, 0, s>>>(
+      part, bias, static_cast<int>(T), E, topk, logits_out, ids, weights);
+  return launch_status();
+}
+
+extern "C" int knx_moe_align(const void* topk_ids, int ids_dtype, int64_t T, int topk, int E,
+                             int block_m, int32_t* counts, int32_t* offsets, int32_t* sorted_pair,
+                             int32_t* inv, int32_t* sorted_rows, int32_t* expert_ids,
+                             int32_t* padded_inv, int32_t* err, void* stream) {
+  using namespace knx;
+  if (T < 0 || topk < 1 || topk > 64 || E < 1 || block_m < 0) return KNX_E_INVALID;
+  if (ids_dtype != KNX_I32 && ids_dtype != KNX_I64) return KNX_E_INVALID;
+  const int64_t N = T * topk;
+  if (!align_supported(N, E)) return KNX_E_UNSUPPORTED;
+  if (N == 0) return KNX_OK;
+  return launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, block_m, 1, counts,
+                      offsets, sorted_pair, inv, sorted_rows, expert_ids, padded_inv, nullptr,
+                      nullptr, nullptr, 0, err, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,450 @@
+// knx_sampler.cu — one streaming pass over fp32 logits that yields, per row, the entropy of
+// softmax(x/T), the Gumbel-max sample and the plain argmax; plus the entropy-bound acceptance
+// mask and the stable-and-confident stop test.
+//
+// Reference semantics: fused_sampler_ops.py:22-93 (entropy, Gumbel argmax), fast_sampler.py:32-65
+// (acceptance, stop), fast_sampler.py:92 (seed mixing, done by the caller).
+//
+// Layout / work split: a row of V logits is cut into a power-of-two number of chunks; a work item
+// is (row, chunk) and persistent CTAs pull items from a counter.  Each warp streams 512 columns
+// per step (4 float4 per lane) and keeps
+//   * an online softmax state (m, s, t) with t = sum (q-m) e^(q-m), so H = log s - t/s is a sum
+//     of two non-negative terms (no cancellation for peaked rows);
+//   * the running argmax of q;
+//   * the running Gumbel winner.  Gumbel noise is bounded above by GUMBEL_MAX, so an element with
+//     q + GUMBEL_MAX < W (W = best q+g seen anywhere in the row so far, shared through a per-row
+//     atomic) cannot win and its Philox draw is skipped.  Candidates are compacted per warp so
+//     the 35-instruction Philox runs on full warps.  Skipping never changes the result, only
+//     the work, so the output is bit-identical whatever the schedule.
+// Chunk partials are merged by the last CTA of each row in chunk order (deterministic).
+#include "knx_common.cuh"
+#include "knx_math.cuh"
+
+namespace knx {
+namespace {
+
+constexpr int SP_THREADS = 256;
+constexpr int SP_WARPS = SP_THREADS / 32;
+constexpr int SP_TILE = 512;                 // columns per warp step
+constexpr int SP_TARGET_CHUNK = 32768;       // columns per work item (before power-of-2 rounding)
+
+struct __align__(16) Part {
+  float m, s, t, bq;
+  int bqi, bgi;
+  float bg, pad;
+};
+
+// order-preserving map float -> uint32 (for atomicMax on the per-row Gumbel bound)
+KNX_DEVINL uint32_t fkey(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+KNX_DEVINL float fdecode(uint32_t k) {
+  if (k < 0x00800000u) return -INFINITY;  // zero-initialised bound = no bound yet
+  const uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+  return __uint_as_float(b);
+}
+
+KNX_DEVINL float ex2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+constexpr float LOG2E = 1.4426950408889634f;
+
+// merge online-softmax states: (m,s,t) with t = sum (q-m) e^(q-m)
+KNX_DEVINL void sm_merge(float& m, float& s, float& t, float m2, float s2, float t2) {
+  if (s2 == 0.f) return;
+  if (s == 0.f) {
+    m = m2; s = s2; t = t2;
+    return;
+  }
+  const float M = fmaxf(m, m2);
+  const float a = ex2((m - M) * LOG2E), b = ex2((m2 - M) * LOG2E);
+  t = a * (t + (m - M) * s) + b * (t2 + (m2 - M) * s2);
+  s = a * s + b * s2;
+  m = M;
+}
+KNX_DEVINL void arg_merge(float& v, int& i, float v2, int i2) {
+  if (v2 > v || (v2 == v && i2 < i)) {
+    v = v2;
+    i = i2;
+  }
+}
+
+KNX_DEVINL void row_key(int64_t seed, int seed_is32, int64_t row, uint32_t& k0, uint32_t& k1) {
+  if (seed_is32) {
+    // Triton passes a 32-bit seed as i32: seed + row wraps in i32, then sign-extends to u64.
+    const int32_t s = static_cast<int32_t>(static_cast<uint32_t>(seed) + static_cast<uint32_t>(row));
+    k0 = static_cast<uint32_t>(s);
+    k1 = s < 0 ? 0xffffffffu : 0u;
+  } else {
+    const uint64_t s = static_cast<uint64_t>(seed + row);
+    k0 = static_cast<uint32_t>(s);
+    k1 = static_cast<uint32_t>(s >> 32);
+  }
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(SP_THREADS, 3)
+    sampler_kernel(const float* __restrict__ logits, int64_t rows, int V, float temp, float rtemp,
+                   int do_div, int64_t seed, int seed_is32, int want_gumbel, int nchunks,
+                   int chunk_cols, Part* __restrict__ parts, uint32_t* __restrict__ row_ticket,
+                   uint32_t* __restrict__ row_bound, int* __restrict__ work_counter,
+                   float* __restrict__ entropy, int64_t* __restrict__ samp,
+                   int64_t* __restrict__ amax) {
+  __shared__ int s_item;
+  __shared__ int s_last;
+  __shared__ Part s_wpart[SP_WARPS];
+  __shared__ int cq_col[SP_WARPS][SP_TILE];
+  __shared__ float cq_q[SP_WARPS][SP_TILE];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t nitems = rows * nchunks;
+
+  for (;;) {
+    if (tid == 0) s_item = atomicAdd(work_counter, 1);
+    __syncthreads();
+    const int64_t item = s_item;
+    if (item >= nitems) break;
+    const int64_t row = item / nchunks;
+    const int chunk = static_cast<int>(item - row * nchunks);
+    const int c_beg = min(V, chunk * chunk_cols);
+    const int c_end = min(V, c_beg + chunk_cols);
+    // warp sub-range, multiple of 4 columns
+    const int per_warp = (((c_end - c_beg) + SP_WARPS * 4 - 1) / (SP_WARPS * 4)) * 4;
+    const int w_beg = min(c_end, c_beg + warp * per_warp);
+    const int w_end = min(c_end, w_beg + per_warp);
+    const float* xr = logits + row * static_cast<int64_t>(V);
+    uint32_t k0 = 0, k1 = 0;
+    row_key(seed, seed_is32, row, k0, k1);
+
+    float m = -INFINITY, s = 0.f, t = 0.f;
+    float bq = -INFINITY, bg = -INFINITY;
+    int bqi = 0x7fffffff, bgi = 0x7fffffff;
+    float W = -INFINITY;
+    bool first = true;
+    for (int base = w_beg; base < w_end; base += SP_TILE) {
+      float qv[16];
+      unsigned valid = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int c0 = base + 128 * j + 4 * lane;
+        if (VEC) {
+          if (c0 < w_end) {  // w_end - c0 is a multiple of 4 when VEC
+            const float4 v = __ldcs(reinterpret_cast<const float4*>(xr + c0));
+            qv[4 * j] = v.x; qv[4 * j + 1] = v.y; qv[4 * j + 2] = v.z; qv[4 * j + 3] = v.w;
+            valid |= 0xfu << (4 * j);
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            if (c0 + c < w_end) {
+              qv[4 * j + c] = __ldcs(xr + c0 + c);
+              valid |= 1u << (4 * j + c);
+            }
+          }
+        }
+      }
+      float tm = -INFINITY;
+      int ti = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (valid & (1u << i)) {
+          if (do_div) qv[i] = div_rn_by(qv[i], temp, rtemp);
+          if (qv[i] > tm) {
+            tm = qv[i];
+            ti = base + 128 * (i >> 2) + 4 * lane + (i & 3);
+          }
+        } else {
+          qv[i] = -INFINITY;
+        }
+      }
+      if (valid) {
+        if (tm > m && tm != -INFINITY) {
+          if (s != 0.f) {
+            const float a = ex2((m - tm) * LOG2E);
+            t = a * (t + (m - tm) * s);
+            s = a * s;
+          }
+          m = tm;
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          if ((valid & (1u << i)) && qv[i] != -INFINITY) {
+            const float d = qv[i] - m;
+            const float e = ex2(d * LOG2E);
+            s += e;
+            t = fmaf(d, e, t);
+          }
+        }
+        if (tm > bq) {
+          bq = tm;
+          bqi = ti;
+        }
+      }
+      if (want_gumbel) {
+        if (first) {  // bootstrap the bound with each lane's tile maximum
+          first = false;
+          if (valid) {
+            const float v = tm + gumbel_from_word(philox_w0(static_cast<uint32_t>(ti), k0, k1));
+            arg_merge(bg, bgi, v, ti);
+          }
+          float wm = bg;
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+          W = fmaxf(W, wm);
+        }
+        unsigned cm = 0;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if ((valid & (1u << i)) && !(qv[i] + GUMBEL_MAX < W)) cm |= 1u << i;
+        const int n = __popc(cm);
+        int incl = n;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const int total = __shfl_sync(0xffffffffu, incl, 31);
+        if (total > 0) {
+          int pos = incl - n;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            if (cm & (1u << i)) {
+              cq_col[warp][pos] = base + 128 * (i >> 2) + 4 * lane + (i & 3);
+              cq_q[warp][pos] = qv[i];
+              ++pos;
+            }
+          }
+          __syncwarp();
+          for (int i = lane; i < total; i += 32) {
+            const int col = cq_col[warp][i];
+            const float v = cq_q[warp][i] + gumbel_from_word(philox_w0(static_cast<uint32_t>(col), k0, k1));
+            arg_merge(bg, bgi, v, col);
+          }
+          __syncwarp();
+        }
+        float wm = bg;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wm = fmaxf(wm, __shfl_xor_sync(0xffffffffu, wm, o));
+        uint32_t old = 0;
+        if (lane == 0) old = atomicMax(row_bound + row, fkey(wm));
+        old = __shfl_sync(0xffffffffu, old, 0);
+        W = fmaxf(fmaxf(W, wm), fdecode(old));
+      }
+    }
+    // warp reductions (fixed butterfly order)
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float t2 = __shfl_xor_sync(0xffffffffu, t, o);
+      const float bq2 = __shfl_xor_sync(0xffffffffu, bq, o);
+      const int bqi2 = __shfl_xor_sync(0xffffffffu, bqi, o);
+      const float bg2 = __shfl_xor_sync(0xffffffffu, bg, o);
+      const int bgi2 = __shfl_xor_sync(0xffffffffu, bgi, o);
+      // merge in a symmetric way so both partners hold the same result
+      float ma = m, sa = s, ta = t, mb = m2, sb = s2, tb = t2;
+      if ((lane & o) != 0) {  // canonical order: lower lane first
+        ma = m2; sa = s2; ta = t2; mb = m; sb = s; tb = t;
+      }
+      sm_merge(ma, sa, ta, mb, sb, tb);
+      m = ma; s = sa; t = ta;
+      arg_merge(bq, bqi, bq2, bqi2);
+      arg_merge(bg, bgi, bg2, bgi2);
+    }
+    if (lane == 0) {
+      Part p;
+      p.m = m; p.s = s; p.t = t; p.bq = bq; p.bqi = bqi; p.bg = bg; p.bgi = bgi; p.pad = 0.f;
+      s_wpart[warp] = p;
+    }
+    __syncthreads();
+    if (tid == 0) {
+      Part acc = s_wpart[0];
+      for (int w = 1; w < SP_WARPS; ++w) {
+        const Part p = s_wpart[w];
+        sm_merge(acc.m, acc.s, acc.t, p.m, p.s, p.t);
+        arg_merge(acc.bq, acc.bqi, p.bq, p.bqi);
+        arg_merge(acc.bg, acc.bgi, p.bg, p.bgi);
+      }
+      parts[item] = acc;
+      __threadfence();
+      const uint32_t tk = atomicAdd(row_ticket + row, 1u);
+      s_last = ((tk + 1u) % static_cast<uint32_t>(nchunks)) == 0u;
+    }
+    __syncthreads();
+    if (s_last && tid == 0) {
+      __threadfence();
+      const float4* pr = reinterpret_cast<const float4*>(parts + row * nchunks);
+      float4 a = __ldcg(pr), b = __ldcg(pr + 1);
+      Part acc;
+      acc.m = a.x; acc.s = a.y; acc.t = a.z; acc.bq = a.w;
+      acc.bqi = __float_as_int(b.x); acc.bgi = __float_as_int(b.y); acc.bg = b.z; acc.pad = 0.f;
+      for (int c = 1; c < nchunks; ++c) {
+        a = __ldcg(pr + 2 * c);
+        b = __ldcg(pr + 2 * c + 1);
+        sm_merge(acc.m, acc.s, acc.t, a.x, a.y, a.z);
+        arg_merge(acc.bq, acc.bqi, a.w, __float_as_int(b.x));
+        arg_merge(acc.bg, acc.bgi, b.z, __float_as_int(b.y));
+      }
+      if (entropy) entropy[row] = logf(acc.s) - acc.t / acc.s;
+      if (amax) amax[row] = acc.bqi;
+      if (samp) samp[row] = acc.bgi;
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Acceptance mask + stop test, one CTA per batch row, one thread per canvas position.
+__global__ void __launch_bounds__(1024)
+    accept_stop_kernel(const float* __restrict__ ent, const int64_t* __restrict__ cur,
+                       const int64_t* __restrict__ prop, int B, int L, float bound,
+                       uint8_t* __restrict__ mask, int64_t* __restrict__ out,
+                       const int64_t* __restrict__ argmax, int64_t* __restrict__ history, int S,
+                       float conf, uint8_t* __restrict__ finished) {
+  __shared__ float sh[1024];
+  __shared__ float sorted[1024];
+  __shared__ uint8_t msorted[1024];
+  const int b = blockIdx.x, i = threadIdx.x;
+  const bool act = i < L;
+  const int64_t gi = static_cast<int64_t>(b) * L + i;
+  const float h = act ? ent[gi] : 0.f;
+  if (act) sh[i] = h;
+  __syncthreads();
+  int rank = 0;
+  if (act) {
+    for (int j = 0; j < L; ++j) {
+      const float hj = sh[j];
+      rank += (hj < h) || (hj == h && j < i);
+    }
+    sorted[rank] = h;
+  }
+  __syncthreads();
+  if (i == 0) {
+    double acc = 0.0;
+    for (int k = 0; k < L; ++k) {
+      acc += static_cast<double>(sorted[k]);
+      const float c = static_cast<float>(acc);
+      msorted[k] = __fsub_rn(c, sorted[k]) <= bound;
+    }
+  }
+  __syncthreads();
+  if (act) {
+    const uint8_t mk = msorted[rank];
+    if (mask) mask[gi] = mk;
+    if (out) out[gi] = mk ? prop[gi] : cur[gi];
+  }
+  if (finished) {
+    int eq = 1;
+    if (S > 0 && act) {
+      const int64_t a = argmax[gi];
+      for (int sidx = 0; sidx < S; ++sidx)
+        eq &= history[(static_cast<int64_t>(sidx) * B + b) * L + i] == a;
+      for (int sidx = 0; sidx + 1 < S; ++sidx)
+        history[(static_cast<int64_t>(sidx) * B + b) * L + i] =
+            history[(static_cast<int64_t>(sidx + 1) * B + b) * L + i];
+      history[(static_cast<int64_t>(S - 1) * B + b) * L + i] = a;
+    }
+    const int stable = __syncthreads_and(eq);
+    if (i == 0) {
+      double acc = 0.0;
+      for (int k = 0; k < L; ++k) acc += static_cast<double>(sh[k]);
+      const float mean = static_cast<float>(acc / static_cast<double>(L));
+      finished[b] = (stable && mean < conf) ? 1 : 0;
+    }
+  }
+}
+
+}  // namespace
+
+size_t sampler_ws_layout(int64_t rows, int64_t V, int* nchunks_out, int* chunk_cols_out,
+                         size_t* off_ticket, size_t* off_bound, size_t* off_counter) {
+  int nch = 1;
+  while (static_cast<int64_t>(nch) * SP_TARGET_CHUNK < V && nch < (1 << 20)) nch <<= 1;
+  int64_t cols = (V + nch - 1) / nch;
+  cols = ((cols + SP_TILE - 1) / SP_TILE) * SP_TILE;
+  if (nchunks_out) *nchunks_out = nch;
+  if (chunk_cols_out) *chunk_cols_out = static_cast<int>(cols);
+  size_t o = static_cast<size_t>(rows) * nch * sizeof(Part);
+  o = (o + 255) & ~size_t(255);
+  if (off_ticket) *off_ticket = o;
+  o += static_cast<size_t>(rows) * 4;
+  o = (o + 255) & ~size_t(255);
+  if (off_bound) *off_bound = o;
+  o += static_cast<size_t>(rows) * 4;
+  o = (o + 255) & ~size_t(255);
+  if (off_counter) *off_counter = o;
+  o += 256;
+  return o;
+}
+
+}  // namespace knx
+
+extern "C" size_t knx_sampler_workspace_size(int64_t rows, int64_t V) {
+  if (rows < 0 || V <= 0) return 0;
+  return knx::sampler_ws_layout(rows, V, nullptr, nullptr, nullptr, nullptr, nullptr);
+}
+
+extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, float temperature,
+                                 int64_t seed, float* entropy, int64_t* samp, int64_t* amax,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace knx;
+  if (rows < 0 || V <= 0 || V > 0x7fffffffLL || rows > (1LL << 31)) return KNX_E_INVALID;
+  if (!(temperature > 0.f) || !isfinite(temperature)) return KNX_E_INVALID;
+  if (!aligned(logits, 4)) return KNX_E_ALIGN;
+  if (rows == 0) return KNX_OK;
+  int nch = 0, ccols = 0;
+  size_t o_ticket = 0, o_bound = 0, o_counter = 0;
+  const size_t need = sampler_ws_layout(rows, V, &nch, &ccols, &o_ticket, &o_bound, &o_counter);
+  if (workspace == nullptr || workspace_bytes < need) return KNX_E_WORKSPACE;
+  if (!aligned(workspace, 256)) return KNX_E_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  // per-row Gumbel bounds and the work counter start from zero every call; the row tickets
+  // are used modulo nchunks (a power of two), so they never need resetting.
+  if (cudaMemsetAsync(ws + o_bound, 0, o_counter + 256 - o_bound, s) != cudaSuccess)
+    return KNX_E_LAUNCH;
+  const float rtemp = 1.0f / temperature;
+  const int do_div = temperature != 1.0f;
+  const int seed_is32 = (seed >= -2147483648LL && seed <= 2147483647LL) ? 1 : 0;
+  const int want_g = samp != nullptr;
+  const bool vec = (V % 4) == 0 && aligned(logits, 16);
+  const int64_t items = rows * nch;
+  const int64_t maxgrid = static_cast<int64_t>(num_sms()) * 3;
+  const int grid = static_cast<int>(items < maxgrid ? items : maxgrid);
+  Part* parts = reinterpret_cast<Part*>(ws);
+  uint32_t* ticket = reinterpret_cast<uint32_t*>(ws + o_ticket);
+  uint32_t* bound = reinterpret_cast<uint32_t*>(ws + o_bound);
+  int* counter = reinterpret_cast<int*>(ws + o_counter);
+  if (vec) {
+    sampler_kernel<true><<<grid, SP_THREADS, 0, s>>>(logits, rows, static_cast<int>(V),
+                                                     temperature, rtemp, do_div, seed, seed_is32,
+                                                     want_g, nch, ccols, parts, ticket, bound,
+                                                     counter, entropy, samp, amax);
+  } else {
+    sampler_kernel<false><<<grid, SP_THREADS, 0, s>>>(logits, rows, static_cast<int>(V),
+                                                      temperature, rtemp, do_div, seed, seed_is32,
+                                                      want_g, nch, ccols, parts, ticket, bound,
+                                                      counter, entropy, samp, amax);
+  }
+  return launch_status();
+}
+
+extern "C" int knx_accept_stop(const float* entropy, const int64_t* cur, const int64_t* proposal,
+                               int64_t B, int64_t L, float entropy_bound, uint8_t* mask,
+                               int64_t* out, const int64_t* argmax, int64_t* history,
+                               int stability_threshold, float confidence_threshold,
+                               uint8_t* finished, void* stream) {
+  using namespace knx;
+  if (B < 0 || L <= 0 || L > 1024 || B > 65535 || stability_threshold < 0) return KNX_E_INVALID;
+  if (finished && stability_threshold > 0 && (history == nullptr || argmax == nullptr))
+    return KNX_E_INVALID;
+  if (out && (cur == nullptr || proposal == nullptr)) return KNX_E_INVALID;
+  if (B == 0) return KNX_OK;
+  const int threads = static_cast<int>(((L + 31) / 32) * 32);
+  accept_stop_kernel<<<static_cast<unsigned>(B), threads, 0, static_cast<cudaStream_t>(stream)>>>(
+      entropy, cur, proposal, static_cast<int>(B), static_cast<int>(L), entropy_bound, mask, out,
+      argmax, history, stability_threshold, confidence_threshold, finished);
+  return launch_status();
+}

@@ -1,0 +1,151 @@
+"""fast_sampler.py — DiffusionGemma denoising-step hooks on sm_100a (drop-in for the reference).
+
+install(parity=False) / uninstall() / stats() patch transformers' DiffusionGemma generation
+classes exactly where the reference does (fast_sampler.py:113-143):
+  * EntropyBoundSampler.accept_canvas  -> _accept_canvas  (fast_sampler.py:32-42)
+  * StableAndConfidentStoppingCriteria.__call__ -> _stop_call (fast_sampler.py:45-65)
+  * with parity=True also DiffusionGemmaGenerationMixin._denoising_step -> _denoising_step_parity
+    (fast_sampler.py:68-110), whose sampling block is ONE streaming pass over the processed logits
+    that yields entropy, Gumbel-max sample and argmax together (the reference needs two passes).
+The "bitexact" tier (parity=False) keeps the stock torch entropy chain and only removes the
+duplicate computation through the (data_ptr, _version) cache, like the reference.  The parity
+tier computes entropies, samples and the acceptance mask with the sm_100a kernels.
+"""
+import torch
+
+_STATE = {}
+_ORIG = {}
+_PARITY = {"on": False}
+
+
+def _G():
+    from transformers.models.diffusion_gemma import generation_diffusion_gemma as G
+    return G
+
+
+def _entropy(logits):
+    if _PARITY["on"]:
+        from fused_sampler_ops import fused_entropy
+        return fused_entropy(logits)
+    return torch.distributions.Categorical(logits=logits).entropy()
+
+
+def _cached_entropy(logits):
+    if _STATE.get("key") == (logits.data_ptr(), logits._version):
+        _STATE["hits"] = _STATE.get("hits", 0) + 1
+        return _STATE["entropy"]
+    _STATE["misses"] = _STATE.get("misses", 0) + 1
+    return None
+
+
+def _accept_canvas(self, current_canvas, denoiser_canvas, logits, cur_step):
+    token_entropy = _cached_entropy(logits) if _PARITY["on"] else None
+    if token_entropy is None:
+        token_entropy = _entropy(logits)
+    _STATE["key"] = (logits.data_ptr(), logits._version)
+    _STATE["entropy"] = token_entropy
+    if _PARITY["on"]:
+        from accept_ops import accept_canvas
+        mask, out = accept_canvas(token_entropy, current_canvas, denoiser_canvas, self.entropy_bound)
+        self.accepted_token_mask = mask
+        return out
+    sorted_h, sorted_idx = torch.sort(token_entropy, dim=-1, descending=False)
+    cum = torch.cumsum(sorted_h, dim=-1)
+    sel = cum - sorted_h <= self.entropy_bound
+    self.accepted_token_mask = torch.scatter(input=torch.zeros_like(sel), dim=-1, index=sorted_idx,
+                                             src=sel)
+    return torch.where(self.accepted_token_mask, denoiser_canvas, current_canvas)
+
+
+def _stop_call(self, argmax_canvas, logits, **kwargs):
+    if self.stability_threshold == 0:
+        stable = torch.ones((logits.shape[0]), device=logits.device, dtype=torch.bool)
+    else:
+        if self.argmax_canvas_history is None:
+            self.argmax_canvas_history = torch.full(
+                (self.stability_threshold, argmax_canvas.shape[0], argmax_canvas.shape[1]), -1,
+                dtype=argmax_canvas.dtype, device=argmax_canvas.device)
+        stable = (self.argmax_canvas_history == argmax_canvas[None, :, :]).all(dim=-1).all(dim=0)
+        self.argmax_canvas_history = torch.roll(self.argmax_canvas_history, shifts=-1, dims=0)
+        self.argmax_canvas_history[-1] = argmax_canvas
+    if _STATE.get("key") == (logits.data_ptr(), logits._version):
+        token_entropy = _STATE["entropy"]
+        _STATE["hits"] = _STATE.get("hits", 0) + 1
+    else:
+        token_entropy = _entropy(logits)
+        _STATE["misses"] = _STATE.get("misses", 0) + 1
+    confident = torch.mean(token_entropy, dim=-1) < self.confidence_threshold
+    return stable & confident
+
+
+def _denoising_step_parity(self, decoder_forward, current_canvas, argmax_canvas, input_ids,
+                           decoder_position_ids, self_conditioning_logits, mask_mapping,
+                           past_key_values, finished_denoising, cur_step, sampler,
+                           logits_processor, diffusion_stopping_criteria, **model_kwargs):
+    """The stock step except its sampling block, which is one fused pass (entropy + Gumbel-max +
+    argmax); the seed mixing is the reference's (fast_sampler.py:92)."""
+    from fused_sampler_ops import sample_step
+    step_int = int(cur_step)
+    cur_step = torch.tensor(cur_step, device=current_canvas.device, dtype=torch.int32)
+    torch.compiler.cudagraph_mark_step_begin()
+    decoder_outputs = decoder_forward(decoder_input_ids=current_canvas,
+                                      self_conditioning_logits=self_conditioning_logits,
+                                      decoder_attention_mask=mask_mapping,
+                                      past_key_values=past_key_values,
+                                      decoder_position_ids=decoder_position_ids, **model_kwargs)
+    processed_logits = logits_processor(input_ids, decoder_outputs.logits, cur_step=cur_step)
+    batch_size, canvas_length = current_canvas.shape
+    seed = (int(torch.randint(0, 2**31 - 1, (1,)).item()) ^ (step_int * 0x9E3779B1)) & 0x7FFFFFFF
+    ent, samp, amax = sample_step(processed_logits, seed)
+    _STATE["key"] = (processed_logits.data_ptr(), processed_logits._version)
+    _STATE["entropy"] = ent.view(batch_size, canvas_length)
+    denoiser_canvas = samp.view(batch_size, canvas_length)
+    new_argmax_canvas = amax.view(batch_size, canvas_length)
+    accepted = sampler.accept_canvas(current_canvas, denoiser_canvas, processed_logits, cur_step)
+    accepted = accepted.clone()
+    new_current_canvas = sampler.renoise_canvas(accepted, cur_step).clone()
+    if diffusion_stopping_criteria is not None:
+        if finished_denoising.any():
+            new_argmax_canvas = torch.where(finished_denoising[:, None], argmax_canvas,
+                                            new_argmax_canvas)
+            new_current_canvas = torch.where(finished_denoising[:, None], current_canvas,
+                                             new_current_canvas)
+            processed_logits = torch.where(finished_denoising[:, None, None],
+                                           self_conditioning_logits, processed_logits)
+        finished_denoising |= diffusion_stopping_criteria(new_argmax_canvas, processed_logits)
+    emb_dtype = self.model.decoder.embed_tokens.weight.dtype
+    self_conditioning_logits = processed_logits.to(emb_dtype)
+    return new_current_canvas, new_argmax_canvas, self_conditioning_logits, finished_denoising
+
+
+def install(parity=False):
+    if _ORIG:
+        if bool(parity) != _PARITY["on"]:
+            raise RuntimeError(f"fast_sampler already installed with parity={_PARITY['on']}; "
+                               f"call uninstall() before install(parity={bool(parity)})")
+        return
+    G = _G()
+    _PARITY["on"] = bool(parity)
+    _ORIG["accept"] = G.EntropyBoundSampler.accept_canvas
+    _ORIG["stop"] = G.StableAndConfidentStoppingCriteria.__call__
+    G.EntropyBoundSampler.accept_canvas = _accept_canvas
+    G.StableAndConfidentStoppingCriteria.__call__ = _stop_call
+    if parity:
+        _ORIG["step"] = G.DiffusionGemmaGenerationMixin._denoising_step
+        G.DiffusionGemmaGenerationMixin._denoising_step = _denoising_step_parity
+    _STATE.clear()
+
+
+def uninstall():
+    if not _ORIG:
+        return
+    G = _G()
+    G.EntropyBoundSampler.accept_canvas = _ORIG.pop("accept")
+    G.StableAndConfidentStoppingCriteria.__call__ = _ORIG.pop("stop")
+    if "step" in _ORIG:
+        G.DiffusionGemmaGenerationMixin._denoising_step = _ORIG.pop("step")
+    _PARITY["on"] = False
+
+
+def stats():
+    return {k: _STATE.get(k, 0) for k in ("hits", "misses")}

@@ -1,0 +1,62 @@
+"""The C-ABI library loads on a machine without a GPU, exports every symbol include/knx.h
+declares, and rejects contract violations on the host before touching the device."""
+import ctypes
+import re
+
+import pytest
+
+import _knx
+from conftest import REPO
+
+
+def header_symbols():
+    text = (REPO / "include" / "knx.h").read_text()
+    return sorted(set(re.findall(r"KNX_API\s+[\w\s\*]+?\b(knx_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _knx.load()
+    declared = header_symbols()
+    assert len(declared) >= 14
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert set(declared) == set(_knx.exported_symbols())
+
+
+def test_status_strings_and_version():
+    lib = _knx.load()
+    assert lib.knx_version() > 0
+    assert lib.knx_status_string(0) == b"ok"
+    assert b"workspace" in lib.knx_status_string(-3)
+
+
+def test_workspace_sizes_are_host_only_and_monotone():
+    lib = _knx.load()
+    a = lib.knx_moe_w4_workspace_size(256, 2816, 704, 128, 8)
+    b = lib.knx_moe_w4_workspace_size(512, 2816, 704, 128, 8)
+    assert 0 < a < b
+    assert a % 256 == 0
+    assert lib.knx_sampler_workspace_size(256, 262144) > 256 * 8 * 32
+    assert lib.knx_router_workspace_size(256, 128) >= 4 * 256 * 128 * 4
+    assert lib.knx_w4a16_workspace_size(64, 2816) >= 64 * 2816 * 2
+
+
+@pytest.mark.parametrize("H,I,gs_gu,gs_dn,expect", [
+    (2816 + 8, 704, 128, 64, -5),   # H % 256 != 0
+    (2816, 700, 128, 64, -5),       # I % 64 != 0
+    (2816, 704, 100, 64, -1),       # group size not a multiple of 32
+    (2816, 704, 128, 48, -1),
+])
+def test_moe_contract_violations_rejected_on_host(H, I, gs_gu, gs_dn, expect):
+    lib = _knx.load()
+    st = lib.knx_moe_w4(None, None, 0, None, 4, None, 2, None, None, None, None, None, None,
+                        256, H, I, 128, 8, gs_gu, gs_dn, None, 0, None, None, None)
+    assert st == expect
+
+
+def test_sampler_and_accept_reject_bad_arguments():
+    lib = _knx.load()
+    assert lib.knx_sampler_fused(None, 4, 100, 0.0, 1, None, None, None, None, 0, None) == -1
+    assert lib.knx_sampler_fused(None, 4, 100, 1.0, 1, None, None, None, None, 0, None) == -3
+    assert lib.knx_accept_stop(None, None, None, 1, 2048, 0.1, None, None, None, None, 0, 0.0,
+                               None, None) == -1
