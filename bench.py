@@ -271,6 +271,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=("layer", "sampler"), default=None,
+                    help="run just one workload (used for profiling captures); prints its timing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -283,6 +285,16 @@ def main():
     dist = world > 1
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if args.only == "layer":
+        ms, stages, counts, _ = time_layer(dev, args.steps, args.warmup, False)
+        print(json.dumps({"only": "layer", "us_per_layer": ms * 1000.0 / args.steps,
+                          "stages_us": {k: v * 1000.0 for k, v in stages.items()}}), flush=True)
+        return
+    if args.only == "sampler":
+        step_ms, kern_ms = time_sampler(dev)
+        print(json.dumps({"only": "sampler", "step_us": step_ms * 1000.0,
+                          "kernel_us": kern_ms * 1000.0}), flush=True)
+        return
     if dist:
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),

@@ -44,6 +44,8 @@ extern "C" {
 /* device error bits (OR-ed into *err when err != NULL) */
 #define KNX_DEV_BAD_EXPERT_ID 0x1 /* topk id < 0 or > E (id == E is the "dropped" sentinel) */
 #define KNX_DEV_CAPACITY 0x2      /* a per-launch capacity bound was exceeded                */
+#define KNX_DEV_TIMEOUT 0x4       /* a bounded on-chip wait gave up (protocol error); the call's
+                                     outputs are invalid, the device and context stay usable  */
 
 /* ---- dtypes ----------------------------------------------------------------------------- */
 #define KNX_F16 0
@@ -51,6 +53,10 @@ extern "C" {
 #define KNX_F32 2
 #define KNX_I32 3
 #define KNX_I64 4
+
+/* weight-format / engine flags */
+#define KNX_W4_INT_ZEROS 0x1 /* all zero-points are integers in [0, 15] */
+#define KNX_W4_WARP_MMA 0x2  /* use the warp-level mma.sync kernels instead of tcgen05 (A/B runs) */
 
 KNX_API int knx_version(void);
 /* 1 when the current device is a compute-capability 10.0 part (the only target). */
@@ -110,24 +116,30 @@ KNX_API int knx_moe_align(const void* topk_ids, int ids_dtype, int64_t T, int to
  * topk_ids: [T,topk] i32/i64; topk_w: [T,topk] F16/BF16/F32.
  * hidden_perm: optional f16 [T,H] copy of hidden already in the MoE K-interleave (as written by
  *   knx_rmsnorm's xperm); NULL = the layer builds it in its workspace.
+ * flags & KNX_W4_INT_ZEROS: the caller guarantees every zero-point is an integer in [0,15] (what
+ *   quantize_w4 writes, w4a16.py:27); weights are then dequantised bit-identically to dequant_w4
+ *   (one rounding of (q - z) * s).  Without it any fp16 zero-point is accepted and weights are
+ *   RN16(RN16(q - z) * s), the fp16 arithmetic of the reference kernel (fused_moe_w4_v2.py:126-128).
  * Contracts (fused_moe_w4_v2.py:325-328): H % 256 == 0, I % 64 == 0, gs_gu % 32 == 0 and
- *   divides H, gs_dn % 32 == 0 and divides I, topk <= 16, E <= 1024.
+ *   divides H, gs_dn % 32 == 0 and divides I, H/gs_gu <= 56, I/gs_dn <= 56, topk <= 16,
+ *   E <= 256, T*topk <= 32768.
  * workspace: >= knx_moe_w4_workspace_size(T, H, I, E, topk) bytes, 256-byte aligned. */
 KNX_API size_t knx_moe_w4_workspace_size(int64_t T, int64_t H, int64_t I, int E, int topk);
 KNX_API int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidden_dtype, const void* topk_ids,
                int ids_dtype, const void* topk_w, int w_dtype, const uint8_t* gu_q,
                const void* gu_s, const void* gu_z, const uint8_t* dn_q, const void* dn_s,
                const void* dn_z, int64_t T, int64_t H, int64_t I, int E, int topk, int gs_gu,
-               int gs_dn, void* workspace, size_t workspace_bytes, void* out, int32_t* err,
-               void* stream);
+               int gs_dn, int flags, void* workspace, size_t workspace_bytes, void* out,
+               int32_t* err, void* stream);
 
 /* ---- dense W4A16 linear -------------------------------------------------------------------
  * Replaces w4a16_linear (w4a16.py:96-108):  Y[M,N] = X[M,K] . dequant(q,s,z)^T, f16 out.
- * X: f16 [M,K] row-major; q u8 [N,K/2]; s,z f16 [N,K/gs].  K % 64 == 0, gs % 32 == 0, gs | K.
+ * X: f16 [M,K] row-major; q u8 [N,K/2]; s,z f16 [N,K/gs].  K % 64 == 0, gs % 32 == 0, gs | K,
+ * K/gs <= 56, N % 8 == 0.  flags: KNX_W4_INT_ZEROS as for knx_moe_w4.
  * workspace: >= knx_w4a16_workspace_size(M, K) bytes. */
 KNX_API size_t knx_w4a16_workspace_size(int64_t M, int64_t K);
 KNX_API int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, const void* z, int64_t M,
-                     int64_t N, int64_t K, int gs, void* Y, void* workspace,
+                     int64_t N, int64_t K, int gs, int flags, void* Y, void* workspace,
                      size_t workspace_bytes, void* stream);
 
 /* ---- sampler ------------------------------------------------------------------------------

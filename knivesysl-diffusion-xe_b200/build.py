@@ -53,7 +53,7 @@ def build(force=False, verbose=False, extra=()):
     stamp = BUILD / "lib.stamp"
     key = ",".join(o.name for o in objs)
     if force or not LIB.exists() or not stamp.exists() or stamp.read_text() != key:
-        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart", "-lcuda"]
+        cmd = [NVCC, *ARCH, "-shared", "-o", str(LIB), *map(str, objs), "-lcudart"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)

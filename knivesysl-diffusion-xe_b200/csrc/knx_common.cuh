@@ -11,6 +11,7 @@
 #include "knx.h"
 
 #define KNX_DEVINL __device__ __forceinline__
+#define KNX_HOST_DEVINL __host__ __device__ __forceinline__
 
 namespace knx {
 
@@ -102,24 +103,51 @@ KNX_DEVINL void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, 
 KNX_DEVINL int kperm_pos(int i) { return 2 * (i & 3) + (i >> 2); }
 
 // Dequantise the 8 nibbles of one u32 (row bytes 4q..4q+3, nibble i = k 8q+i, low nibble = even
-// k) into four f16x2 A-fragment registers:
-//   w0 = (k0,k4)  w1 = (k1,k5)  w2 = (k2,k6)  w3 = (k3,k7),   w = n*s + nzs,  nzs = -z*s.
-// 0x6400 is f16 1024: OR-ing a nibble into the low mantissa bits gives 1024 + n exactly, so
-// n = h - 1024.  An upper nibble lands at 1024 + 16n, and n = h/16 - 64 exactly (one fma).
-KNX_DEVINL void dequant8(uint32_t u, __half2 s, __half2 nzs, uint32_t (&w)[4]) {
+// k) into four f16x2 A-fragment registers:  w0 = (k0,k4)  w1 = (k1,k5)  w2 = (k2,k6)  w3 = (k3,k7).
+// 0x6400 is f16 1024: OR-ing a low nibble into the mantissa gives h = 1024 + n exactly; a high
+// nibble lands at h = 1024 + 16n.  Per (row, group) the caller supplies
+//   s  = (s, s),   s16 = (s/16, s/16)
+// and, for ZINT (integer zero-points 0..15, what quantize_w4 produces):
+//   c  = 1024 + z,  c16 = 1024 + 16z      w = (h - c) * s    = RN16((n - z) * s)     exact
+//                                          w = (h - c16) * s16 = RN16((n - z) * s)   exact
+// i.e. bit-identical to the fp32 dequant rounded once (dequant_w4);  otherwise (any fp16 z):
+//   c  = z,  c16 = 16z                     w = RN16(RN16(n - z) * s)
+// which is the fp16 arithmetic of the reference kernel, (w - z) * s (fused_moe_w4_v2.py:126-128).
+// (s/16 is exact for s >= 2^-10; smaller scales round their last bits.)
+template <bool ZINT>
+KNX_DEVINL void dequant8(uint32_t u, __half2 s, __half2 s16, __half2 c, __half2 c16,
+                         uint32_t (&w)[4]) {
   const uint32_t MAG = 0x64006400u;
-  const __half2 k1024 = u32_as_h2(0x64006400u);   // (1024, 1024)
-  const __half2 k1_16 = u32_as_h2(0x2c002c00u);   // (1/16, 1/16)
-  const __half2 km64 = u32_as_h2(0xd400d400u);    // (-64, -64)
   const uint32_t p0 = lop3_and_or(u, 0x000F000Fu, MAG);
   const uint32_t p1 = lop3_and_or(u, 0x00F000F0u, MAG);
   const uint32_t u8 = u >> 8;
   const uint32_t p2 = lop3_and_or(u8, 0x000F000Fu, MAG);
   const uint32_t p3 = lop3_and_or(u8, 0x00F000F0u, MAG);
-  w[0] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(p0), k1024), s, nzs));
-  w[1] = h2_as_u32(__hfma2(__hfma2(u32_as_h2(p1), k1_16, km64), s, nzs));
-  w[2] = h2_as_u32(__hfma2(__hsub2(u32_as_h2(p2), k1024), s, nzs));
-  w[3] = h2_as_u32(__hfma2(__hfma2(u32_as_h2(p3), k1_16, km64), s, nzs));
+  if constexpr (ZINT) {
+    w[0] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(p0), c), s));
+    w[1] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(p1), c16), s16));
+    w[2] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(p2), c), s));
+    w[3] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(p3), c16), s16));
+  } else {
+    const __half2 k1024 = u32_as_h2(MAG);
+    w[0] = h2_as_u32(__hmul2(__hsub2(__hsub2(u32_as_h2(p0), k1024), c), s));
+    w[1] = h2_as_u32(__hmul2(__hsub2(__hsub2(u32_as_h2(p1), k1024), c16), s16));
+    w[2] = h2_as_u32(__hmul2(__hsub2(__hsub2(u32_as_h2(p2), k1024), c), s));
+    w[3] = h2_as_u32(__hmul2(__hsub2(__hsub2(u32_as_h2(p3), k1024), c16), s16));
+  }
+}
+
+// Per (row, group) dequant constants, packed as two f16x2: {s, c} and {s/16, c16} (see dequant8).
+template <bool ZINT>
+KNX_DEVINL uint2 make_sz(__half s, __half z) {
+  const float sf = __half2float(s), zf = __half2float(z);
+  const __half s16 = __float2half_rn(sf * 0.0625f);
+  const __half c = ZINT ? __float2half_rn(1024.0f + zf) : z;
+  const __half c16 = __float2half_rn(ZINT ? 1024.0f + 16.0f * zf : 16.0f * zf);
+  uint2 r;
+  r.x = (static_cast<uint32_t>(__half_as_ushort(c)) << 16) | __half_as_ushort(s);
+  r.y = (static_cast<uint32_t>(__half_as_ushort(c16)) << 16) | __half_as_ushort(s16);
+  return r;
 }
 
 KNX_DEVINL float warp_sum(float v) {

@@ -38,7 +38,7 @@ namespace {
 constexpr int THREADS = 256;
 constexpr int M_MAX = 32;       // tokens per task
 constexpr int NT = M_MAX / 8;   // n8 tiles per task
-constexpr int SZ_MAX_GROUPS = 64;
+constexpr int SZ_MAX_GROUPS = 56;  // H/gs (gate_up) and I/gs (down) limit
 
 // GEMM1 (gate_up + GELU): slice = 64 gate rows + the matching 64 up rows, 256 k per stage.
 constexpr int G1_ROWS = 64;
@@ -59,8 +59,16 @@ constexpr int G2_AROW = G2_BK * 2 + 64;                   // 320 B
 constexpr int G2_STAGE_BYTES = G2_WBYTES + M_MAX * G2_AROW;  // 18 KB
 constexpr int G2_OROW = G2_ROWS * 2 + 16;                 // epilogue tile row (272 B)
 
-inline size_t g1_smem(int ng) { return size_t(G1_STAGES) * G1_STAGE_BYTES + size_t(1024) * ng; }
-inline size_t g2_smem(int ng) { return size_t(G2_STAGES) * G2_STAGE_BYTES + size_t(1024) * ng; }
+// + raw scale/zero blocks (512*ng bytes) + per (row, group) dequant constants (128 rows x ng x 8 B)
+inline size_t g1_smem(int ng) { return size_t(G1_STAGES) * G1_STAGE_BYTES + size_t(1536) * ng; }
+inline size_t g2_smem(int ng) { return size_t(G2_STAGES) * G2_STAGE_BYTES + size_t(1536) * ng; }
+
+KNX_DEVINL void unpack_sz(uint2 v, __half2& s, __half2& s16, __half2& c, __half2& c16) {
+  s = __low2half2(u32_as_h2(v.x));
+  c = __high2half2(u32_as_h2(v.x));
+  s16 = __low2half2(u32_as_h2(v.y));
+  c16 = __high2half2(u32_as_h2(v.y));
+}
 
 // position of channel n inside the MoE K-interleave of its 8-group
 KNX_DEVINL int perm_pos(int n) { return (n & ~7) + 2 * (n & 3) + ((n >> 2) & 1); }
@@ -73,13 +81,8 @@ KNX_DEVINL float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + th);
 }
 
-// Convert the raw scale/zero block (rows x ng halfs each) into {s, -z*s} pairs.
-KNX_DEVINL uint32_t make_sz(__half s, __half z) {
-  const __half nzs = __float2half_rn(-(__half2float(z) * __half2float(s)));
-  return (static_cast<uint32_t>(__half_as_ushort(nzs)) << 16) | __half_as_ushort(s);
-}
-
 // ------------------------------------------------------------------------------------------
+template <bool ZINT>
 __global__ void __launch_bounds__(THREADS, 1)
     gateup_gelu_kernel(const __half* __restrict__ xp, const int32_t* __restrict__ sorted_pair,
                        int topk, const int32_t* __restrict__ offsets,
@@ -95,7 +98,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int nslices = I / G1_ROWS;
   const int nwork = *ntasks_ptr * nslices;
   uint8_t* sz_raw = smem + G1_STAGES * G1_STAGE_BYTES;  // 4 blocks x 64*ng halfs
-  uint32_t* sz2 = reinterpret_cast<uint32_t*>(sz_raw + 512 * ng);  // [128 rows][ng]
+  uint2* sz2 = reinterpret_cast<uint2*>(sz_raw + 512 * ng);  // [128 rows][ng]
   const int rowbytes = H >> 1;
   const int nst = H / G1_BK;
   const int mt = warp & 3, kh = warp >> 2;
@@ -166,7 +169,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const __half* rs = reinterpret_cast<const __half*>(sz_raw + blk * 128 * ng);
           const __half* rz = reinterpret_cast<const __half*>(sz_raw + (blk + 1) * 128 * ng);
           const int rr = row & (G1_ROWS - 1);
-          sz2[row * ng + grp] = make_sz(rs[rr * ng + grp], rz[rr * ng + grp]);
+          sz2[row * ng + grp] = make_sz<ZINT>(rs[rr * ng + grp], rz[rr * ng + grp]);
         }
         __syncthreads();
       }
@@ -180,29 +183,24 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t wg0 = Wb + r0 * G1_WROW, wg8 = wg0 + 8 * G1_WROW;
       const uint32_t wu0 = Wb + (G1_ROWS + r0) * G1_WROW, wu8 = wu0 + 8 * G1_WROW;
       int cur = -1;
-      __half2 sg0, zg0, sg8, zg8, su0, zu0, su8, zu8;
+      __half2 sg0, tg0, cg0, dg0, sg8, tg8, cg8, dg8, su0, tu0, cu0, du0, su8, tu8, cu8, du8;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int ss = 4 * kh + j;
         const int grp = (st * G1_BK + ss * 32) / gs;
         if (grp != cur) {
           cur = grp;
-          uint32_t v;
-          v = sz2[r0 * ng + grp];
-          sg0 = __low2half2(u32_as_h2(v)); zg0 = __high2half2(u32_as_h2(v));
-          v = sz2[(r0 + 8) * ng + grp];
-          sg8 = __low2half2(u32_as_h2(v)); zg8 = __high2half2(u32_as_h2(v));
-          v = sz2[(G1_ROWS + r0) * ng + grp];
-          su0 = __low2half2(u32_as_h2(v)); zu0 = __high2half2(u32_as_h2(v));
-          v = sz2[(G1_ROWS + r0 + 8) * ng + grp];
-          su8 = __low2half2(u32_as_h2(v)); zu8 = __high2half2(u32_as_h2(v));
+          unpack_sz(sz2[r0 * ng + grp], sg0, tg0, cg0, dg0);
+          unpack_sz(sz2[(r0 + 8) * ng + grp], sg8, tg8, cg8, dg8);
+          unpack_sz(sz2[(G1_ROWS + r0) * ng + grp], su0, tu0, cu0, du0);
+          unpack_sz(sz2[(G1_ROWS + r0 + 8) * ng + grp], su8, tu8, cu8, du8);
         }
         const uint32_t cho = ((ss ^ (r0 & 7)) << 4) + 4 * q;
         uint32_t fg0[4], fg8[4], fu0[4], fu8[4];
-        dequant8(lds32(wg0 + cho), sg0, zg0, fg0);
-        dequant8(lds32(wg8 + cho), sg8, zg8, fg8);
-        dequant8(lds32(wu0 + cho), su0, zu0, fu0);
-        dequant8(lds32(wu8 + cho), su8, zu8, fu8);
+        dequant8<ZINT>(lds32(wg0 + cho), sg0, tg0, cg0, dg0, fg0);
+        dequant8<ZINT>(lds32(wg8 + cho), sg8, tg8, cg8, dg8, fg8);
+        dequant8<ZINT>(lds32(wu0 + cho), su0, tu0, cu0, du0, fu0);
+        dequant8<ZINT>(lds32(wu8 + cho), su8, tu8, cu8, du8, fu8);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           if (nt < ntl) {
@@ -261,6 +259,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // Generic "rows-by-slot" W4A16 GEMM used for the MoE down projection and the dense linear:
 //   out[slot, n] = sum_k act[slot, k] * dequant(q[e, n, k]),   act in the K-interleave.
 // tasks == nullptr: dense mode, task t = rows [32t, 32t+32) of expert 0, static striding.
+template <bool ZINT>
 __global__ void __launch_bounds__(THREADS, 2)
     rows_gemm_kernel(const __half* __restrict__ act, int64_t act_stride, int K,
                      const int32_t* __restrict__ offsets, const int4* __restrict__ tasks,
@@ -276,7 +275,7 @@ __global__ void __launch_bounds__(THREADS, 2)
   const int ntasks = tasks ? *ntasks_ptr : (dense_rows + M_MAX - 1) / M_MAX;
   const int nwork = ntasks * nslices;
   uint8_t* sz_raw = smem + G2_STAGES * G2_STAGE_BYTES;               // s block, z block
-  uint32_t* sz2 = reinterpret_cast<uint32_t*>(sz_raw + 512 * ng);    // [128][ng]
+  uint2* sz2 = reinterpret_cast<uint2*>(sz_raw + 512 * ng);          // [128][ng]
   const int rowbytes = K >> 1;
   const int nst = (K + G2_BK - 1) / G2_BK;
   const int r0 = 16 * warp + g;
@@ -358,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 2)
       if (st == 0) {
         const __half* rs = reinterpret_cast<const __half*>(sz_raw);
         const __half* rz = reinterpret_cast<const __half*>(sz_raw + 256 * ng);
-        for (int i = tid; i < nvalid * ng; i += THREADS) sz2[i] = make_sz(rs[i], rz[i]);
+        for (int i = tid; i < nvalid * ng; i += THREADS) sz2[i] = make_sz<ZINT>(rs[i], rz[i]);
         __syncthreads();
       }
       {
@@ -373,22 +372,21 @@ __global__ void __launch_bounds__(THREADS, 2)
       const int nss = min(G2_BK, K - k0) >> 5;
       const bool rows_ok = r0 < nvalid;  // r0 + 8 may still be out of range: garbage, not stored
       int cur = -1;
-      __half2 s0, z0, s8, z8;
+      __half2 s0, t0_, c0, d0, s8, t8, c8, d8;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (j < nss && rows_ok) {
           const int grp = (k0 + 32 * j) / gs;
           if (grp != cur) {
             cur = grp;
-            uint32_t v = sz2[r0 * ng + grp];
-            s0 = __low2half2(u32_as_h2(v)); z0 = __high2half2(u32_as_h2(v));
-            v = (r0 + 8 < nvalid) ? sz2[(r0 + 8) * ng + grp] : 0u;
-            s8 = __low2half2(u32_as_h2(v)); z8 = __high2half2(u32_as_h2(v));
+            unpack_sz(sz2[r0 * ng + grp], s0, t0_, c0, d0);
+            unpack_sz((r0 + 8 < nvalid) ? sz2[(r0 + 8) * ng + grp] : make_uint2(0u, 0u), s8, t8,
+                      c8, d8);
           }
           const uint32_t cho = ((j ^ swz) << 4) + 4 * q;
           uint32_t f0[4], f8[4];
-          dequant8(lds32(w0 + cho), s0, z0, f0);
-          dequant8(lds32(w8 + cho), s8, z8, f8);
+          dequant8<ZINT>(lds32(w0 + cho), s0, t0_, c0, d0, f0);
+          dequant8<ZINT>(lds32(w8 + cho), s8, t8, c8, d8, f8);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             if (nt < ntl) {
@@ -508,11 +506,16 @@ bool set_smem_attrs() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!done[dev & 63]) {
-    if (cudaFuncSetAttribute(gateup_gelu_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(g1_smem(SZ_MAX_GROUPS))) != cudaSuccess)
-      return false;
-    if (cudaFuncSetAttribute(rows_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(g2_smem(SZ_MAX_GROUPS))) != cudaSuccess)
+    const int m1 = static_cast<int>(g1_smem(SZ_MAX_GROUPS));
+    const int m2 = static_cast<int>(g2_smem(SZ_MAX_GROUPS));
+    if (cudaFuncSetAttribute(gateup_gelu_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             m1) != cudaSuccess ||
+        cudaFuncSetAttribute(gateup_gelu_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             m1) != cudaSuccess ||
+        cudaFuncSetAttribute(rows_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             m2) != cudaSuccess ||
+        cudaFuncSetAttribute(rows_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             m2) != cudaSuccess)
       return false;
     done[dev & 63] = true;
   }
@@ -533,9 +536,10 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
                           const uint8_t* gu_q, const void* gu_s, const void* gu_z,
                           const uint8_t* dn_q, const void* dn_s, const void* dn_z, int64_t T,
                           int64_t H, int64_t I, int E, int topk, int gs_gu, int gs_dn,
-                          void* workspace, size_t workspace_bytes, void* out, int32_t* err,
-                          void* stream) {
+                          int flags, void* workspace, size_t workspace_bytes, void* out,
+                          int32_t* err, void* stream) {
   using namespace knx;
+  const bool zint = (flags & KNX_W4_INT_ZEROS) != 0;
   if (T < 0 || H <= 0 || I <= 0 || E <= 0 || topk <= 0 || topk > 16) return KNX_E_INVALID;
   if ((H % G1_BK) != 0 || (I % G1_ROWS) != 0 || H > (1 << 20) || I > (1 << 20))
     return KNX_E_UNSUPPORTED;
@@ -567,18 +571,36 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
     if (st != KNX_OK) return st;
     xp = w.xp;
   }
-  st = launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0, M_MAX, w.counts,
+  const bool use_tc = !(flags & KNX_W4_WARP_MMA) &&
+                      tc_supported(H, gs_gu, ng1, 2 * I, true) &&
+                      tc_supported(I, gs_dn, ng2, H, false);
+  const int task_tokens = use_tc ? TC_TASK_TOKENS : M_MAX;
+  st = launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0, task_tokens, w.counts,
                     w.offsets, w.sorted_pair, w.inv, nullptr, nullptr, nullptr, w.tasks, w.ntasks,
                     w.counters, 2, err, s);
   if (st != KNX_OK) return st;
   const int64_t N = T * topk;
-  const int64_t max_tasks = (N + M_MAX - 1) / M_MAX + E;
+  const int64_t max_tasks = (N + task_tokens - 1) / task_tokens + E;
   const int sms = num_sms();
   prof::mark(pc, 1, s);
+  if (use_tc) {
+    st = launch_tc_gateup(xp, w.sorted_pair, topk, w.offsets, w.tasks, w.ntasks, w.counters, gu_q,
+                          static_cast<const __half*>(gu_s), static_cast<const __half*>(gu_z), E,
+                          static_cast<int>(H), static_cast<int>(I), ng1, gs_gu, zint, w.out2,
+                          max_tasks, err, s);
+    if (st != KNX_OK) return st;
+    prof::mark(pc, 2, s);
+    st = launch_tc_rows(w.out2, I, static_cast<int>(I), w.offsets, w.tasks, w.ntasks, 0,
+                        w.counters + 1, dn_q, static_cast<const __half*>(dn_s),
+                        static_cast<const __half*>(dn_z), E, static_cast<int>(H), ng2, gs_dn, zint,
+                        w.out3, H, max_tasks, err, s);
+    if (st != KNX_OK) return st;
+  } else {
   {
     const int64_t work = max_tasks * (I / G1_ROWS);
     const int grid = static_cast<int>(work < sms ? work : sms);
-    gateup_gelu_kernel<<<grid, THREADS, g1_smem(ng1), s>>>(
+    auto kern = zint ? gateup_gelu_kernel<true> : gateup_gelu_kernel<false>;
+    kern<<<grid, THREADS, g1_smem(ng1), s>>>(
         xp, w.sorted_pair, topk, w.offsets, w.tasks, w.ntasks, w.counters,
         gu_q, static_cast<const __half*>(gu_s), static_cast<const __half*>(gu_z),
         static_cast<int>(H), static_cast<int>(I), ng1, gs_gu, w.out2);
@@ -589,12 +611,14 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
   {
     const int64_t work = max_tasks * ((H + G2_ROWS - 1) / G2_ROWS);
     const int grid = static_cast<int>(work < 2 * sms ? work : 2 * sms);
-    rows_gemm_kernel<<<grid, THREADS, g2_smem(ng2), s>>>(
+    auto kern = zint ? rows_gemm_kernel<true> : rows_gemm_kernel<false>;
+    kern<<<grid, THREADS, g2_smem(ng2), s>>>(
         w.out2, I, static_cast<int>(I), w.offsets, w.tasks, w.ntasks, 0, w.counters + 1, dn_q,
         static_cast<const __half*>(dn_s), static_cast<const __half*>(dn_z), static_cast<int>(H),
         ng2, gs_dn, w.out3, H);
     st = launch_status();
     if (st != KNX_OK) return st;
+  }
   }
   prof::mark(pc, 3, s);
   {
@@ -615,12 +639,12 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
 
 extern "C" size_t knx_w4a16_workspace_size(int64_t M, int64_t K) {
   if (M < 0 || K <= 0) return 0;
-  return knx::up256(size_t(M) * size_t(K) * 2);
+  return knx::up256(size_t(M) * size_t(K) * 2) + 256;  // K-interleaved X + a work counter
 }
 
 extern "C" int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, const void* z,
-                                int64_t M, int64_t N, int64_t K, int gs, void* Y, void* workspace,
-                                size_t workspace_bytes, void* stream) {
+                                int64_t M, int64_t N, int64_t K, int gs, int flags, void* Y,
+                                void* workspace, size_t workspace_bytes, void* stream) {
   using namespace knx;
   if (M < 0 || N <= 0 || K <= 0 || (K % 64) != 0 || (N % 8) != 0 || gs <= 0 || (gs % 32) != 0 ||
       (K % gs) != 0 || M > (1 << 28) || N > (1 << 24) || K > (1 << 20))
@@ -639,10 +663,21 @@ extern "C" int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, 
   __half* xp = static_cast<__half*>(workspace);
   int rc = launch_permute(X, KNX_F16, xp, M * K, st);
   if (rc != KNX_OK) return rc;
+  const bool zint = (flags & KNX_W4_INT_ZEROS) != 0;
+  if (!(flags & KNX_W4_WARP_MMA) && tc_supported(K, gs, ng, N, false)) {
+    int* counter = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + up256(size_t(M) * K * 2));
+    if (cudaMemsetAsync(counter, 0, sizeof(int), st) != cudaSuccess) return KNX_E_LAUNCH;
+    return launch_tc_rows(xp, K, static_cast<int>(K), nullptr, nullptr, nullptr,
+                          static_cast<int>(M), counter, q, static_cast<const __half*>(s),
+                          static_cast<const __half*>(z), 1, static_cast<int>(N), ng, gs, zint,
+                          static_cast<__half*>(Y), N, (M + TC_TASK_TOKENS - 1) / TC_TASK_TOKENS,
+                          nullptr, st);
+  }
   const int64_t work = ((M + M_MAX - 1) / M_MAX) * ((N + G2_ROWS - 1) / G2_ROWS);
   const int sms = num_sms();
   const int grid = static_cast<int>(work < 2 * sms ? work : 2 * sms);
-  rows_gemm_kernel<<<grid, THREADS, g2_smem(ng), st>>>(
+  auto kern = zint ? rows_gemm_kernel<true> : rows_gemm_kernel<false>;
+  kern<<<grid, THREADS, g2_smem(ng), st>>>(
       xp, K, static_cast<int>(K), nullptr, nullptr, nullptr, static_cast<int>(M), nullptr, q,
       static_cast<const __half*>(s), static_cast<const __half*>(z), static_cast<int>(N), ng, gs,
       static_cast<__half*>(Y), N);

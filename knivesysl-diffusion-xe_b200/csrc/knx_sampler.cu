@@ -8,8 +8,9 @@
 // Layout / work split: a row of V logits is cut into a power-of-two number of chunks; a work item
 // is (row, chunk) and persistent CTAs pull items from a counter.  Each warp streams 512 columns
 // per step (4 float4 per lane) and keeps
-//   * an online softmax state (m, s, t) with t = sum (q-m) e^(q-m), so H = log s - t/s is a sum
-//     of two non-negative terms (no cancellation for peaked rows);
+//   * an online softmax state (m, sp, t): sp = sum e^(q-m) minus the max element's 1, t =
+//     sum (q-m) e^(q-m), so H = log1p(sp) - t/(1+sp) is a sum of two non-negative terms and keeps
+//     its relative precision for peaked (near-zero entropy) rows;
 //   * the running argmax of q;
 //   * the running Gumbel winner.  Gumbel noise is bounded above by GUMBEL_MAX, so an element with
 //     q + GUMBEL_MAX < W (W = best q+g seen anywhere in the row so far, shared through a per-row
@@ -52,18 +53,25 @@ KNX_DEVINL float ex2(float x) {
 }
 constexpr float LOG2E = 1.4426950408889634f;
 
-// merge online-softmax states: (m,s,t) with t = sum (q-m) e^(q-m)
-KNX_DEVINL void sm_merge(float& m, float& s, float& t, float m2, float s2, float t2) {
-  if (s2 == 0.f) return;
-  if (s == 0.f) {
-    m = m2; s = s2; t = t2;
+// Online-softmax state (m, sp, t) of a set of logits q:  m = max q,  S = sum e^(q-m) = 1 + sp
+// (sp excludes one element equal to the max, so tiny entropies keep their relative precision),
+// t = sum (q-m) e^(q-m) <= 0.  Entropy = log S - t/S = log1p(sp) - t/(1+sp).  m = -inf: empty.
+KNX_DEVINL void sm_merge(float& m, float& sp, float& t, float m2, float sp2, float t2) {
+  if (m2 == -INFINITY) return;
+  if (m == -INFINITY) {
+    m = m2; sp = sp2; t = t2;
     return;
   }
-  const float M = fmaxf(m, m2);
-  const float a = ex2((m - M) * LOG2E), b = ex2((m2 - M) * LOG2E);
-  t = a * (t + (m - M) * s) + b * (t2 + (m2 - M) * s2);
-  s = a * s + b * s2;
-  m = M;
+  if (m >= m2) {
+    const float a = ex2((m2 - m) * LOG2E), S2 = 1.0f + sp2;
+    t = t + a * (t2 + (m2 - m) * S2);
+    sp = sp + a * S2;
+  } else {
+    const float a = ex2((m - m2) * LOG2E), S1 = 1.0f + sp;
+    t = t2 + a * (t + (m - m2) * S1);
+    sp = sp2 + a * S1;
+    m = m2;
+  }
 }
 KNX_DEVINL void arg_merge(float& v, int& i, float v2, int i2) {
   if (v2 > v || (v2 == v && i2 < i)) {
@@ -146,7 +154,7 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
         }
       }
       float tm = -INFINITY;
-      int ti = 0x7fffffff;
+      int ti = 0x7fffffff, imax = -1;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         if (valid & (1u << i)) {
@@ -154,23 +162,29 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
           if (qv[i] > tm) {
             tm = qv[i];
             ti = base + 128 * (i >> 2) + 4 * lane + (i & 3);
+            imax = i;
           }
         } else {
           qv[i] = -INFINITY;
         }
       }
       if (valid) {
-        if (tm > m && tm != -INFINITY) {
-          if (s != 0.f) {
-            const float a = ex2((m - tm) * LOG2E);
-            t = a * (t + (m - tm) * s);
-            s = a * s;
+        int skip = -1;  // the element that becomes the running max contributes the implicit 1
+        if (tm > m) {
+          if (m != -INFINITY) {
+            const float a = ex2((m - tm) * LOG2E), S = 1.0f + s;
+            t = a * (t + (m - tm) * S);
+            s = a * S;
+          } else {
+            s = 0.f;
+            t = 0.f;
           }
           m = tm;
+          skip = imax;
         }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          if ((valid & (1u << i)) && qv[i] != -INFINITY) {
+          if ((valid & (1u << i)) && qv[i] != -INFINITY && i != skip) {
             const float d = qv[i] - m;
             const float e = ex2(d * LOG2E);
             s += e;
@@ -270,7 +284,7 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
       parts[item] = acc;
       __threadfence();
       const uint32_t tk = atomicAdd(row_ticket + row, 1u);
-      s_last = ((tk + 1u) % static_cast<uint32_t>(nchunks)) == 0u;
+      s_last = (tk + 1u) == static_cast<uint32_t>(nchunks);
     }
     __syncthreads();
     if (s_last && tid == 0) {
@@ -287,7 +301,7 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
         arg_merge(acc.bq, acc.bqi, a.w, __float_as_int(b.x));
         arg_merge(acc.bg, acc.bgi, b.z, __float_as_int(b.y));
       }
-      if (entropy) entropy[row] = logf(acc.s) - acc.t / acc.s;
+      if (entropy) entropy[row] = log1pf(acc.s) - acc.t / (1.0f + acc.s);
       if (amax) amax[row] = acc.bqi;
       if (samp) samp[row] = acc.bgi;
     }
@@ -401,9 +415,8 @@ extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, f
   if (!aligned(workspace, 256)) return KNX_E_ALIGN;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  // per-row Gumbel bounds and the work counter start from zero every call; the row tickets
-  // are used modulo nchunks (a power of two), so they never need resetting.
-  if (cudaMemsetAsync(ws + o_bound, 0, o_counter + 256 - o_bound, s) != cudaSuccess)
+  // row tickets, per-row Gumbel bounds and the work counter start from zero every call
+  if (cudaMemsetAsync(ws + o_ticket, 0, o_counter + 256 - o_ticket, s) != cudaSuccess)
     return KNX_E_LAUNCH;
   const float rtemp = 1.0f / temperature;
   const int do_div = temperature != 1.0f;

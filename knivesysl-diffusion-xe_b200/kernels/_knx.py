@@ -21,6 +21,18 @@ LIB_PATH = pathlib.Path(os.environ.get("KNX_LIB", PKG / "lib" / "libknx.so"))
 KNX_F16, KNX_BF16, KNX_F32, KNX_I32, KNX_I64 = 0, 1, 2, 3, 4
 KNX_RMS_ROUND_BF16 = 0x1
 KNX_DEV_BAD_EXPERT_ID = 0x1
+KNX_DEV_TIMEOUT = 0x4
+KNX_W4_INT_ZEROS = 0x1
+KNX_W4_WARP_MMA = 0x2
+
+
+def engine_flags(engine=None):
+    """KNX_W4_WARP_MMA when the warp-level mma.sync kernels are requested (engine="mma" or the
+    KNX_ENGINE environment variable); the default engine is tcgen05."""
+    engine = engine or os.environ.get("KNX_ENGINE", "tc")
+    if engine not in ("tc", "mma"):
+        raise ValueError(f"unknown engine {engine!r}")
+    return KNX_W4_WARP_MMA if engine == "mma" else 0
 
 _c = ctypes
 _vp, _i64, _i32, _f32, _sz = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_float, _c.c_size_t
@@ -36,9 +48,11 @@ _SIGS = {
                              _vp, _vp]),
     "knx_moe_w4_workspace_size": (_sz, [_i64, _i64, _i64, _i32, _i32]),
     "knx_moe_w4": (_i32, [_vp, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
-                          _i64, _i64, _i64, _i32, _i32, _i32, _i32, _vp, _sz, _vp, _vp, _vp]),
+                          _i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp, _vp,
+                          _vp]),
     "knx_w4a16_workspace_size": (_sz, [_i64, _i64]),
-    "knx_w4a16_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp, _sz, _vp]),
+    "knx_w4a16_linear": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i32, _i32, _vp, _vp, _sz,
+                                _vp]),
     "knx_sampler_workspace_size": (_sz, [_i64, _i64]),
     "knx_sampler_fused": (_i32, [_vp, _i64, _i64, _f32, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "knx_accept_stop": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp, _i32, _f32,
@@ -122,6 +136,25 @@ def stream_of(device_index):
 def dtype_code(dt):
     return {torch.float16: KNX_F16, torch.bfloat16: KNX_BF16, torch.float32: KNX_F32,
             torch.int32: KNX_I32, torch.int64: KNX_I64}[dt]
+
+
+def zero_flags(*zeros):
+    """KNX_W4_INT_ZEROS when every zero-point tensor holds integers in [0, 15] (quantize_w4's
+    output): the kernels then dequantise bit-identically to dequant_w4.  The check runs once per
+    tensor object and version (one device sync at first use) and is cached on the tensor."""
+    flag = KNX_W4_INT_ZEROS
+    for z in zeros:
+        c = getattr(z, "_knx_zint", None)
+        if c is None or c[0] != z._version:
+            ok = bool(((z == torch.round(z)) & (z >= 0) & (z <= 15)).all())
+            c = (z._version, ok)
+            try:
+                z._knx_zint = c
+            except (AttributeError, RuntimeError):
+                pass
+        if not c[1]:
+            flag = 0
+    return flag
 
 
 _ws = {}

@@ -17,8 +17,8 @@ import os
 
 import torch
 
-from _knx import (KNX_DEV_BAD_EXPERT_ID, check, dtype_code, load, ptr, require_device, stream_of,
-                  workspace)
+from _knx import (KNX_DEV_BAD_EXPERT_ID, KNX_DEV_TIMEOUT, KNX_W4_INT_ZEROS, check, dtype_code, engine_flags, load,
+                  ptr, require_device, stream_of, workspace, zero_flags)
 
 # Tile constants of the sm_100a kernels (reported for parity with the reference's module globals;
 # the kernels do not use BM-padded blocks: tasks are expert token chunks of at most 32).
@@ -94,8 +94,10 @@ def _err_word(dev):
 
 
 def moe_forward(hidden, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, topk_ids, topk_w, hidden_perm=None,
-                out=None):
-    """Raw entry: one MoE layer from explicit buffers (see knx_moe_w4 in include/knx.h)."""
+                out=None, int_zeros=None, engine=None):
+    """Raw entry: one MoE layer from explicit buffers (see knx_moe_w4 in include/knx.h).
+    int_zeros: True/False to state whether the zero-points are integers in [0, 15]; None checks
+    once per tensor (see _knx.zero_flags)."""
     dev = require_device(hidden)
     T, H = hidden.shape
     tk = topk_ids.shape[1]
@@ -112,6 +114,11 @@ def moe_forward(hidden, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, topk_ids, topk_w, hi
     w = topk_w.contiguous()
     if out is None:
         out = torch.empty_like(hidden)
+    if int_zeros is None:
+        flags = zero_flags(gu_z, dn_z)
+    else:
+        flags = KNX_W4_INT_ZEROS if int_zeros else 0
+    flags |= engine_flags(engine)
     lib = load()
     nbytes = lib.knx_moe_w4_workspace_size(T, H, I, E, tk)
     ws = workspace(dev, nbytes, "moe")
@@ -119,10 +126,12 @@ def moe_forward(hidden, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, topk_ids, topk_w, hi
     check(lib.knx_moe_w4(ptr(hidden), ptr(hidden_perm), dtype_code(hidden.dtype), ptr(ids),
                          dtype_code(ids.dtype), ptr(w), dtype_code(w.dtype), ptr(gu_q), ptr(gu_s),
                          ptr(gu_z), ptr(dn_q), ptr(dn_s), ptr(dn_z), T, H, I, E, tk, gs_gu, gs_dn,
-                         ptr(ws), ws.numel(), ptr(out), ptr(err), stream_of(dev)), "knx_moe_w4")
+                         flags, ptr(ws), ws.numel(), ptr(out), ptr(err), stream_of(dev)),
+          "knx_moe_w4")
     if err is not None:
         bad = int(err.item())
         assert not (bad & KNX_DEV_BAD_EXPERT_ID), f"moe: expert ids must be in [0,{E}]"
+        assert not (bad & KNX_DEV_TIMEOUT), "moe: a bounded on-chip wait timed out"
     return out
 
 

@@ -12,7 +12,8 @@ two nibbles per byte, the even k in the low nibble.
 """
 import torch
 
-from _knx import (check, dtype_code, load, ptr, require_device, stream_of, workspace)
+from _knx import (KNX_W4_INT_ZEROS, check, engine_flags, load, ptr, require_device, stream_of,
+                  workspace, zero_flags)
 
 GS = 128  # default group size along K
 
@@ -25,7 +26,9 @@ def quantize_w4(W, group_size=GS):
     Wg = W.float().reshape(N, K // group_size, group_size)
     lo = Wg.amin(-1)
     hi = Wg.amax(-1)
-    scale = (hi - lo).clamp(min=1e-8) / 15.0
+    # tensor divisors keep the division IEEE-exact on every device (a CUDA tensor divided by a
+    # Python scalar is a multiply by the reciprocal), so CPU and GPU packs are bit-identical
+    scale = (hi - lo).clamp(min=1e-8) / torch.full_like(hi, 15.0)
     zero = torch.round(-lo / scale).clamp(0, 15)
     q = torch.round(Wg / scale[..., None] + zero[..., None]).clamp(0, 15).to(torch.uint8)
     q = q.reshape(N, K)
@@ -44,11 +47,12 @@ def dequant_w4(qpacked, scale, zero, group_size=GS):
     return W.reshape(N, K).to(torch.float16)
 
 
-def w4a16_linear(X, qpacked, scale, zero, BK=GS):
+def w4a16_linear(X, qpacked, scale, zero, BK=GS, int_zeros=None, engine=None):
     """Y[M,N] = X[M,K] @ dequant(qpacked)[N,K].T, fp16 out; reads the packed nibbles directly.
 
     BK is the group size (the reference ties its K tile to it).  Requirements: K % 64 == 0,
-    BK % 32 == 0, K % BK == 0, N % 8 == 0, K / BK <= 64."""
+    BK % 32 == 0, K % BK == 0, N % 8 == 0, K / BK <= 56.  Integer zero-points (quantize_w4's)
+    dequantise exactly like dequant_w4; other fp16 zero-points as RN16(RN16(q - z) * s)."""
     M, K = X.shape
     N = qpacked.shape[0]
     assert K % BK == 0, "K must be divisible by BK (== group size)"
@@ -58,9 +62,14 @@ def w4a16_linear(X, qpacked, scale, zero, BK=GS):
     s = scale.contiguous().to(torch.float16)
     z = zero.contiguous().to(torch.float16)
     Y = torch.empty(M, N, device=X.device, dtype=torch.float16)
+    if int_zeros is None:
+        flags = zero_flags(z)
+    else:
+        flags = KNX_W4_INT_ZEROS if int_zeros else 0
+    flags |= engine_flags(engine)
     lib = load()
     nbytes = lib.knx_w4a16_workspace_size(M, K)
     ws = workspace(dev, nbytes, "w4a16")
-    check(lib.knx_w4a16_linear(ptr(Xc), ptr(q), ptr(s), ptr(z), M, N, K, int(BK), ptr(Y), ptr(ws),
-                               ws.numel(), stream_of(dev)), "knx_w4a16_linear")
+    check(lib.knx_w4a16_linear(ptr(Xc), ptr(q), ptr(s), ptr(z), M, N, K, int(BK), flags, ptr(Y),
+                               ptr(ws), ws.numel(), stream_of(dev)), "knx_w4a16_linear")
     return Y

@@ -190,8 +190,9 @@ def router_topk(x, wr, bias, topk, logits=None):
 
 
 # ---------------------------------------------------------------------------------- sampler
-def entropy(logits):
-    return torch.distributions.Categorical(logits=logits.float()).entropy()
+def entropy(logits, dtype=torch.float32):
+    """torch Categorical entropy (fast_sampler.py:29); dtype=float64 gives the accurate value."""
+    return torch.distributions.Categorical(logits=logits.to(dtype)).entropy()
 
 
 def gumbel_argmax(logits, seed, temperature=1.0, nthreads=8):

@@ -50,7 +50,7 @@ def test_workspace_sizes_are_host_only_and_monotone():
 def test_moe_contract_violations_rejected_on_host(H, I, gs_gu, gs_dn, expect):
     lib = _knx.load()
     st = lib.knx_moe_w4(None, None, 0, None, 4, None, 2, None, None, None, None, None, None,
-                        256, H, I, 128, 8, gs_gu, gs_dn, None, 0, None, None, None)
+                        256, H, I, 128, 8, gs_gu, gs_dn, 0, None, 0, None, None, None)
     assert st == expect
 
 
