@@ -3,19 +3,19 @@
 // Same contract as the warp-MMA kernels in knx_moe.cu (gate_up+GELU into out2, down into out3,
 // dense rows GEMM), different engine.  One persistent CTA per SM, warp-specialised:
 //
-//   warp 12      scheduler + weight producer: pulls (task, slice) work items from the counter,
+//   warp 20      scheduler + weight producer: pulls (task, slice) work items from the counter,
 //                publishes them in a 2-slot item ring (with the slice's scale/zero rows fetched by
 //                1-D bulk copies), then streams the slice's packed nibbles with 2-D TMA loads
 //                (64 B x rows boxes, 64-byte swizzle) into an 8-stage ring, 128 k per stage.
-//   warp 13      activation producer: gathers the task's token rows (K-interleaved f16) with
+//   warp 21      activation producer: gathers the task's token rows (K-interleaved f16) with
 //                cp.async straight into the UMMA 128-byte-swizzle K-major layout, 4-stage ring.
-//   warps 0-7    dequant: thread = one weight row (= one TMEM lane); warps w and w+4 split each
-//                stage's 128 k.  Nibbles -> f16 pairs in registers (dequant8), tcgen05.st into a
+//   warps 0-15   dequant: thread = one weight row (= one TMEM lane); warps w, w+4, w+8, w+12
+//                split each stage's 128 k in quarters.  Nibbles -> f16 pairs in registers (dequant8), tcgen05.st into a
 //                TMEM A buffer (4 x 64 columns).
-//   warp 14      MMA issuer (one thread): tcgen05.mma kind::f16, A from TMEM, B from shared memory
+//   warp 22      MMA issuer (one thread): tcgen05.mma kind::f16, A from TMEM, B from shared memory
 //                via a descriptor, D (fp32, 128 lanes x N tokens) in TMEM, double-buffered across
 //                work items; tcgen05.commit releases A buffers, activation stages and D.
-//   warps 8-11   epilogue: tcgen05.ld of D, tanh-GELU(gate) * up (gated) or plain f16 cast,
+//   warps 16-19  epilogue: tcgen05.ld of D, tanh-GELU(gate) * up (gated) or plain f16 cast,
 //                transposed through shared memory, coalesced row stores.
 //
 // The MMA is D[128 x N] += A[128 x 16] . B[N x 16]^T per k16 step, M = weight rows (64 gate + 64
@@ -45,11 +45,13 @@ constexpr int A_STAGE = 2 * A_KBLK;       // 16 KB
 constexpr int A_COL0 = 0;                 // TMEM columns [0, 256): A buffers, 64 columns each
 constexpr int D_COL0 = NA * 64;           // TMEM columns [256, 256 + 2*N_MAX): D buffers
 constexpr int TMEM_COLS = 512;
-constexpr int NUM_WARPS = 15;
+constexpr int DQ_WARPS = 16;              // 4 per SM sub-partition; warp w: lanes 32*(w%4), k quarter w/4
+constexpr int NUM_WARPS = DQ_WARPS + 4 + 3;
 constexpr int NTHREADS = NUM_WARPS * 32;
-constexpr int WARP_WPROD = 12, WARP_APROD = 13, WARP_MMA = 14, WARP_EPI0 = 8;
-constexpr int ITEM_CONSUMERS = 8 + 1 + 1 + 4;  // dequant warps, act producer, MMA, epilogue warps
-constexpr int SZ_MAX = 56;
+constexpr int WARP_EPI0 = DQ_WARPS;       // warps 16-19: epilogue (lane quadrant = warp % 4)
+constexpr int WARP_WPROD = DQ_WARPS + 4, WARP_APROD = DQ_WARPS + 5, WARP_MMA = DQ_WARPS + 6;
+constexpr int ITEM_CONSUMERS = DQ_WARPS + 1 + 1 + 4;  // dequant, act producer, MMA, epilogue warps
+constexpr int SZ_MAX = 40;                // scale/zero groups per row on this path
 
 struct Item {
   int valid, e, cnt, slice;
@@ -96,7 +98,7 @@ constexpr int OFF_A = 0;
 constexpr int OFF_W = OFF_A + SA * A_STAGE;
 constexpr int OFF_SZ = OFF_W + SW * W_STAGE;
 KNX_HOST_DEVINL size_t sz_slot_bytes(int ng) { return (static_cast<size_t>(512) * ng + 1023) & ~size_t(1023); }
-constexpr int EPI_BYTES = 64 * N_MAX * 4 + N_MAX * (ROWS + 8) * 2;  // up exchange + out tile
+constexpr int EPI_BYTES = 2 * 64 * N_MAX * 4 + N_MAX * (ROWS + 8) * 2;  // gate/up exchange + out tile
 inline size_t smem_bytes(int ng) {
   return 1024 + OFF_SZ + IR * sz_slot_bytes(ng) + EPI_BYTES;
 }
@@ -125,9 +127,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int nst = (p.K + BK - 1) / BK;
 
   if (tid == 0) {
-    for (int s = 0; s < SW; ++s) { mbar_init(&ctrl.w_full[s], 1); mbar_init(&ctrl.w_empty[s], 8); }
+    for (int s = 0; s < SW; ++s) { mbar_init(&ctrl.w_full[s], 1); mbar_init(&ctrl.w_empty[s], DQ_WARPS); }
     for (int s = 0; s < SA; ++s) { mbar_init(&ctrl.a_full[s], 32); mbar_init(&ctrl.a_empty[s], 1); }
-    for (int b = 0; b < NA; ++b) { mbar_init(&ctrl.t_full[b], 8); mbar_init(&ctrl.t_empty[b], 1); }
+    for (int b = 0; b < NA; ++b) { mbar_init(&ctrl.t_full[b], DQ_WARPS); mbar_init(&ctrl.t_empty[b], 1); }
     for (int d = 0; d < 2; ++d) { mbar_init(&ctrl.d_full[d], 1); mbar_init(&ctrl.d_empty[d], 4); }
     for (int i = 0; i < IR; ++i) {
       mbar_init(&ctrl.i_full[i], 1);
@@ -151,9 +153,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     *abort_flag = 1;
     if (p.err) atomicOr(p.err, KNX_DEV_TIMEOUT);
   };
-  auto wait = [&](uint64_t* bar, uint32_t parity) -> bool {
+  // bounded mbarrier wait; `backoff_ns` > 0 sleeps between polls (roles that wait long and
+  // would otherwise take issue slots from the dequant warps)
+  auto wait = [&](uint64_t* bar, uint32_t parity, uint32_t backoff_ns = 0) -> bool {
     if (*abort_flag) return false;
-    if (!mbar_wait(bar, parity)) {
+    if (!mbar_wait(bar, parity, 2000000000ull, backoff_ns)) {
       fail();
       return false;
     }
@@ -240,34 +244,39 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) mbar_arrive(&ctrl.i_empty[slot]);
         break;
       }
-      int64_t r_lo = 0, r_hi = 0;  // activation rows of tokens `lane` and `lane + 32`
+      // lane l copies the rows of tokens l and l + 32 (16-byte chunks straight into the swizzled
+      // K-major layout: row t, chunk j -> block j/8, row group t/8, chunk (j%8) ^ (t%8))
+      const __half* src0 = nullptr;
+      const __half* src1 = nullptr;
       if (lane < it.cnt)
-        r_lo = p.sorted_pair ? p.sorted_pair[it.slot0 + lane] / p.topk : it.slot0 + lane;
+        src0 = p.act + (p.sorted_pair ? p.sorted_pair[it.slot0 + lane] / p.topk
+                                      : static_cast<int64_t>(it.slot0 + lane)) * p.act_stride;
       if (lane + 32 < it.cnt)
-        r_hi = p.sorted_pair ? p.sorted_pair[it.slot0 + lane + 32] / p.topk : it.slot0 + lane + 32;
+        src1 = p.act + (p.sorted_pair ? p.sorted_pair[it.slot0 + lane + 32] / p.topk
+                                      : static_cast<int64_t>(it.slot0 + lane + 32)) * p.act_stride;
+      const uint32_t dst_row0 = (lane >> 3) * 1024 + (lane & 7) * 128;
+      const uint32_t dst_row1 = ((lane + 32) >> 3) * 1024 + (lane & 7) * 128;
       bool ok = true;
       for (int st = 0; st < nst; ++st, ++ast) {
         const int s = ast % SA;
-        if (!wait(&ctrl.a_empty[s], ((ast / SA) & 1) ^ 1)) {
+        if (!wait(&ctrl.a_empty[s], ((ast / SA) & 1) ^ 1, 32)) {
           ok = false;
           break;
         }
         uint8_t* dst = a_ring + s * A_STAGE;
         const int k0 = st * BK;
-        const int kch = min(BK, p.K - k0) >> 3;  // 16-byte chunks per row this stage
-        const int total = it.cnt * kch;
-        for (int b = 0; b < total; b += 32) {
-          const int idx = b + lane;
-          const int t = idx / kch, j = idx - t * kch;
-          const int64_t lo = __shfl_sync(0xffffffffu, r_lo, t & 31);
-          const int64_t hi = __shfl_sync(0xffffffffu, r_hi, t & 31);
-          if (idx < total) {
-            const int64_t row = t < 32 ? lo : hi;
-            const __half* src = p.act + row * p.act_stride + k0 + j * 8;
-            uint8_t* d = dst + (j >> 3) * A_KBLK + (t >> 3) * 1024 + (t & 7) * 128 +
-                         (((j & 7) ^ (t & 7)) << 4);
-            cp_async16(d, src);
-          }
+        const int kch = min(BK, p.K - k0) >> 3;  // 16-byte chunks per row this stage (16 or 8)
+        if (src0) {
+#pragma unroll 4
+          for (int j = 0; j < kch; ++j)
+            cp_async16(dst + (j >> 3) * A_KBLK + dst_row0 + (((j & 7) ^ (lane & 7)) << 4),
+                       src0 + k0 + j * 8);
+        }
+        if (src1) {
+#pragma unroll 4
+          for (int j = 0; j < kch; ++j)
+            cp_async16(dst + (j >> 3) * A_KBLK + dst_row1 + (((j & 7) ^ (lane & 7)) << 4),
+                       src1 + k0 + j * 8);
         }
         cp_async_mbar_arrive_noinc(&ctrl.a_full[s]);
       }
@@ -275,9 +284,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!ok) break;
       if (lane == 0) mbar_arrive(&ctrl.i_empty[slot]);
     }
-  } else if (warp < 8) {
+  } else if (warp < DQ_WARPS) {
     // ---------------------------------------------------------------- dequant -> TMEM
-    const int q = warp & 3, kh = warp >> 2;
+    const int q = warp & 3, kq = warp >> 2;  // lane quadrant, k quarter (32 k) of the stage
     const int row = 32 * q + lane;
     uint32_t wst = 0, tb = 0;
     for (int n = 0;; ++n) {
@@ -301,6 +310,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         zrow = szs + 128 * ng + row * ng;
       }
       const bool row_ok = row < it.nvalid;
+      const int sw = (row >> 1) & 3;
       bool ok = true;
       for (int st = 0; st < nst; ++st, ++wst, ++tb) {
         const int ws = wst % SW, b = tb % NA;
@@ -308,38 +318,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ok = false;
           break;
         }
-        const int k0 = st * BK + kh * 64;
+        const int k0 = st * BK + kq * 32;
         if (k0 < p.K) {
-          uint32_t v[32];
+          uint32_t v[16];
           if (row_ok) {
             const int grp = k0 / p.gs;
             const uint2 c = make_sz<ZINT>(srow[grp], zrow[grp]);
             const __half2 s2 = __low2half2(u32_as_h2(c.x)), cc = __high2half2(u32_as_h2(c.x));
             const __half2 s16 = __low2half2(u32_as_h2(c.y)), c16 = __high2half2(u32_as_h2(c.y));
-            const uint32_t wrow = smem_u32(w_ring + ws * W_STAGE + row * WROW);
-            const int sw = (row >> 1) & 3;
-            const uint4 u0 = lds128(wrow + (((2 * kh) ^ sw) << 4));
-            const uint4 u1 = lds128(wrow + (((2 * kh + 1) ^ sw) << 4));
-            const uint32_t uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+            const uint4 u = lds128(smem_u32(w_ring + ws * W_STAGE + row * WROW) + ((kq ^ sw) << 4));
+            const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
+            for (int i = 0; i < 4; ++i) {
               uint32_t w4[4];
               dequant8<ZINT>(uu[i], s2, s16, cc, c16, w4);
               v[4 * i] = w4[0]; v[4 * i + 1] = w4[1]; v[4 * i + 2] = w4[2]; v[4 * i + 3] = w4[3];
             }
           } else {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = 0u;
+            for (int i = 0; i < 16; ++i) v[i] = 0u;
           }
-          tmem_st32(tmem + ((32u * q) << 16) + A_COL0 + b * 64 + kh * 32, v);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctrl.w_empty[ws]);  // weights of this stage consumed
+          tmem_st16(tmem + ((32u * q) << 16) + A_COL0 + b * 64 + kq * 16, v);
           tmem_wait_st();
+        } else {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctrl.w_empty[ws]);
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&ctrl.w_empty[ws]);
-          mbar_arrive(&ctrl.t_full[b]);
-        }
+        if (lane == 0) mbar_arrive(&ctrl.t_full[b]);
       }
       if (!ok) break;
       __syncwarp();
@@ -395,8 +404,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int q = warp & 3;
     const int row = 32 * q + lane;
     const int et = tid - WARP_EPI0 * 32;  // 0..127
-    float* xup = reinterpret_cast<float*>(epi);                          // [N_MAX][64] fp32
-    __half* otile = reinterpret_cast<__half*>(epi + 64 * N_MAX * 4);     // [N_MAX][ROWS + 8]
+    float* xgate = reinterpret_cast<float*>(epi);                        // [N_MAX][64] fp32
+    float* xup = xgate + 64 * N_MAX;                                     // [N_MAX][64] fp32
+    __half* otile = reinterpret_cast<__half*>(epi + 2 * 64 * N_MAX * 4); // [N_MAX][ROWS + 8]
     constexpr int OT = ROWS + 8;
     uint32_t dc = 0;
     // The four epilogue warps meet at named barriers, which have no timeout; so after every
@@ -411,7 +421,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     };
     for (int n = 0;; ++n) {
       const int slot = n % IR;
-      if (!agree(wait(&ctrl.i_full[slot], (n / IR) & 1))) break;
+      if (!agree(wait(&ctrl.i_full[slot], (n / IR) & 1, 256))) break;
       const Item it = ctrl.items[slot];
       if (!it.valid) {
         __syncwarp();
@@ -419,35 +429,33 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         break;
       }
       const int db = dc & 1;
-      if (!agree(wait(&ctrl.d_full[db], (dc >> 1) & 1))) break;
+      if (!agree(wait(&ctrl.d_full[db], (dc >> 1) & 1, 128))) break;
       tc_fence_after();
-      float acc[N_MAX];
+      // D (128 rows x npad tokens, fp32) -> shared memory, 16 columns at a time
+#pragma unroll 1
+      for (int c = 0; c < it.npad / 16; ++c) {
+        uint32_t v[16];
+        tmem_ld16(tmem + ((32u * q) << 16) + D_COL0 + db * N_MAX + c * 16, v);
+        tmem_wait_ld();
+        if (GATED) {
+          float* xb = row < 64 ? xgate : xup;  // [N_MAX][64] fp32, token-major
 #pragma unroll
-      for (int c = 0; c < N_MAX / 16; ++c) {
-        if (c * 16 < it.npad) {
-          uint32_t v[16];
-          tmem_ld16(tmem + ((32u * q) << 16) + D_COL0 + db * N_MAX + c * 16, v);
-          tmem_wait_ld();
+          for (int i = 0; i < 16; ++i) xb[(c * 16 + i) * 64 + (row & 63)] = __uint_as_float(v[i]);
+        } else {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[c * 16 + i] = __uint_as_float(v[i]);
+          for (int i = 0; i < 16; ++i) otile[(c * 16 + i) * OT + row] = __float2half_rn(__uint_as_float(v[i]));
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctrl.d_empty[db]);
       ++dc;
+      named_bar(1, 128);
       if (GATED) {
-        if (q >= 2) {
-#pragma unroll
-          for (int t = 0; t < N_MAX; ++t)
-            if (t < it.cnt) xup[t * 64 + (row - 64)] = acc[t];
-        }
-        named_bar(1, 128);
-        if (q < 2) {
-#pragma unroll
-          for (int t = 0; t < N_MAX; ++t)
-            if (t < it.cnt)
-              otile[t * OT + perm_pos(row)] = __float2half_rn(gelu_tanh(acc[t]) * xup[t * 64 + row]);
+        for (int i = et; i < it.cnt * 64; i += 128) {
+          const int t = i >> 6, nn = i & 63;
+          otile[t * OT + perm_pos(nn)] =
+              __float2half_rn(gelu_tanh(xgate[t * 64 + nn]) * xup[t * 64 + nn]);
         }
         named_bar(1, 128);
         for (int c = et; c < it.cnt * 8; c += 128) {
@@ -456,12 +464,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                     it.slice * 64 + ch * 8) =
               *reinterpret_cast<const uint4*>(otile + t * OT + ch * 8);
         }
-        named_bar(1, 128);
       } else {
-#pragma unroll
-        for (int t = 0; t < N_MAX; ++t)
-          if (t < it.cnt) otile[t * OT + row] = __float2half_rn(acc[t]);
-        named_bar(1, 128);
         const int vch = it.nvalid >> 3;
         for (int c = et; c < it.cnt * vch; c += 128) {
           const int t = c / vch, ch = c - t * vch;
@@ -469,8 +472,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                     it.slice * ROWS + ch * 8) =
               *reinterpret_cast<const uint4*>(otile + t * OT + ch * 8);
         }
-        named_bar(1, 128);
       }
+      named_bar(1, 128);
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctrl.i_empty[slot]);
     }

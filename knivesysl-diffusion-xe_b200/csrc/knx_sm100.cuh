@@ -54,10 +54,12 @@ KNX_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Wait for the phase with the given parity to complete.  Gives up after `limit_ns` (returns false)
 // so that a protocol error can never hang the GPU; the caller then aborts the kernel cleanly.
-KNX_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull) {
+KNX_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns = 2000000000ull,
+                          uint32_t backoff_ns = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (!mbar_try_wait(bar, parity)) {
+    if (backoff_ns) __nanosleep(backoff_ns);
     if (globaltimer() - t0 > limit_ns) return false;
   }
   return true;
@@ -128,6 +130,15 @@ KNX_DEVINL void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
       "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
       "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
       "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+KNX_DEVINL void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
+      "%11, %12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15])
       : "memory");
 }
 // Each thread loads 16 consecutive 32-bit columns of its own lane.
