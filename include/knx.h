@@ -57,6 +57,7 @@ extern "C" {
 /* weight-format / engine flags */
 #define KNX_W4_INT_ZEROS 0x1 /* all zero-points are integers in [0, 15] */
 #define KNX_W4_WARP_MMA 0x2  /* use the warp-level mma.sync kernels instead of tcgen05 (A/B runs) */
+#define KNX_W4_WARP_WS 0x8   /* use the warp-specialised mma.sync kernels (TMA-fed, 16 math warps) */
 
 KNX_API int knx_version(void);
 /* 1 when the current device is a compute-capability 10.0 part (the only target). */

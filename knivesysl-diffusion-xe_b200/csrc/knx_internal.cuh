@@ -29,6 +29,19 @@ int launch_tc_rows(const __half* act, int64_t act_stride, int K, const int32_t* 
                    int gs, bool zint, __half* out, int64_t out_stride, int64_t max_tasks,
                    int32_t* err, cudaStream_t s);
 
+// warp-specialised mma.sync grouped W4A16 GEMMs (knx_moe_hw.cu), 32 tokens per task
+constexpr int HW_TASK_TOKENS = 32;
+bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated);
+int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, const int32_t* offsets,
+                     const int4* tasks, const int32_t* ntasks, int* counter, const uint8_t* gu_q,
+                     const __half* gu_s, const __half* gu_z, int E, int H, int I, int ng, int gs,
+                     bool zint, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s);
+int launch_hw_rows(const __half* act, int64_t act_stride, int K, const int32_t* offsets,
+                   const int4* tasks, const int32_t* ntasks, int dense_rows, int* counter,
+                   const uint8_t* wq, const __half* ws, const __half* wz, int E, int N, int ng,
+                   int gs, bool zint, __half* out, int64_t out_stride, int64_t max_tasks,
+                   int32_t* err, cudaStream_t s);
+
 namespace prof {
 int begin_call();                                  // -1 when stage recording is off
 void mark(int call, int slot, cudaStream_t stream);  // record boundary `slot` of call `call`

@@ -571,10 +571,13 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
     if (st != KNX_OK) return st;
     xp = w.xp;
   }
-  const bool use_tc = !(flags & KNX_W4_WARP_MMA) &&
+  const bool use_ws = !(flags & KNX_W4_WARP_MMA) && (flags & KNX_W4_WARP_WS) &&
+                      hw_supported(H, gs_gu, ng1, 2 * I, true) &&
+                      hw_supported(I, gs_dn, ng2, H, false);
+  const bool use_tc = !use_ws && !(flags & (KNX_W4_WARP_MMA | KNX_W4_WARP_WS)) &&
                       tc_supported(H, gs_gu, ng1, 2 * I, true) &&
                       tc_supported(I, gs_dn, ng2, H, false);
-  const int task_tokens = use_tc ? TC_TASK_TOKENS : M_MAX;
+  const int task_tokens = use_tc ? TC_TASK_TOKENS : use_ws ? HW_TASK_TOKENS : M_MAX;
   st = launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0, task_tokens, w.counts,
                     w.offsets, w.sorted_pair, w.inv, nullptr, nullptr, nullptr, w.tasks, w.ntasks,
                     w.counters, 2, err, s);
@@ -591,6 +594,18 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
     if (st != KNX_OK) return st;
     prof::mark(pc, 2, s);
     st = launch_tc_rows(w.out2, I, static_cast<int>(I), w.offsets, w.tasks, w.ntasks, 0,
+                        w.counters + 1, dn_q, static_cast<const __half*>(dn_s),
+                        static_cast<const __half*>(dn_z), E, static_cast<int>(H), ng2, gs_dn, zint,
+                        w.out3, H, max_tasks, err, s);
+    if (st != KNX_OK) return st;
+  } else if (use_ws) {
+    st = launch_hw_gateup(xp, w.sorted_pair, topk, w.offsets, w.tasks, w.ntasks, w.counters, gu_q,
+                          static_cast<const __half*>(gu_s), static_cast<const __half*>(gu_z), E,
+                          static_cast<int>(H), static_cast<int>(I), ng1, gs_gu, zint, w.out2,
+                          max_tasks, err, s);
+    if (st != KNX_OK) return st;
+    prof::mark(pc, 2, s);
+    st = launch_hw_rows(w.out2, I, static_cast<int>(I), w.offsets, w.tasks, w.ntasks, 0,
                         w.counters + 1, dn_q, static_cast<const __half*>(dn_s),
                         static_cast<const __half*>(dn_z), E, static_cast<int>(H), ng2, gs_dn, zint,
                         w.out3, H, max_tasks, err, s);
@@ -664,7 +679,16 @@ extern "C" int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, 
   int rc = launch_permute(X, KNX_F16, xp, M * K, st);
   if (rc != KNX_OK) return rc;
   const bool zint = (flags & KNX_W4_INT_ZEROS) != 0;
-  if (!(flags & KNX_W4_WARP_MMA) && tc_supported(K, gs, ng, N, false)) {
+  if (!(flags & KNX_W4_WARP_MMA) && (flags & KNX_W4_WARP_WS) && hw_supported(K, gs, ng, N, false)) {
+    int* counter = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + up256(size_t(M) * K * 2));
+    if (cudaMemsetAsync(counter, 0, sizeof(int), st) != cudaSuccess) return KNX_E_LAUNCH;
+    return launch_hw_rows(xp, K, static_cast<int>(K), nullptr, nullptr, nullptr,
+                          static_cast<int>(M), counter, q, static_cast<const __half*>(s),
+                          static_cast<const __half*>(z), 1, static_cast<int>(N), ng, gs, zint,
+                          static_cast<__half*>(Y), N, (M + HW_TASK_TOKENS - 1) / HW_TASK_TOKENS,
+                          nullptr, st);
+  }
+  if (!(flags & (KNX_W4_WARP_MMA | KNX_W4_WARP_WS)) && tc_supported(K, gs, ng, N, false)) {
     int* counter = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + up256(size_t(M) * K * 2));
     if (cudaMemsetAsync(counter, 0, sizeof(int), st) != cudaSuccess) return KNX_E_LAUNCH;
     return launch_tc_rows(xp, K, static_cast<int>(K), nullptr, nullptr, nullptr,

@@ -24,15 +24,18 @@ KNX_DEV_BAD_EXPERT_ID = 0x1
 KNX_DEV_TIMEOUT = 0x4
 KNX_W4_INT_ZEROS = 0x1
 KNX_W4_WARP_MMA = 0x2
+KNX_W4_WARP_WS = 0x8
+_ENGINES = {"tc": 0, "mma": KNX_W4_WARP_MMA, "ws": KNX_W4_WARP_WS}
 
 
 def engine_flags(engine=None):
-    """KNX_W4_WARP_MMA when the warp-level mma.sync kernels are requested (engine="mma" or the
-    KNX_ENGINE environment variable); the default engine is tcgen05."""
+    """Engine selection flags for the W4A16 GEMMs: "tc" (tcgen05, the default), "ws" (the
+    warp-specialised mma.sync kernels) or "mma" (the plain mma.sync kernels); `engine` or the
+    KNX_ENGINE environment variable chooses."""
     engine = engine or os.environ.get("KNX_ENGINE", "tc")
-    if engine not in ("tc", "mma"):
+    if engine not in _ENGINES:
         raise ValueError(f"unknown engine {engine!r}")
-    return KNX_W4_WARP_MMA if engine == "mma" else 0
+    return _ENGINES[engine]
 
 _c = ctypes
 _vp, _i64, _i32, _f32, _sz = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_float, _c.c_size_t

@@ -105,7 +105,7 @@ def _moe_case(T, E, H, I, tk, seed, skew=None):
     return W, hidden, ids, w
 
 
-@pytest.mark.parametrize("engine", ["tc", "mma"])
+@pytest.mark.parametrize("engine", ["tc", "ws", "mma"])
 @pytest.mark.parametrize("T,E,H,I,tk,skew", [
     (256, 128, 2816, 704, 8, None),       # configs[0] shapes
     (1, 128, 2816, 704, 8, None), (7, 16, 512, 128, 4, None), (33, 8, 256, 64, 2, "one"),
@@ -127,12 +127,13 @@ def test_moe_engines_agree_and_are_deterministic(cuda):
     Wd = _to(W, cuda)
     args = (Wd["gu_q"], Wd["gu_s"], Wd["gu_z"], Wd["dn_q"], Wd["dn_s"], Wd["dn_z"])
     ys = {}
-    for eng in ("tc", "mma"):
+    for eng in ("tc", "ws", "mma"):
         a = fused_moe_w4_v2.moe_forward(hidden.to(cuda), *args, ids.to(cuda), w.to(cuda), engine=eng)
         b = fused_moe_w4_v2.moe_forward(hidden.to(cuda), *args, ids.to(cuda), w.to(cuda), engine=eng)
         assert torch.equal(a.view(torch.int16), b.view(torch.int16)), eng
         ys[eng] = a
     assert_close_fp16(ys["tc"], ys["mma"], what="tc vs mma")
+    assert_close_fp16(ys["ws"], ys["mma"], what="ws vs mma")
 
 
 def test_moe_integer_zeros_exact_dequant(cuda):
@@ -150,7 +151,7 @@ def test_moe_integer_zeros_exact_dequant(cuda):
     hidden = (torch.randn(T, H, generator=g) * 0.5).half()
     ids, w = workloads.random_routing(T, E, tk, seed=5)
     want = ref.moe_layer(hidden, *packs["gu"], *packs["dn"], ids, w)
-    for eng in ("tc", "mma"):
+    for eng in ("tc", "ws", "mma"):
         y = fused_moe_w4_v2.moe_forward(hidden.to(cuda), *[t.to(cuda) for t in packs["gu"]],
                                         *[t.to(cuda) for t in packs["dn"]], ids.to(cuda),
                                         w.to(cuda), engine=eng)
@@ -212,7 +213,7 @@ def test_w4a16_linear_vs_reference_golden(cuda, tag):
     assert_close_fp16(Y, torch.from_numpy(gd[f"{tag}_Y"]), what=tag)
 
 
-@pytest.mark.parametrize("engine", ["tc", "mma"])
+@pytest.mark.parametrize("engine", ["tc", "ws", "mma"])
 @pytest.mark.parametrize("N,K,M", [(2816, 2816, 256), (1408, 2816, 64), (2816, 704, 64),
                                    (4096, 2816, 256), (200, 256, 3), (1408, 2816, 130)])
 def test_w4a16_linear_killtest_shapes(cuda, N, K, M, engine):
