@@ -5,8 +5,9 @@
  * Every entry point takes plain device pointers, element counts and a CUDA stream handle
  * (`cudaStream_t` passed as `void*`; NULL = legacy default stream). Nothing here allocates
  * device memory: callers pass outputs and, where a function needs scratch space, a workspace
- * whose size the matching `*_workspace_size` function reports. Every call is stream-ordered,
- * never synchronises the host and is safe to capture in a CUDA graph.
+ * whose size the matching `*_workspace_size` function reports (knx_sampler_fused_static keeps
+ * its scratch inside the library instead). Every call is stream-ordered and never synchronises
+ * the host.
  *
  * Return value: KNX_OK (0) or a negative KNX_E* status for host-detectable contract violations
  * (bad sizes, misaligned pointers, launch failures). Data-dependent problems found on the
@@ -157,6 +158,24 @@ KNX_API size_t knx_sampler_workspace_size(int64_t rows, int64_t V);
 KNX_API int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, float temperature,
                       int64_t seed, float* entropy, int64_t* samp, int64_t* amax,
                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* knx_sampler_fused without a workspace argument, for callers that cannot allocate device memory
+ * when they sample (FFI hosts without a CUDA allocator, serving loops whose device memory is
+ * frozen after warm-up).  No counterpart in the reference: its sampler allocates its outputs and
+ * temporaries through torch on every call.  Same outputs as knx_sampler_fused.
+ * Scratch is a fixed KNX_SAMPLER_STATIC_SCRATCH_BYTES array inside the library, one per device:
+ *   - calls needing more (knx_sampler_workspace_size(rows, V) > the limit; more than 3,969 rows
+ *     at V = 262144) return KNX_E_WORKSPACE without launching anything;
+ *   - the first call on a device looks the array up (cudaGetSymbolAddress with that device
+ *     current); make it before any stream capture begins;
+ *   - tickets/bounds/counter are zeroed in stream order by every call;
+ *   - calls that can overlap in time on one device (other streams, unordered host threads) race
+ *     on the shared scratch; calls in order on one stream are safe.
+ * Allocates nothing (no cudaMalloc/cudaFree, no allocating library). */
+#define KNX_SAMPLER_STATIC_SCRATCH_BYTES (1u << 20)
+KNX_API int knx_sampler_fused_static(const float* logits, int64_t rows, int64_t V,
+                                     float temperature, int64_t seed, float* entropy,
+                                     int64_t* samp, int64_t* amax, void* stream);
 
 /* Entropy-bound acceptance and the stable-and-confident stop test, one launch per batch.
  * Replaces _accept_canvas (fast_sampler.py:32-42) and _stop_call (fast_sampler.py:45-65).

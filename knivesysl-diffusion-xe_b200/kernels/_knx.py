@@ -22,6 +22,7 @@ KNX_F16, KNX_BF16, KNX_F32, KNX_I32, KNX_I64 = 0, 1, 2, 3, 4
 KNX_RMS_ROUND_BF16 = 0x1
 KNX_DEV_BAD_EXPERT_ID = 0x1
 KNX_DEV_TIMEOUT = 0x4
+KNX_SAMPLER_STATIC_SCRATCH_BYTES = 1 << 20  # include/knx.h
 KNX_W4_INT_ZEROS = 0x1
 KNX_W4_WARP_MMA = 0x2
 KNX_W4_WARP_WS = 0x8
@@ -58,6 +59,7 @@ _SIGS = {
                                 _vp]),
     "knx_sampler_workspace_size": (_sz, [_i64, _i64]),
     "knx_sampler_fused": (_i32, [_vp, _i64, _i64, _f32, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "knx_sampler_fused_static": (_i32, [_vp, _i64, _i64, _f32, _i64, _vp, _vp, _vp, _vp]),
     "knx_accept_stop": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp, _i32, _f32,
                                _vp, _vp]),
     "knx_prof_start": (_i32, [_i32]),
