@@ -480,7 +480,7 @@ inline size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 MoeWs carve_moe_ws(uint8_t* base, int64_t T, int64_t H, int64_t I, int E, int topk) {
   MoeWs w{};
   const int64_t N = T * topk;
-  const int64_t max_tasks = (N + M_MAX - 1) / M_MAX + E;
+  const int64_t max_tasks = (N + MIN_TASK_TOKENS - 1) / MIN_TASK_TOKENS + E;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     uint8_t* p = base ? base + o : nullptr;

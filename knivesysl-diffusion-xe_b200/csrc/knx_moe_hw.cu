@@ -1,23 +1,29 @@
 // knx_moe_hw.cu — warp-specialised grouped W4A16 GEMMs on the warp-level tensor-core path
-// (mma.sync m16n8k16), the engine for the small-token regime (~16 tokens per expert), where it
-// moves about twice as many weight-rows x k per cycle as tcgen05 (whose instructions cost ~128
-// cycles each whatever N is).
+// (mma.sync m16n8k16) for the small-token regime (<= 16 tokens per task).
 //
-// One persistent CTA per SM:
-//   warps 0-15   math: dequantise nibbles in registers straight into A fragments (dequant8) and
-//                issue m16n8k16 MMAs against the task's tokens (B fragments from shared memory).
-//                Warp w owns two m16 row tiles (gated: 16 gate rows + the matching 16 up rows;
-//                plain: 32 consecutive rows) and the k quarter w/4 of every 128-k stage; the four
-//                quarters are summed through shared memory in fixed order at the end of a work
-//                item (deterministic).
-//   warp 16      scheduler + weight producer: work items from the counter, the slice's
-//                scale/zero rows by 1-D bulk copies, packed nibbles by 2-D TMA (64-byte swizzle)
-//                into an 8-stage ring; weight loads carry an L2 evict-first hint.
-//   warp 17      activation producer: gathers the task's token rows (K-interleaved f16) with
-//                cp.async into a 4-stage ring (rows padded to 320 B: conflict-free fragment
-//                loads), with an L2 evict-last hint so the rows stay cached across slices.
-// All waits are bounded (2 s); on a timeout the kernel sets KNX_DEV_TIMEOUT and every role leaves
-// at the next work-item boundary (math warps agree through a named barrier first).
+// Why this shape (measured on B200): a tcgen05 M128 x K16 instruction costs ~108 ns whatever N
+// is, which caps a weights-as-M tcgen05 GEMM at ~1.4 TB/s of nibbles when N (tokens) is small,
+// while mma.sync has no such floor; and HBM only streams at full rate with >= ~128 KB of loads
+// in flight per SM.  So:
+//   * one persistent CTA per SM; a work item is (task of <= 16 tokens of one expert, slice of 256
+//     weight rows) — gated: 128 gate rows + the matching 128 up rows;
+//   * warp 16 (scheduler + weights): per item the slice's scale/zero rows by 1-D bulk copies, then
+//     the packed nibbles by 2-D TMA (128-byte swizzle) in 32 KB stages (256 rows x 256 k) into a
+//     ring of up to 4 stages (128 KB in flight);
+//   * warp 17 (activations): per stage, one 1-D bulk copy per token of 256 k (512 B) gathered
+//     by token id into a 4-stage ring (rows padded to 576 B: conflict-free fragment loads);
+//   * warps 0-15 (math): warp w owns one m16 row tile — gated: gate rows 8w..8w+7 on tile rows
+//     0-7 and the matching up rows on tile rows 8-15, so each lane ends with gate and up of one
+//     intermediate column; plain: rows 16w..16w+15 — over the full K.  Nibbles are dequantised in
+//     registers into A fragments (dequant8: bit-identical to dequant_w4 for integer zero-points,
+//     the reference kernel's f16 arithmetic otherwise) and multiplied with the tokens' B
+//     fragments.  No split-K: every output is one warp's fixed-order sum (deterministic).
+//   * GELU(gate) * up (gated) or the plain result goes through a shared-memory tile to
+//     coalesced 16-byte stores; the gated output is written in the K-interleave the down GEMM
+//     reads.
+// All waits are bounded (2 s): on a timeout the kernel sets KNX_DEV_TIMEOUT and every role
+// leaves at the next work-item boundary (the math warps agree through bar.red first); the
+// producers wait (bounded) for their copies in flight before the CTA exits.
 #include "knx_common.cuh"
 #include "knx_internal.cuh"
 #include "knx_sm100.cuh"
@@ -27,21 +33,28 @@ namespace hw {
 
 using namespace sm100;
 
-constexpr int TOK = 32;                  // tokens per task
-constexpr int NT = TOK / 8;              // n8 tiles
-constexpr int BK = 128;                  // k per stage
-constexpr int WROW = BK / 2;             // 64 bytes of nibbles per row per stage
-constexpr int ROWS = 128;                // weight rows per item (gated: 64 gate + 64 up)
-constexpr int SW = 8, SA = 4, IR = 2;
-constexpr int W_STAGE = ROWS * WROW;     // 8 KB
-constexpr int AROW = BK * 2 + 64;        // 320 B per token row per stage
-constexpr int A_STAGE = TOK * AROW;      // 10 KB
+constexpr int TOK = HW_TASK_TOKENS;      // tokens per task (16)
+constexpr int NT = TOK / 8;              // n8 tiles per task
+constexpr int BK = 256;                  // k per stage
+constexpr int WROW = BK / 2;             // 128 bytes of nibbles per row per stage
+constexpr int ROWS = 256;                // weight rows per item
+constexpr int GROWS = ROWS / 2;          // gated: gate rows per item
+constexpr int BOX_ROWS = 128;            // rows per TMA box
+constexpr int SW_MAX = 4, SA = 4, IR = 2;
+constexpr int W_STAGE = ROWS * WROW;     // 32 KB
+constexpr int AROW = BK * 2 + 64;        // 576 B per token row per stage
+constexpr int A_STAGE = TOK * AROW;      // 9 KB
 constexpr int MATH_WARPS = 16;
 constexpr int NUM_WARPS = MATH_WARPS + 2;
 constexpr int NTHREADS = NUM_WARPS * 32;
 constexpr int WARP_WPROD = MATH_WARPS, WARP_APROD = MATH_WARPS + 1;
-constexpr int SZ_MAX = 32;
+constexpr int SZ_MAX = 32;               // groups per row
 constexpr int OT = ROWS + 8;             // output tile row (halfs)
+constexpr int OT_BYTES = TOK * OT * 2;
+constexpr size_t SMEM_LIMIT = 232448;    // 227 KB opt-in per block
+constexpr size_t STATIC_RESERVE = 1024;  // Ctrl + alignment of the dynamic base
+
+static_assert(NT == 2, "the math loop is written for 16-token tasks");
 
 struct Item {
   int valid, e, cnt, slice;
@@ -49,7 +62,7 @@ struct Item {
 };
 
 struct Ctrl {
-  uint64_t w_full[SW], w_empty[SW];
+  uint64_t w_full[SW_MAX], w_empty[SW_MAX];
   uint64_t a_full[SA], a_empty[SA];
   uint64_t i_full[IR], i_empty[IR];
   Item items[IR];
@@ -72,20 +85,19 @@ struct Params {
   __half* out;
   int64_t out_stride;
   int nslices;
+  int sw;  // weight ring depth (stages)
   int32_t* err;
 };
 
-// shared memory (from a 1024-aligned base)
-constexpr int OFF_W = 0;
-constexpr int OFF_A = OFF_W + SW * W_STAGE;
-constexpr int OFF_RED = OFF_A + SA * A_STAGE;
-constexpr int RED_BYTES = 3 * 4 * 32 * 32 * 4;   // k quarters 1..3 x 4 row pairs x 32 lanes x 32 f32
-constexpr int OFF_OT = OFF_RED + RED_BYTES;
-constexpr int OT_BYTES = TOK * OT * 2;
-constexpr int OFF_SZ = OFF_OT + ((OT_BYTES + 1023) & ~1023);
-KNX_HOST_DEVINL size_t sz_raw_bytes(int ng) { return (static_cast<size_t>(512) * ng + 127) & ~size_t(127); }
-inline size_t smem_bytes(int ng) {
-  return 1024 + OFF_SZ + IR * sz_raw_bytes(ng) + static_cast<size_t>(ROWS) * ng * 8;
+KNX_HOST_DEVINL size_t sz_slot_bytes(int ng) { return static_cast<size_t>(ROWS) * ng * 4; }
+inline size_t smem_bytes(int ng, int sw) {
+  return 1024 + static_cast<size_t>(sw) * W_STAGE + SA * A_STAGE + ((OT_BYTES + 127) & ~127) +
+         IR * sz_slot_bytes(ng);
+}
+inline int ring_depth(int ng) {
+  for (int sw = SW_MAX; sw >= 2; --sw)
+    if (smem_bytes(ng, sw) + STATIC_RESERVE <= SMEM_LIMIT) return sw;
+  return 0;
 }
 
 KNX_DEVINL void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
@@ -109,15 +121,19 @@ KNX_DEVINL float gelu_tanh(float x) {
 }
 KNX_DEVINL int perm_pos(int n) { return (n & ~7) + 2 * (n & 3) + ((n >> 2) & 1); }
 
-KNX_DEVINL uint64_t policy_evict_last() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-KNX_DEVINL void cp_async16_hint(void* smem, const void* gmem, uint64_t pol) {
-  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(
-                   smem_u32(smem)),
-               "l"(gmem), "l"(pol));
+// Dequant constants of one (row, group) as f16x2 broadcasts; the same values as make_sz (every
+// operation below is exact or a single rounding of the exact result).
+template <bool ZINT>
+KNX_DEVINL void group_consts(__half s, __half z, __half2& s2, __half2& s16, __half2& c2,
+                             __half2& c16) {
+  const __half k16 = __ushort_as_half(0x4c00u), k1024 = __ushort_as_half(0x6400u);
+  const __half sh = __hmul(s, __ushort_as_half(0x2c00u));  // s / 16
+  const __half c = ZINT ? __hadd(z, k1024) : z;
+  const __half ch = ZINT ? __hfma(z, k16, k1024) : __hmul(z, k16);
+  s2 = __half2half2(s);
+  s16 = __half2half2(sh);
+  c2 = __half2half2(c);
+  c16 = __half2half2(ch);
 }
 
 template <bool GATED, bool ZINT>
@@ -126,19 +142,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   extern __shared__ uint8_t dsm_raw[];
   __shared__ Ctrl ctrl;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* w_ring = base + OFF_W;
-  uint8_t* a_ring = base + OFF_A;
-  float* red = reinterpret_cast<float*>(base + OFF_RED);
-  __half* otile = reinterpret_cast<__half*>(base + OFF_OT);
-  const size_t szr = sz_raw_bytes(p.ng);
-  uint8_t* sz_ring = base + OFF_SZ;
-  uint2* sz2 = reinterpret_cast<uint2*>(sz_ring + IR * szr);  // [ROWS][ng]
+  const int sw = p.sw;
+  uint8_t* w_ring = base;
+  uint8_t* a_ring = base + sw * W_STAGE;
+  __half* otile = reinterpret_cast<__half*>(a_ring + SA * A_STAGE);
+  uint8_t* sz_ring = a_ring + SA * A_STAGE + ((OT_BYTES + 127) & ~127);
+  const size_t szr = sz_slot_bytes(p.ng);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nst = (p.K + BK - 1) / BK;
 
   if (tid == 0) {
-    for (int s = 0; s < SW; ++s) { mbar_init(&ctrl.w_full[s], 1); mbar_init(&ctrl.w_empty[s], MATH_WARPS); }
-    for (int s = 0; s < SA; ++s) { mbar_init(&ctrl.a_full[s], 32); mbar_init(&ctrl.a_empty[s], MATH_WARPS); }
+    for (int s = 0; s < sw; ++s) { mbar_init(&ctrl.w_full[s], 1); mbar_init(&ctrl.w_empty[s], MATH_WARPS); }
+    for (int s = 0; s < SA; ++s) { mbar_init(&ctrl.a_full[s], 1); mbar_init(&ctrl.a_empty[s], MATH_WARPS); }
     for (int i = 0; i < IR; ++i) {
       mbar_init(&ctrl.i_full[i], 1);
       mbar_init(&ctrl.i_empty[i], MATH_WARPS + 1);
@@ -168,7 +183,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int i = 0; i < IR; ++i) last_on_slot[i] = -1;
       for (int n = 0;; ++n) {
         const int slot = n % IR;
-        if (!wait(&ctrl.i_empty[slot], ((n / IR) & 1) ^ 1)) break;
+        if (!wait(&ctrl.i_empty[slot], ((n / IR) & 1) ^ 1, 64)) break;
         const int wi = atomicAdd(p.work_counter, 1);
         Item it{};
         if (wi < nwork) {
@@ -182,7 +197,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             it.e = 0; t0 = task * TOK; it.cnt = min(TOK, p.dense_rows - t0);
           }
           it.slot0 = (p.offsets ? p.offsets[it.e] : 0) + t0;
-          it.nvalid = GATED ? ROWS : min(ROWS, p.rows_per_expert - it.slice * ROWS);
+          it.nvalid = GATED ? min(GROWS, p.I - it.slice * GROWS)
+                            : min(ROWS, p.rows_per_expert - it.slice * ROWS);
           it.valid = 1;
         }
         ctrl.items[slot] = it;
@@ -194,49 +210,53 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         last_on_slot[slot] = n;
         uint8_t* szs = sz_ring + slot * szr;
         const int ng = p.ng;
+        // scale/zero rows (16-byte multiples): gated [s_gate | z_gate | s_up | z_up] regions of
+        // 128 rows each, plain [s | z] regions of 256 rows each
+        const uint32_t b = static_cast<uint32_t>(it.nvalid) * ng * 2u;
         if (GATED) {
-          const int64_t g0 = (static_cast<int64_t>(it.e) * p.rows_per_expert + it.slice * 64) * ng;
+          const int64_t g0 = (static_cast<int64_t>(it.e) * p.rows_per_expert + it.slice * GROWS) * ng;
           const int64_t u0 = g0 + static_cast<int64_t>(p.I) * ng;
-          const uint32_t b = 64u * ng * 2u;
+          const uint32_t reg = GROWS * ng * 2u;
           mbar_arrive_expect_tx(&ctrl.i_full[slot], 4 * b);
-          bulk_load(szs + 0 * b, p.ws + g0, b, &ctrl.i_full[slot]);
-          bulk_load(szs + 1 * b, p.wz + g0, b, &ctrl.i_full[slot]);
-          bulk_load(szs + 2 * b, p.ws + u0, b, &ctrl.i_full[slot]);
-          bulk_load(szs + 3 * b, p.wz + u0, b, &ctrl.i_full[slot]);
+          bulk_load(szs + 0 * reg, p.ws + g0, b, &ctrl.i_full[slot]);
+          bulk_load(szs + 1 * reg, p.wz + g0, b, &ctrl.i_full[slot]);
+          bulk_load(szs + 2 * reg, p.ws + u0, b, &ctrl.i_full[slot]);
+          bulk_load(szs + 3 * reg, p.wz + u0, b, &ctrl.i_full[slot]);
         } else {
           const int64_t r0 = (static_cast<int64_t>(it.e) * p.rows_per_expert + it.slice * ROWS) * ng;
-          const uint32_t b = static_cast<uint32_t>(it.nvalid) * ng * 2u;
+          const uint32_t reg = ROWS * ng * 2u;
           mbar_arrive_expect_tx(&ctrl.i_full[slot], 2 * b);
           bulk_load(szs, p.ws + r0, b, &ctrl.i_full[slot]);
-          bulk_load(szs + 256 * ng, p.wz + r0, b, &ctrl.i_full[slot]);
+          bulk_load(szs + reg, p.wz + r0, b, &ctrl.i_full[slot]);
         }
         for (int st = 0; st < nst; ++st, ++wst) {
-          const int s = wst % SW;
-          if (!wait(&ctrl.w_empty[s], ((wst / SW) & 1) ^ 1)) break;
+          const int s = wst % sw;
+          if (!wait(&ctrl.w_empty[s], ((wst / sw) & 1) ^ 1)) break;
           uint8_t* dst = w_ring + s * W_STAGE;
           mbar_arrive_expect_tx(&ctrl.w_full[s], W_STAGE);
           const int x = st * WROW;
           if (GATED) {
-            const int y = it.e * p.rows_per_expert + it.slice * 64;
+            const int y = it.e * p.rows_per_expert + it.slice * GROWS;
             tma_load_2d(dst, &wmap, &ctrl.w_full[s], x, y);
-            tma_load_2d(dst + 64 * WROW, &wmap, &ctrl.w_full[s], x, y + p.I);
+            tma_load_2d(dst + BOX_ROWS * WROW, &wmap, &ctrl.w_full[s], x, y + p.I);
           } else {
-            tma_load_2d(dst, &wmap, &ctrl.w_full[s], x, it.e * p.rows_per_expert + it.slice * ROWS);
+            const int y = it.e * p.rows_per_expert + it.slice * ROWS;
+            tma_load_2d(dst, &wmap, &ctrl.w_full[s], x, y);
+            tma_load_2d(dst + BOX_ROWS * WROW, &wmap, &ctrl.w_full[s], x, y + BOX_ROWS);
           }
         }
         if (*abort_flag) break;
       }
       // Copies already issued must land before the CTA exits (only pending after an abort): the
       // newest phase of every weight stage and of every item slot is waited for, bounded.
-      for (uint32_t x = wst > SW ? wst - SW : 0; x < wst; ++x)
-        mbar_wait(&ctrl.w_full[x % SW], (x / SW) & 1);
+      for (uint32_t x = wst > static_cast<uint32_t>(sw) ? wst - sw : 0; x < wst; ++x)
+        mbar_wait(&ctrl.w_full[x % sw], (x / sw) & 1);
       for (int i = 0; i < IR; ++i)
         if (last_on_slot[i] >= 0) mbar_wait(&ctrl.i_full[i], (last_on_slot[i] / IR) & 1);
     }
     __syncwarp();
   } else if (warp == WARP_APROD) {
     // ---------------------------------------------------------------- activation gather
-    const uint64_t pol = policy_evict_last();
     uint32_t ast = 0;
     for (int n = 0;; ++n) {
       const int slot = n % IR;
@@ -258,29 +278,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ok = false;
           break;
         }
-        if (src) {
-          uint8_t* dst = a_ring + s * A_STAGE + lane * AROW;
-          const int k0 = st * BK;
-          const int kch = min(BK, p.K - k0) >> 3;
-#pragma unroll 4
-          for (int j = 0; j < kch; ++j) cp_async16_hint(dst + j * 16, src + k0 + j * 8, pol);
-        }
-        cp_async_mbar_arrive_noinc(&ctrl.a_full[s]);
+        const int k0 = st * BK;
+        const uint32_t kb = static_cast<uint32_t>(min(BK, p.K - k0)) * 2u;
+        if (lane == 0) mbar_arrive_expect_tx(&ctrl.a_full[s], kb * it.cnt);
+        __syncwarp();
+        if (src) bulk_load(a_ring + s * A_STAGE + lane * AROW, src + k0, kb, &ctrl.a_full[s]);
       }
       __syncwarp();
       if (!ok) break;
       if (lane == 0) mbar_arrive(&ctrl.i_empty[slot]);
     }
-    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    // bulk copies already issued must land before the CTA exits (bounded)
+    if (lane == 0)
+      for (uint32_t x = ast > static_cast<uint32_t>(SA) ? ast - SA : 0; x < ast; ++x)
+        mbar_wait(&ctrl.a_full[x % SA], (x / SA) & 1);
+    __syncwarp();
   } else {
     // ---------------------------------------------------------------- math warps
-    const int mp = warp & 3, kq = warp >> 2;
     const int g = lane >> 2, q = lane & 3;
-    // two m16 row tiles: A = rows rA, rA+8; B = rows rB, rB+8
-    const int rA = GATED ? 16 * mp + g : 32 * mp + g;
-    const int rB = GATED ? 64 + 16 * mp + g : 32 * mp + 16 + g;
-    const uint32_t chA = ((kq ^ ((rA >> 1) & 3)) << 4) + 4 * q;  // swizzled byte offset in the row
-    const uint32_t chB = ((kq ^ ((rB >> 1) & 3)) << 4) + 4 * q;
+    // smem rows of this lane's two fragment rows (tile rows g and g+8); both are = g (mod 8),
+    // which the 128-byte swizzle uses: 16-byte chunk j of row r sits at chunk j ^ (r & 7)
+    const int rA = GATED ? 8 * warp + g : 16 * warp + g;
+    const int rB = GATED ? GROWS + 8 * warp + g : 16 * warp + 8 + g;
+    const int first_row = GATED ? 8 * warp : 16 * warp;  // tile's first row (validity)
     uint32_t wst = 0, ast = 0;
     for (int n = 0;; ++n) {
       const int slot = n % IR;
@@ -292,132 +312,105 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0 && got) mbar_arrive(&ctrl.i_empty[slot]);
         break;
       }
-      // per-item dequant constants {s, c, s/16, c16} for every (row, group)
-      {
-        const __half* szs = reinterpret_cast<const __half*>(sz_ring + slot * szr);
-        const int ng = p.ng;
-        for (int i = tid; i < ROWS * ng; i += MATH_WARPS * 32) {
-          const int row = i / ng, grp = i - row * ng;
-          const __half* srow;
-          const __half* zrow;
-          if (GATED) {
-            srow = szs + (row < 64 ? 0 : 128 * ng) + (row & 63) * ng;
-            zrow = srow + 64 * ng;
-          } else {
-            srow = szs + row * ng;
-            zrow = szs + 128 * ng + row * ng;
-          }
-          sz2[i] = row < it.nvalid ? make_sz<ZINT>(srow[grp], zrow[grp]) : make_uint2(0u, 0u);
-        }
+      const __half* szs = reinterpret_cast<const __half*>(sz_ring + slot * szr);
+      const int ng = p.ng;
+      // scale/zero rows of this lane's two fragment rows
+      const __half* sA;
+      const __half* zA;
+      const __half* sB;
+      const __half* zB;
+      if (GATED) {
+        sA = szs + (8 * warp + g) * ng;
+        zA = sA + GROWS * ng;
+        sB = sA + 2 * GROWS * ng;
+        zB = sA + 3 * GROWS * ng;
+      } else {
+        sA = szs + (16 * warp + g) * ng;
+        zA = sA + ROWS * ng;
+        sB = sA + 8 * ng;
+        zB = zA + 8 * ng;
       }
-      named_bar(1, MATH_WARPS * 32);
-      float accA[NT][4], accB[NT][4];
+      const bool active = first_row < it.nvalid;
+      const int ntl = (it.cnt + 7) >> 3;
+      const int jpg = p.gs / 32;  // k32 steps per scale group
+      float acc[NT][4];
 #pragma unroll
       for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) accA[t][i] = accB[t][i] = 0.f;
-      const int ntl = (it.cnt + 7) >> 3;
+        for (int i = 0; i < 4; ++i) acc[t][i] = 0.f;
+      __half2 sa2, sa16, ca2, ca16, sb2, sb16, cb2, cb16;
+      int grp = 0, jg = 0;
       for (int st = 0; st < nst; ++st, ++wst, ++ast) {
-        const int ws = wst % SW, as = ast % SA;
-        const bool ready = wait(&ctrl.w_full[ws], (wst / SW) & 1) && wait(&ctrl.a_full[as], (ast / SA) & 1);
-        const int k0 = st * BK + kq * 32;
-        if (ready && k0 < p.K) {
-          const int grp = k0 / p.gs;
-          __half2 sA0, tA0, cA0, dA0, sA8, tA8, cA8, dA8, sB0, tB0, cB0, dB0, sB8, tB8, cB8, dB8;
-          auto unpack = [&](uint2 v, __half2& s, __half2& s16, __half2& c, __half2& c16) {
-            s = __low2half2(u32_as_h2(v.x));
-            c = __high2half2(u32_as_h2(v.x));
-            s16 = __low2half2(u32_as_h2(v.y));
-            c16 = __high2half2(u32_as_h2(v.y));
-          };
-          unpack(sz2[rA * p.ng + grp], sA0, tA0, cA0, dA0);
-          unpack(sz2[(rA + 8) * p.ng + grp], sA8, tA8, cA8, dA8);
-          unpack(sz2[rB * p.ng + grp], sB0, tB0, cB0, dB0);
-          unpack(sz2[(rB + 8) * p.ng + grp], sB8, tB8, cB8, dB8);
-          const uint32_t wb = smem_u32(w_ring + ws * W_STAGE);
-          uint32_t fA0[4], fA8[4], fB0[4], fB8[4];
-          dequant8<ZINT>(lds32(wb + rA * WROW + chA), sA0, tA0, cA0, dA0, fA0);
-          dequant8<ZINT>(lds32(wb + (rA + 8) * WROW + chA), sA8, tA8, cA8, dA8, fA8);
-          dequant8<ZINT>(lds32(wb + rB * WROW + chB), sB0, tB0, cB0, dB0, fB0);
-          dequant8<ZINT>(lds32(wb + (rB + 8) * WROW + chB), sB8, tB8, cB8, dB8, fB8);
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ctrl.w_empty[ws]);  // nibbles consumed
-          const uint32_t ab = smem_u32(a_ring + as * A_STAGE) + kq * 64 + q * 16;
+        const int ws = wst % sw, as = ast % SA;
+        const bool ready = wait(&ctrl.w_full[ws], (wst / sw) & 1) && wait(&ctrl.a_full[as], (ast / SA) & 1);
+        if (ready && active) {
+          const uint32_t wa = smem_u32(w_ring + ws * W_STAGE) + rA * WROW + 4 * q;
+          const uint32_t wb = smem_u32(w_ring + ws * W_STAGE) + rB * WROW + 4 * q;
+          const uint32_t ab = smem_u32(a_ring + as * A_STAGE) + g * AROW + q * 16;
+          const int jmax = min(8, (p.K - st * BK) >> 5);
 #pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            if (t < ntl) {
-              const uint4 b = lds128(ab + (8 * t + g) * AROW);
-              mma_16816(accA[t], fA0[0], fA8[0], fA0[1], fA8[1], b.x, b.y);
-              mma_16816(accA[t], fA0[2], fA8[2], fA0[3], fA8[3], b.z, b.w);
-              mma_16816(accB[t], fB0[0], fB8[0], fB0[1], fB8[1], b.x, b.y);
-              mma_16816(accB[t], fB0[2], fB8[2], fB0[3], fB8[3], b.z, b.w);
+          for (int j = 0; j < 8; ++j) {
+            if (j < jmax) {
+              if (jg == 0) {
+                group_consts<ZINT>(sA[grp], zA[grp], sa2, sa16, ca2, ca16);
+                group_consts<ZINT>(sB[grp], zB[grp], sb2, sb16, cb2, cb16);
+              }
+              const uint32_t sw_off = static_cast<uint32_t>((j ^ g) << 4);
+              uint32_t fa[4], fb[4];
+              dequant8<ZINT>(lds32(wa + sw_off), sa2, sa16, ca2, ca16, fa);
+              dequant8<ZINT>(lds32(wb + sw_off), sb2, sb16, cb2, cb16, fb);
+#pragma unroll
+              for (int t = 0; t < NT; ++t) {
+                if (t < ntl) {
+                  const uint4 b = lds128(ab + t * 8 * AROW + j * 64);
+                  mma_16816(acc[t], fa[0], fb[0], fa[1], fb[1], b.x, b.y);
+                  mma_16816(acc[t], fa[2], fb[2], fa[3], fb[3], b.z, b.w);
+                }
+              }
+              if (++jg == jpg) {
+                jg = 0;
+                ++grp;
+              }
             }
           }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&ctrl.a_empty[as]);
-        } else {
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&ctrl.w_empty[ws]);
-            mbar_arrive(&ctrl.a_empty[as]);
-          }
+        }
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&ctrl.w_empty[ws]);
+          mbar_arrive(&ctrl.a_empty[as]);
         }
       }
-      // ---- fixed-order split-K reduction over the four k quarters, epilogue, stores
-      if (kq > 0) {
-        float* r = red + ((kq - 1) * 4 + mp) * 32 * 32 + lane;
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            r[(t * 4 + i) * 32] = accA[t][i];
-            r[(16 + t * 4 + i) * 32] = accB[t][i];
-          }
-      }
-      named_bar(1, MATH_WARPS * 32);
-      if (kq == 0) {
+      // ---- epilogue: shared tile -> coalesced 16-byte stores
+      named_bar(1, MATH_WARPS * 32);  // the previous item's stores have read the tile
+      if (active) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
           if (t < ntl) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              float a = accA[t][i], b = accB[t][i];
-#pragma unroll
-              for (int k = 0; k < 3; ++k) {
-                const float* r = red + (k * 4 + mp) * 32 * 32 + lane;
-                a += r[(t * 4 + i) * 32];
-                b += r[(16 + t * 4 + i) * 32];
-              }
-              const int tok = 8 * t + 2 * q + (i & 1);
-              const int dr = (i & 2) ? 8 : 0;
+            for (int h = 0; h < 2; ++h) {
+              const int tok = 8 * t + 2 * q + h;
               if (GATED) {
-                otile[tok * OT + perm_pos(16 * mp + g + dr)] = __float2half_rn(gelu_tanh(a) * b);
+                const float v = gelu_tanh(acc[t][h]) * acc[t][2 + h];
+                otile[tok * OT + perm_pos(8 * warp + g)] = __float2half_rn(v);
               } else {
-                otile[tok * OT + rA + dr] = __float2half_rn(a);
-                otile[tok * OT + rB + dr] = __float2half_rn(b);
+                otile[tok * OT + 16 * warp + g] = __float2half_rn(acc[t][h]);
+                otile[tok * OT + 16 * warp + 8 + g] = __float2half_rn(acc[t][2 + h]);
               }
             }
           }
         }
       }
       named_bar(1, MATH_WARPS * 32);
-      if (GATED) {
-        for (int c = tid; c < it.cnt * 8; c += MATH_WARPS * 32) {
-          const int t = c >> 3, ch = c & 7;
-          *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(it.slot0 + t) * p.out_stride +
-                                    it.slice * 64 + ch * 8) =
-              *reinterpret_cast<const uint4*>(otile + t * OT + ch * 8);
-        }
-      } else {
-        const int vch = it.nvalid >> 3;
+      {
+        const int vch = it.nvalid >> 3;  // 16-byte chunks per token row
+        const int col0 = GATED ? it.slice * GROWS : it.slice * ROWS;
         for (int c = tid; c < it.cnt * vch; c += MATH_WARPS * 32) {
           const int t = c / vch, ch = c - t * vch;
           *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(it.slot0 + t) * p.out_stride +
-                                    it.slice * ROWS + ch * 8) =
+                                    col0 + ch * 8) =
               *reinterpret_cast<const uint4*>(otile + t * OT + ch * 8);
         }
       }
-      named_bar(1, MATH_WARPS * 32);
       __syncwarp();
       if (lane == 0) mbar_arrive(&ctrl.i_empty[slot]);
     }
@@ -434,8 +427,7 @@ using EncodeTiledFn2 = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_
                                     const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
                                     CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-bool encode_map_hw(CUtensorMap* map, const uint8_t* q, int64_t total_rows, int64_t row_bytes,
-                   int box_rows) {
+bool encode_map_hw(CUtensorMap* map, const uint8_t* q, int64_t total_rows, int64_t row_bytes) {
   static EncodeTiledFn2 fn = nullptr;
   if (fn == nullptr) {
     void* f = nullptr;
@@ -447,15 +439,15 @@ bool encode_map_hw(CUtensorMap* map, const uint8_t* q, int64_t total_rows, int64
   }
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(total_rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(hw::WROW), static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(hw::WROW), static_cast<cuuint32_t>(hw::BOX_ROWS)};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <bool GATED, bool ZINT>
-int launch_hw(const hw::Params& p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
+int launch_hw(hw::Params p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
               int64_t work_bound, cudaStream_t s) {
   static bool attr[64] = {};
   int dev = 0;
@@ -463,24 +455,26 @@ int launch_hw(const hw::Params& p, const uint8_t* wq, int64_t total_rows, int64_
   if (!attr[dev & 63]) {
     if (cudaFuncSetAttribute(hw::hw_gemm_kernel<GATED, ZINT>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(hw::smem_bytes(hw::SZ_MAX))) != cudaSuccess)
+                             static_cast<int>(hw::SMEM_LIMIT - hw::STATIC_RESERVE)) != cudaSuccess)
       return KNX_E_DEVICE;
     attr[dev & 63] = true;
   }
+  p.sw = hw::ring_depth(p.ng);
+  if (p.sw == 0) return KNX_E_UNSUPPORTED;
   CUtensorMap map;
-  if (!encode_map_hw(&map, wq, total_rows, row_bytes, GATED ? 64 : hw::ROWS)) return KNX_E_DEVICE;
+  if (!encode_map_hw(&map, wq, total_rows, row_bytes)) return KNX_E_DEVICE;
   const int sms = num_sms();
   const int grid = static_cast<int>(work_bound < sms ? (work_bound > 0 ? work_bound : 1) : sms);
-  hw::hw_gemm_kernel<GATED, ZINT><<<grid, hw::NTHREADS, hw::smem_bytes(p.ng), s>>>(map, p);
+  hw::hw_gemm_kernel<GATED, ZINT><<<grid, hw::NTHREADS, hw::smem_bytes(p.ng, p.sw), s>>>(map, p);
   return launch_status();
 }
 
 }  // namespace
 
 bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated) {
-  if (gs % 32 != 0 || ng > hw::SZ_MAX || (K % 64) != 0) return false;
+  if (gs % 32 != 0 || ng > hw::SZ_MAX || (K % 64) != 0 || hw::ring_depth(ng) == 0) return false;
   if (gated) return (rows_per_expert / 2) % 64 == 0;
-  return rows_per_expert % hw::ROWS == 0;
+  return rows_per_expert % 16 == 0;
 }
 
 int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, const int32_t* offsets,
@@ -491,7 +485,7 @@ int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, con
   p.act = xp; p.act_stride = H; p.sorted_pair = sorted_pair; p.topk = topk; p.offsets = offsets;
   p.tasks = tasks; p.ntasks = ntasks; p.work_counter = counter; p.ws = gu_s; p.wz = gu_z;
   p.K = H; p.rows_per_expert = 2 * I; p.I = I; p.ng = ng; p.gs = gs; p.out = out2;
-  p.out_stride = I; p.nslices = I / 64; p.err = err;
+  p.out_stride = I; p.nslices = (I + hw::GROWS - 1) / hw::GROWS; p.err = err;
   const int64_t work = max_tasks * p.nslices;
   return zint ? launch_hw<true, true>(p, gu_q, int64_t(E) * 2 * I, H / 2, work, s)
               : launch_hw<true, false>(p, gu_q, int64_t(E) * 2 * I, H / 2, work, s);
