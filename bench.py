@@ -34,9 +34,13 @@ METRIC = json.loads((REPO / "BASELINE.json").read_text())["metric"]
 T, H, I, E, TOPK = 256, 2816, 704, 128, 8
 V_SAMPLER = 262144
 NSETS = 4
-# DRAM bytes per launch of the dominant kernel (gate_up+GELU GEMM) from one ncu capture of the
-# configs[1] layer (see profiles/); None until a capture exists for the current kernel.
-GEMM1_NCU_TRAFFIC = None
+# The dominant kernel per GEMM engine, and its DRAM bytes per launch (dram__bytes_read.sum +
+# dram__bytes_write.sum) from one ncu capture of the configs[1] layer, summarised under profiles/;
+# None where no capture of the current kernel exists.
+GEMM1_KERNEL = {"tc": "tc_gemm_kernel<1,0> (gate_up + GELU)",
+                "ws": "hw_gemm_kernel<1> (gate_up + GELU)",
+                "mma": "gateup_gelu_kernel"}
+GEMM1_NCU_TRAFFIC = {"tc": 276.584960e6 + 6.810624e6}
 
 
 def peaks():
@@ -323,6 +327,7 @@ def main():
                "sample": "one layer: RMSNorm+router on all 256 tokens, MoE on experts e%16==0 "
                          "(dequant inside the timed region) scaled x16"}
     achieved = gemm1_bytes / (gemm1_ms * 1e-3) / 1e9
+    engine = os.environ.get("KNX_ENGINE", "tc")
     line = {
         "metric": METRIC, "value": value, "unit": "us", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False,
@@ -336,9 +341,9 @@ def main():
         "layer_hbm_frac": bytes_layer / (ms_step * 1e-3) / 1e9 / peak,
         "layer_bytes": bytes_layer,
         "stages_us": {k: v * 1000.0 for k, v in stages.items()},
-        "roofline": {"kernel": "gateup_gelu_kernel", "bound": "hbm", "achieved": achieved,
+        "roofline": {"kernel": GEMM1_KERNEL[engine], "bound": "hbm", "achieved": achieved,
                      "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                     "peak_kind": peak_kind, "traffic": GEMM1_NCU_TRAFFIC,
+                     "peak_kind": peak_kind, "traffic": GEMM1_NCU_TRAFFIC.get(engine),
                      "algorithmic_bytes": gemm1_bytes},
         "sampler_step_us": samp_step_ms * 1000.0,
         "sampler_roofline": {"kernel": "sampler_kernel", "bound": "hbm",
