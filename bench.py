@@ -38,7 +38,7 @@ NSETS = 4
 # dram__bytes_write.sum) from one ncu capture of the configs[1] layer, summarised under profiles/;
 # None where no capture of the current kernel exists.
 GEMM1_KERNEL = {"tc": "tc_gemm_kernel<1,0> (gate_up + GELU)",
-                "ws": "hw_gemm_kernel<1> (gate_up + GELU)",
+                "ws": "hw_gemm_kernel<1,0,4> (gate_up + GELU)",
                 "mma": "gateup_gelu_kernel"}
 GEMM1_NCU_TRAFFIC = {"tc": 276.584960e6 + 6.810624e6}
 
@@ -327,7 +327,9 @@ def main():
                "sample": "one layer: RMSNorm+router on all 256 tokens, MoE on experts e%16==0 "
                          "(dequant inside the timed region) scaled x16"}
     achieved = gemm1_bytes / (gemm1_ms * 1e-3) / 1e9
-    engine = os.environ.get("KNX_ENGINE", "tc")
+    engine = os.environ.get("KNX_ENGINE", "auto")
+    if engine == "auto":  # the library's rule: ws up to 64 pairs per expert, tcgen05 above
+        engine = "ws" if T * TOPK // E <= 64 else "tc"
     line = {
         "metric": METRIC, "value": value, "unit": "us", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False,

@@ -477,6 +477,16 @@ struct MoeWs {
 
 inline size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
+// The GEMM engine a call runs: an explicit flag, else the warp-specialised mma.sync kernels for
+// small per-expert token counts (where a tcgen05 instruction's ~108 ns cost does not pay off)
+// and tcgen05 for large ones.
+int engine_choice(int flags, int64_t tokens_per_expert) {
+  if (flags & KNX_W4_WARP_MMA) return KNX_W4_WARP_MMA;
+  if (flags & KNX_W4_WARP_WS) return KNX_W4_WARP_WS;
+  if (flags & KNX_W4_TCGEN05) return KNX_W4_TCGEN05;
+  return tokens_per_expert <= 64 ? KNX_W4_WARP_WS : KNX_W4_TCGEN05;
+}
+
 MoeWs carve_moe_ws(uint8_t* base, int64_t T, int64_t H, int64_t I, int E, int topk) {
   MoeWs w{};
   const int64_t N = T * topk;
@@ -571,10 +581,10 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
     if (st != KNX_OK) return st;
     xp = w.xp;
   }
-  const bool use_ws = !(flags & KNX_W4_WARP_MMA) && (flags & KNX_W4_WARP_WS) &&
-                      hw_supported(H, gs_gu, ng1, 2 * I, true) &&
+  const int eng = engine_choice(flags, T * topk / E);
+  const bool use_ws = eng == KNX_W4_WARP_WS && hw_supported(H, gs_gu, ng1, 2 * I, true) &&
                       hw_supported(I, gs_dn, ng2, H, false);
-  const bool use_tc = !use_ws && !(flags & (KNX_W4_WARP_MMA | KNX_W4_WARP_WS)) &&
+  const bool use_tc = !use_ws && eng != KNX_W4_WARP_MMA &&
                       tc_supported(H, gs_gu, ng1, 2 * I, true) &&
                       tc_supported(I, gs_dn, ng2, H, false);
   const int task_tokens = use_tc ? TC_TASK_TOKENS : use_ws ? HW_TASK_TOKENS : M_MAX;
@@ -679,7 +689,8 @@ extern "C" int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, 
   int rc = launch_permute(X, KNX_F16, xp, M * K, st);
   if (rc != KNX_OK) return rc;
   const bool zint = (flags & KNX_W4_INT_ZEROS) != 0;
-  if (!(flags & KNX_W4_WARP_MMA) && (flags & KNX_W4_WARP_WS) && hw_supported(K, gs, ng, N, false)) {
+  const int eng = engine_choice(flags, M);
+  if (eng == KNX_W4_WARP_WS && hw_supported(K, gs, ng, N, false)) {
     int* counter = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + up256(size_t(M) * K * 2));
     if (cudaMemsetAsync(counter, 0, sizeof(int), st) != cudaSuccess) return KNX_E_LAUNCH;
     return launch_hw_rows(xp, K, static_cast<int>(K), nullptr, nullptr, nullptr,
@@ -688,7 +699,7 @@ extern "C" int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, 
                           static_cast<__half*>(Y), N, (M + HW_TASK_TOKENS - 1) / HW_TASK_TOKENS,
                           nullptr, st);
   }
-  if (!(flags & (KNX_W4_WARP_MMA | KNX_W4_WARP_WS)) && tc_supported(K, gs, ng, N, false)) {
+  if (eng != KNX_W4_WARP_MMA && tc_supported(K, gs, ng, N, false)) {
     int* counter = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + up256(size_t(M) * K * 2));
     if (cudaMemsetAsync(counter, 0, sizeof(int), st) != cudaSuccess) return KNX_E_LAUNCH;
     return launch_tc_rows(xp, K, static_cast<int>(K), nullptr, nullptr, nullptr,

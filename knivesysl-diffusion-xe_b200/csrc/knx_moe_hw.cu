@@ -55,6 +55,17 @@ constexpr size_t SMEM_LIMIT = 232448;    // 227 KB opt-in per block
 constexpr size_t STATIC_RESERVE = 1024;  // Ctrl + alignment of the dynamic base
 
 static_assert(NT == 2, "the math loop is written for 16-token tasks");
+#ifndef KNX_HW_NACC
+#define KNX_HW_NACC 2
+#endif
+constexpr int NACC = KNX_HW_NACC;  // accumulator sets per n8 tile (2 or 4)
+// The producers run stages ahead of the math warps and share their SM sub-partitions (warp 16
+// with warps 0/4/8/12, warp 17 with 1/5/9/13): they back off between polls of their "empty"
+// barriers instead of spinning, which would take issue slots from those math warps.
+#ifndef KNX_HW_PROD_BACKOFF
+#define KNX_HW_PROD_BACKOFF 256
+#endif
+constexpr uint32_t PROD_BACKOFF_NS = KNX_HW_PROD_BACKOFF;
 
 struct Item {
   int valid, e, cnt, slice;
@@ -136,7 +147,38 @@ KNX_DEVINL void group_consts(__half s, __half z, __half2& s2, __half2& s16, __ha
   c16 = __half2half2(ch);
 }
 
-template <bool GATED, bool ZINT>
+// One stage (256 k) of one warp's m16 tile: 8 k32 steps (jmax in the K tail), NTT n8 token
+// tiles.  Scale-group boundaries are compile-time (GPJ k32 steps per group; GPJ = 8 also serves
+// groups that span several stages), so the unrolled loop carries no per-step bookkeeping.
+template <bool ZINT, int NTT, int GPJ, bool TAIL>
+KNX_DEVINL void mma_stage(uint32_t wa, uint32_t wb, uint32_t ab, int g, int jmax, int grp0,
+                          const __half* sA, const __half* zA, const __half* sB, const __half* zB,
+                          float (&acc)[NT][NACC][4]) {
+  __half2 sa2, sa16, ca2, ca16, sb2, sb16, cb2, cb16;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (!TAIL || j < jmax) {
+      if (j % GPJ == 0) {
+        const int grp = grp0 + j / GPJ;
+        group_consts<ZINT>(sA[grp], zA[grp], sa2, sa16, ca2, ca16);
+        group_consts<ZINT>(sB[grp], zB[grp], sb2, sb16, cb2, cb16);
+      }
+      const uint32_t sw_off = static_cast<uint32_t>((j ^ g) << 4);
+      uint32_t fa[4], fb[4];
+      dequant8<ZINT>(lds32(wa + sw_off), sa2, sa16, ca2, ca16, fa);
+      dequant8<ZINT>(lds32(wb + sw_off), sb2, sb16, cb2, cb16, fb);
+#pragma unroll
+      for (int t = 0; t < NTT; ++t) {
+        const uint4 b = lds128(ab + t * 8 * AROW + j * 64);
+        constexpr int UJ = NACC / 2;
+        mma_16816(acc[t][2 * (j % UJ)], fa[0], fb[0], fa[1], fb[1], b.x, b.y);
+        mma_16816(acc[t][2 * (j % UJ) + 1], fa[2], fb[2], fa[3], fb[3], b.z, b.w);
+      }
+    }
+  }
+}
+
+template <bool GATED, bool ZINT, int GPJ>
 __global__ void __launch_bounds__(NTHREADS, 1)
     hw_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const Params p) {
   extern __shared__ uint8_t dsm_raw[];
@@ -183,7 +225,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int i = 0; i < IR; ++i) last_on_slot[i] = -1;
       for (int n = 0;; ++n) {
         const int slot = n % IR;
-        if (!wait(&ctrl.i_empty[slot], ((n / IR) & 1) ^ 1, 64)) break;
+        if (!wait(&ctrl.i_empty[slot], ((n / IR) & 1) ^ 1, PROD_BACKOFF_NS)) break;
         const int wi = atomicAdd(p.work_counter, 1);
         Item it{};
         if (wi < nwork) {
@@ -231,7 +273,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         for (int st = 0; st < nst; ++st, ++wst) {
           const int s = wst % sw;
-          if (!wait(&ctrl.w_empty[s], ((wst / sw) & 1) ^ 1)) break;
+          if (!wait(&ctrl.w_empty[s], ((wst / sw) & 1) ^ 1, PROD_BACKOFF_NS)) break;
           uint8_t* dst = w_ring + s * W_STAGE;
           mbar_arrive_expect_tx(&ctrl.w_full[s], W_STAGE);
           const int x = st * WROW;
@@ -260,7 +302,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint32_t ast = 0;
     for (int n = 0;; ++n) {
       const int slot = n % IR;
-      if (!wait(&ctrl.i_full[slot], (n / IR) & 1, 64)) break;
+      if (!wait(&ctrl.i_full[slot], (n / IR) & 1, PROD_BACKOFF_NS)) break;
       const Item it = ctrl.items[slot];
       if (!it.valid) {
         __syncwarp();
@@ -274,7 +316,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bool ok = true;
       for (int st = 0; st < nst; ++st, ++ast) {
         const int s = ast % SA;
-        if (!wait(&ctrl.a_empty[s], ((ast / SA) & 1) ^ 1, 32)) {
+        if (!wait(&ctrl.a_empty[s], ((ast / SA) & 1) ^ 1, PROD_BACKOFF_NS)) {
           ok = false;
           break;
         }
@@ -332,14 +374,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       const bool active = first_row < it.nvalid;
       const int ntl = (it.cnt + 7) >> 3;
-      const int jpg = p.gs / 32;  // k32 steps per scale group
-      float acc[NT][4];
+      // NACC independent accumulator sets per n8 tile (k16 half, j parity), added in a fixed
+      // order at the end of the item
+      float acc[NT][NACC][4];
 #pragma unroll
       for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[t][i] = 0.f;
-      __half2 sa2, sa16, ca2, ca16, sb2, sb16, cb2, cb16;
-      int grp = 0, jg = 0;
+        for (int u = 0; u < NACC; ++u)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[t][u][i] = 0.f;
       for (int st = 0; st < nst; ++st, ++wst, ++ast) {
         const int ws = wst % sw, as = ast % SA;
         const bool ready = wait(&ctrl.w_full[ws], (wst / sw) & 1) && wait(&ctrl.a_full[as], (ast / SA) & 1);
@@ -348,30 +391,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t wb = smem_u32(w_ring + ws * W_STAGE) + rB * WROW + 4 * q;
           const uint32_t ab = smem_u32(a_ring + as * A_STAGE) + g * AROW + q * 16;
           const int jmax = min(8, (p.K - st * BK) >> 5);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            if (j < jmax) {
-              if (jg == 0) {
-                group_consts<ZINT>(sA[grp], zA[grp], sa2, sa16, ca2, ca16);
-                group_consts<ZINT>(sB[grp], zB[grp], sb2, sb16, cb2, cb16);
-              }
-              const uint32_t sw_off = static_cast<uint32_t>((j ^ g) << 4);
-              uint32_t fa[4], fb[4];
-              dequant8<ZINT>(lds32(wa + sw_off), sa2, sa16, ca2, ca16, fa);
-              dequant8<ZINT>(lds32(wb + sw_off), sb2, sb16, cb2, cb16, fb);
-#pragma unroll
-              for (int t = 0; t < NT; ++t) {
-                if (t < ntl) {
-                  const uint4 b = lds128(ab + t * 8 * AROW + j * 64);
-                  mma_16816(acc[t], fa[0], fb[0], fa[1], fb[1], b.x, b.y);
-                  mma_16816(acc[t], fa[2], fb[2], fa[3], fb[3], b.z, b.w);
-                }
-              }
-              if (++jg == jpg) {
-                jg = 0;
-                ++grp;
-              }
-            }
+          const int grp0 = (st * BK) / p.gs;
+          if (jmax == 8) {
+            if (ntl == 2) mma_stage<ZINT, 2, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc);
+            else mma_stage<ZINT, 1, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc);
+          } else {
+            if (ntl == 2) mma_stage<ZINT, 2, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc);
+            else mma_stage<ZINT, 1, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc);
           }
         }
         __syncwarp();
@@ -380,6 +406,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           mbar_arrive(&ctrl.a_empty[as]);
         }
       }
+      float res[NT][4];
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float v = acc[t][0][i];
+#pragma unroll
+          for (int u = 1; u < NACC; ++u) v += acc[t][u][i];
+          res[t][i] = v;
+        }
       // ---- epilogue: shared tile -> coalesced 16-byte stores
       named_bar(1, MATH_WARPS * 32);  // the previous item's stores have read the tile
       if (active) {
@@ -390,11 +426,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int h = 0; h < 2; ++h) {
               const int tok = 8 * t + 2 * q + h;
               if (GATED) {
-                const float v = gelu_tanh(acc[t][h]) * acc[t][2 + h];
+                const float v = gelu_tanh(res[t][h]) * res[t][2 + h];
                 otile[tok * OT + perm_pos(8 * warp + g)] = __float2half_rn(v);
               } else {
-                otile[tok * OT + 16 * warp + g] = __float2half_rn(acc[t][h]);
-                otile[tok * OT + 16 * warp + 8 + g] = __float2half_rn(acc[t][2 + h]);
+                otile[tok * OT + 16 * warp + g] = __float2half_rn(res[t][h]);
+                otile[tok * OT + 16 * warp + 8 + g] = __float2half_rn(res[t][2 + h]);
               }
             }
           }
@@ -446,33 +482,45 @@ bool encode_map_hw(CUtensorMap* map, const uint8_t* q, int64_t total_rows, int64
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool GATED, bool ZINT>
-int launch_hw(hw::Params p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
-              int64_t work_bound, cudaStream_t s) {
+template <bool GATED, bool ZINT, int GPJ>
+int launch_hw_g(const hw::Params& p, const CUtensorMap& map, int grid, cudaStream_t s) {
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    if (cudaFuncSetAttribute(hw::hw_gemm_kernel<GATED, ZINT>,
+    if (cudaFuncSetAttribute(hw::hw_gemm_kernel<GATED, ZINT, GPJ>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(hw::SMEM_LIMIT - hw::STATIC_RESERVE)) != cudaSuccess)
       return KNX_E_DEVICE;
     attr[dev & 63] = true;
   }
+  hw::hw_gemm_kernel<GATED, ZINT, GPJ><<<grid, hw::NTHREADS, hw::smem_bytes(p.ng, p.sw), s>>>(map, p);
+  return launch_status();
+}
+
+template <bool GATED, bool ZINT>
+int launch_hw(hw::Params p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
+              int64_t work_bound, cudaStream_t s) {
   p.sw = hw::ring_depth(p.ng);
   if (p.sw == 0) return KNX_E_UNSUPPORTED;
   CUtensorMap map;
   if (!encode_map_hw(&map, wq, total_rows, row_bytes)) return KNX_E_DEVICE;
   const int sms = num_sms();
   const int grid = static_cast<int>(work_bound < sms ? (work_bound > 0 ? work_bound : 1) : sms);
-  hw::hw_gemm_kernel<GATED, ZINT><<<grid, hw::NTHREADS, hw::smem_bytes(p.ng, p.sw), s>>>(map, p);
-  return launch_status();
+  switch (p.gs) {
+    case 32: return launch_hw_g<GATED, ZINT, 1>(p, map, grid, s);
+    case 64: return launch_hw_g<GATED, ZINT, 2>(p, map, grid, s);
+    case 128: return launch_hw_g<GATED, ZINT, 4>(p, map, grid, s);
+    default: return launch_hw_g<GATED, ZINT, 8>(p, map, grid, s);  // gs % 256 == 0
+  }
 }
 
 }  // namespace
 
 bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated) {
-  if (gs % 32 != 0 || ng > hw::SZ_MAX || (K % 64) != 0 || hw::ring_depth(ng) == 0) return false;
+  // scale groups must not straddle a 256-k stage unless they cover whole stages
+  if (!(gs == 32 || gs == 64 || gs == 128 || (gs > 0 && gs % 256 == 0))) return false;
+  if (ng > hw::SZ_MAX || (K % 64) != 0 || hw::ring_depth(ng) == 0) return false;
   if (gated) return (rows_per_expert / 2) % 64 == 0;
   return rows_per_expert % 16 == 0;
 }

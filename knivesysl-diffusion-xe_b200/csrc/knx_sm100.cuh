@@ -42,6 +42,12 @@ KNX_DEVINL void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
       "r"(bytes)
       : "memory");
 }
+// Raise the expected transaction bytes of the current phase without arriving.
+KNX_DEVINL void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
 KNX_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(

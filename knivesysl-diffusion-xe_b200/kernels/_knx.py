@@ -26,14 +26,15 @@ KNX_SAMPLER_STATIC_SCRATCH_BYTES = 1 << 20  # include/knx.h
 KNX_W4_INT_ZEROS = 0x1
 KNX_W4_WARP_MMA = 0x2
 KNX_W4_WARP_WS = 0x8
-_ENGINES = {"tc": 0, "mma": KNX_W4_WARP_MMA, "ws": KNX_W4_WARP_WS}
+KNX_W4_TCGEN05 = 0x10
+_ENGINES = {"auto": 0, "tc": KNX_W4_TCGEN05, "mma": KNX_W4_WARP_MMA, "ws": KNX_W4_WARP_WS}
 
 
 def engine_flags(engine=None):
-    """Engine selection flags for the W4A16 GEMMs: "tc" (tcgen05, the default), "ws" (the
-    warp-specialised mma.sync kernels) or "mma" (the plain mma.sync kernels); `engine` or the
-    KNX_ENGINE environment variable chooses."""
-    engine = engine or os.environ.get("KNX_ENGINE", "tc")
+    """Engine selection flags for the W4A16 GEMMs: "auto" (the default: the warp-specialised
+    mma.sync kernels up to 64 tokens per expert, tcgen05 above), "ws", "tc" (tcgen05) or "mma"
+    (the plain mma.sync kernels); `engine` or the KNX_ENGINE environment variable chooses."""
+    engine = engine or os.environ.get("KNX_ENGINE", "auto")
     if engine not in _ENGINES:
         raise ValueError(f"unknown engine {engine!r}")
     return _ENGINES[engine]
