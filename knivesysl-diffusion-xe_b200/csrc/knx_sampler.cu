@@ -20,6 +20,7 @@
 // Chunk partials are merged by the last CTA of each row in chunk order (deterministic).
 #include "knx_common.cuh"
 #include "knx_math.cuh"
+#include "knx_sm100.cuh"
 
 namespace knx {
 namespace {
@@ -310,6 +311,411 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
 }
 
 // ------------------------------------------------------------------------------------------
+// Streaming variant for V % 4 == 0 (the configs' 262144-wide rows): one persistent CTA per SM.
+//   * work items are quarter rows (SX_CHUNK = 65536 columns, 8 stages), assigned statically (CTA
+//     c takes items c, c + grid, ...), so all roles walk the same sequence without a work queue;
+//   * warp 16 streams each item through a ring of 4 x 32 KB shared-memory stages with 1-D bulk
+//     copies (128 KB in flight per SM, what HBM needs at full rate);
+//   * warps 0-15 each take 512 columns of every 8192-column stage.  The running maximum and the
+//     argmax are kept per warp, so their updates are rare, uniform branches; the common path per
+//     element is the IEEE division by the temperature, a max and five operations of the entropy
+//     update (log2 units).  Gumbel candidates are pruned against the best q + g seen so far in
+//     the row — this CTA's warps share it through shared memory at once, the other CTAs of the
+//     row through a fire-and-forget atomic max on the per-row bound, which warp 18 keeps copying
+//     into shared memory; a stale bound only prunes less, never wrongly;
+//   * warp 17 merges the 16 warp partials of each item (in warp order) into parts[item], double
+//     buffered so the math warps never wait for it; rows are finished by row_merge_kernel.
+// Every decision (argmax ties, Gumbel winner, merge order) is the same as sampler_kernel's, so the
+// sampled and argmax indices are identical; the entropy agrees to fp32 rounding.
+constexpr int SX_COLS = 8192;               // columns per stage
+constexpr int SX_BYTES = SX_COLS * 4;
+constexpr int SX_CHUNK = 8 * SX_COLS;       // columns per work item
+constexpr int SX_RING = 4;
+constexpr int SX_WARPS = 16;                // math warps
+constexpr int SX_THREADS = (SX_WARPS + 3) * 32;
+constexpr size_t SX_SMEM = 128 + static_cast<size_t>(SX_RING) * SX_BYTES +
+                           static_cast<size_t>(SX_WARPS) * SP_TILE * 8;
+
+struct SxCtrl {
+  uint64_t full[SX_RING], empty[SX_RING];
+  uint64_t pfull[2], pempty[2];
+  unsigned long long wbound;  // (row << 32) | fkey(best q + g): rows only grow along a CTA's items
+  long long cur_row;          // row of the item math warp 0 is on (for the bound relay)
+  int done;                   // math warps finished
+  int abort;
+};
+
+KNX_DEVINL uint32_t ld_relaxed_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+KNX_DEVINL float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+KNX_DEVINL int warp_min_i(int v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__global__ void __launch_bounds__(SX_THREADS, 1)
+    sampler_stream_kernel(const float* __restrict__ logits, int64_t rows, int V, float temp,
+                          float rtemp, int do_div, int64_t seed, int seed_is32, int want_gumbel,
+                          int nchunks, Part* __restrict__ parts, uint32_t* __restrict__ row_bound,
+                          int* __restrict__ err) {
+  using namespace sm100;
+  extern __shared__ uint8_t sx_raw[];
+  __shared__ SxCtrl c;
+  __shared__ Part s_wpart[2][SX_WARPS];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sx_raw) + 127) & ~uintptr_t(127));
+  int* cq_col = reinterpret_cast<int*>(ring + SX_RING * SX_BYTES);          // [SX_WARPS][SP_TILE]
+  float* cq_q = reinterpret_cast<float*>(cq_col + SX_WARPS * SP_TILE);     // [SX_WARPS][SP_TILE]
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t nitems = rows * nchunks;
+  if (tid == 0) {
+    for (int i = 0; i < SX_RING; ++i) { mbar_init(&c.full[i], 1); mbar_init(&c.empty[i], SX_WARPS); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&c.pfull[i], SX_WARPS); mbar_init(&c.pempty[i], 1); }
+    c.wbound = 0ull;
+    c.cur_row = -1;
+    c.done = 0;
+    c.abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  volatile int* abort_flag = &c.abort;
+  auto fail = [&]() {
+    *abort_flag = 1;
+    atomicOr(err, KNX_DEV_TIMEOUT);
+  };
+
+  if (warp == SX_WARPS) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t u = 0;
+      for (int64_t item = blockIdx.x; item < nitems && !*abort_flag; item += gridDim.x) {
+        const int64_t row = item / nchunks;
+        const int chunk = static_cast<int>(item - row * nchunks);
+        const int c_beg = min(V, chunk * SX_CHUNK), c_end = min(V, c_beg + SX_CHUNK);
+        const float* xr = logits + row * static_cast<int64_t>(V);
+        for (int c0 = c_beg; c0 < c_end; c0 += SX_COLS, ++u) {
+          const int slot = u % SX_RING;
+          if (!mbar_wait(&c.empty[slot], ((u / SX_RING) & 1) ^ 1, 2000000000ull, 128)) {
+            fail();
+            break;
+          }
+          const uint32_t bytes = static_cast<uint32_t>(min(SX_COLS, c_end - c0)) * 4u;
+          mbar_arrive_expect_tx(&c.full[slot], bytes);
+          bulk_load(ring + slot * SX_BYTES, xr + c0, bytes, &c.full[slot]);
+        }
+      }
+      // copies already issued land before the CTA exits (bounded)
+      for (uint32_t x = u > SX_RING ? u - SX_RING : 0; x < u; ++x)
+        mbar_wait(&c.full[x % SX_RING], (x / SX_RING) & 1);
+    }
+    __syncwarp();
+  } else if (warp == SX_WARPS + 1) {
+    // ------------------------------------------------------------ item merger
+    if (lane == 0) {
+      int k = 0;
+      for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++k) {
+        const int b = k & 1;
+        if (*abort_flag || !mbar_wait(&c.pfull[b], (k >> 1) & 1, 2000000000ull, 64)) {
+          if (!*abort_flag) fail();
+          break;
+        }
+        Part acc = s_wpart[b][0];
+        for (int w = 1; w < SX_WARPS; ++w) {
+          const Part pw = s_wpart[b][w];
+          sm_merge(acc.m, acc.s, acc.t, pw.m, pw.s, pw.t);
+          arg_merge(acc.bq, acc.bqi, pw.bq, pw.bqi);
+          arg_merge(acc.bg, acc.bgi, pw.bg, pw.bgi);
+        }
+        parts[item] = acc;
+        mbar_arrive(&c.pempty[b]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == SX_WARPS + 2) {
+    // ------------------------------------------------------------ bound relay
+    // Copies the global per-row Gumbel bound (other CTAs' best q + g for the row) into this CTA's
+    // shared bound, so no math warp waits on a global round trip.  Bounded by a time limit.
+    if (lane == 0 && want_gumbel) {
+      const uint64_t t0 = globaltimer();
+      volatile long long* vrow = &c.cur_row;
+      volatile int* vdone = &c.done;
+      while (*vdone < SX_WARPS && !*abort_flag && globaltimer() - t0 < 4000000000ull) {
+        const long long r = *vrow;
+        if (r >= 0) {
+          const uint32_t v = ld_relaxed_u32(row_bound + r);
+          if (v) atomicMax(&c.wbound, (static_cast<unsigned long long>(r) << 32) | v);
+        }
+        __nanosleep(256);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ math warps
+    uint32_t u = 0;
+    const float L = LOG2E;
+    int k = 0;
+    int* wcol = cq_col + warp * SP_TILE;   // this warp's deferred Gumbel candidates
+    float* wq = cq_q + warp * SP_TILE;
+    for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++k) {
+      const int64_t row = item / nchunks;
+      const int chunk = static_cast<int>(item - row * nchunks);
+      const int c_beg = min(V, chunk * SX_CHUNK), c_end = min(V, c_beg + SX_CHUNK);
+      uint32_t k0 = 0, k1 = 0;
+      row_key(seed, seed_is32, row, k0, k1);
+      if (warp == 0 && lane == 0) *reinterpret_cast<volatile long long*>(&c.cur_row) = row;
+      // entropy state: m (warp-uniform running max), per lane sp = sum of 2^d2 over the lane's
+      // elements except the one element that carries the implicit 1, t2 = sum d2 * 2^d2
+      float m = -INFINITY, m2 = -INFINITY, sp = 0.f, t2 = 0.f;
+      float bq = -INFINITY;  // warp-uniform argmax
+      int bqi = 0x7fffffff;
+      float bg = -INFINITY;  // per-lane Gumbel winner
+      int bgi = 0x7fffffff;
+      float W = -INFINITY;  // best exact q + g known for the row (warp view)
+      bool first = true;
+      int nbuf = 0;         // deferred candidates in wcol/wq
+      // Evaluates the deferred candidates, 32 at a time.  Each is re-tested against the newest
+      // bound; its Philox word is then screened with the exact-safe test u >= e^(-e^(-y)) - 2e-6
+      // (y = best - q, u the clamped uniform; q + g(u) >= best needs u >= e^(-e^(-y)), and the
+      // approximate exponentials err by far less than the margin), and only survivors get the
+      // exact Gumbel value and enter the argmax.
+      auto flush = [&]() {
+        __syncwarp();
+        const float thr_now = W - GUMBEL_MAX;
+        for (int i0 = 0; i0 < nbuf; i0 += 128) {
+          // four independent Philox chains per lane (latency hiding), taken in column order
+          uint32_t wv[4];
+          float qv[4];
+          int colv[4];
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            const int i = i0 + 32 * r + lane;
+            qv[r] = i < nbuf ? wq[i] : -INFINITY;
+            colv[r] = i < nbuf ? wcol[i] : 0;
+            wv[r] = qv[r] < thr_now ? 0u : philox_w0(static_cast<uint32_t>(colv[r]), k0, k1);
+          }
+#pragma unroll
+          for (int r = 0; r < 4; ++r) {
+            if (!(qv[r] < thr_now)) {
+              const float u = fminf(fmaxf(uint_to_uniform(wv[r]), 0x1.b7cdfep-34f), 0x1.fffffcp-1f);
+              const float y = fmaxf(W, bg) - qv[r];
+              const float umin = ex2(-ex2(-y * L) * L);
+              if (u >= umin - 2e-6f) arg_merge(bg, bgi, qv[r] + gumbel_from_word(wv[r]), colv[r]);
+            }
+          }
+        }
+        __syncwarp();
+        nbuf = 0;
+        const float wm = warp_max(bg);
+        if (wm > W) {
+          W = wm;
+          if (lane == 0) {
+            atomicMax(&c.wbound, (static_cast<unsigned long long>(row) << 32) | fkey(wm));
+            atomicMax(row_bound + row, fkey(wm));  // result unused: a reduction
+          }
+        }
+      };
+      for (int c0 = c_beg; c0 < c_end; c0 += SX_COLS, ++u) {
+        const int slot = u % SX_RING;
+        bool ok = !*abort_flag;
+        if (ok && !mbar_wait(&c.full[slot], (u / SX_RING) & 1)) {
+          fail();
+          ok = false;
+        }
+        const int scols = min(SX_COLS, c_end - c0);
+        const int base = warp * SP_TILE;  // this warp's columns inside the stage
+        if (ok && base < scols) {
+          const float* sx = reinterpret_cast<const float*>(ring + slot * SX_BYTES);
+          float q[16];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int cl = base + 128 * j + 4 * lane;
+            if (cl < scols) {  // scols - cl is a multiple of 4
+              const float4 v = *reinterpret_cast<const float4*>(sx + cl);
+              q[4 * j] = v.x; q[4 * j + 1] = v.y; q[4 * j + 2] = v.z; q[4 * j + 3] = v.w;
+            } else {
+              q[4 * j] = q[4 * j + 1] = q[4 * j + 2] = q[4 * j + 3] = -INFINITY;
+            }
+          }
+          if (do_div) {
+            float xabs = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) xabs = fmaxf(xabs, fabsf(q[i]));
+            if (__all_sync(0xffffffffu, xabs <= 3.0e38f)) {  // finite: Markstein = IEEE quotient
+#pragma unroll
+              for (int i = 0; i < 16; ++i) q[i] = div_rn_by(q[i], temp, rtemp);
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) q[i] = isfinite(q[i]) ? div_rn_by(q[i], temp, rtemp) : q[i] * rtemp;
+            }
+          }
+          float tm = q[0];
+#pragma unroll
+          for (int i = 1; i < 16; ++i) tm = fmaxf(tm, q[i]);
+          const float wmx = warp_max(tm);
+          const int col0 = c0 + base + 4 * lane;  // column of q[0]; q[i] at col0 + 128*(i>>2) + (i&3)
+          if (wmx > bq || wmx > m) {  // rare: a new maximum of the item in this tile
+            int fc = 0x7fffffff, fi = -1;  // this lane's first element equal to wmx
+#pragma unroll
+            for (int i = 15; i >= 0; --i) {
+              if (q[i] == wmx) {
+                fi = i;
+                fc = col0 + 128 * (i >> 2) + (i & 3);
+              }
+            }
+            const int wfc = warp_min_i(fc);
+            if (wmx > bq) {
+              bq = wmx;
+              bqi = wfc;
+            }
+            if (wmx > m) {
+              if (m != -INFINITY) {  // move the implicit 1 to the new maximum: lane 0 takes the old one
+                const float a = ex2((m - wmx) * L);
+                t2 = a * (t2 + (m - wmx) * L * sp);
+                sp = a * sp;
+                if (lane == 0) {
+                  t2 += a * (m - wmx) * L;
+                  sp += a;
+                }
+              }
+              m = wmx;
+              m2 = wmx * L;
+              const int skip = (fc == wfc) ? fi : -1;  // the element carrying the new implicit 1
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                if (i != skip) {
+                  const float d2 = fmaxf(fmaf(q[i], L, -m2), -1000.0f);
+                  const float e = ex2(d2);
+                  sp += e;
+                  t2 = fmaf(d2, e, t2);
+                }
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const float d2 = fmaxf(fmaf(q[i], L, -m2), -1000.0f);
+                const float e = ex2(d2);
+                sp += e;
+                t2 = fmaf(d2, e, t2);
+              }
+            }
+          } else if (m != -INFINITY) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float d2 = fmaxf(fmaf(q[i], L, -m2), -1000.0f);
+              const float e = ex2(d2);
+              sp += e;
+              t2 = fmaf(d2, e, t2);
+            }
+          }
+          if (want_gumbel) {
+            if (first) {  // bootstrap the bound with each lane's tile maximum
+              first = false;
+              if (tm != -INFINITY) {
+                int im = 0;
+#pragma unroll
+                for (int i = 15; i >= 0; --i)
+                  if (q[i] == tm) im = i;
+                const int ci = col0 + 128 * (im >> 2) + (im & 3);
+                arg_merge(bg, bgi, tm + gumbel_from_word(philox_w0(static_cast<uint32_t>(ci), k0, k1)), ci);
+              }
+              W = fmaxf(W, warp_max(bg));
+            }
+            {
+              const unsigned long long sb = *reinterpret_cast<volatile unsigned long long*>(&c.wbound);
+              if (static_cast<int64_t>(sb >> 32) == row) W = fmaxf(W, fdecode(static_cast<uint32_t>(sb)));
+            }
+            const float thr = W - GUMBEL_MAX;
+            unsigned cm = 0;
+            if (!(tm < thr)) {
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (!(q[i] < thr) && q[i] != -INFINITY) cm |= 1u << i;
+            }
+            if (__any_sync(0xffffffffu, cm != 0)) {
+              const int n = __popc(cm);
+              int incl = n;
+#pragma unroll
+              for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += y;
+              }
+              const int total = __shfl_sync(0xffffffffu, incl, 31);
+              if (nbuf + total > SP_TILE) flush();
+              int pos = nbuf + incl - n;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                if (cm & (1u << i)) {
+                  wcol[pos] = col0 + 128 * (i >> 2) + (i & 3);
+                  wq[pos] = q[i];
+                  ++pos;
+                }
+              }
+              nbuf += total;
+              if (nbuf >= 32) flush();
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&c.empty[slot]);
+      }
+      if (want_gumbel && nbuf > 0) flush();
+      // ---- item result: m and the argmax are warp-uniform; sp, t2 add up in a fixed tree
+      float spw = sp, t2w = t2;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        spw += __shfl_xor_sync(0xffffffffu, spw, o);
+        t2w += __shfl_xor_sync(0xffffffffu, t2w, o);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float bgo = __shfl_xor_sync(0xffffffffu, bg, o);
+        const int bgio = __shfl_xor_sync(0xffffffffu, bgi, o);
+        arg_merge(bg, bgi, bgo, bgio);
+      }
+      if (lane == 0) {
+        const int b = k & 1;
+        if (!*abort_flag && !mbar_wait(&c.pempty[b], ((k >> 1) & 1) ^ 1, 2000000000ull, 32)) fail();
+        Part pt;
+        pt.m = m; pt.s = spw; pt.t = t2w * 0.6931471805599453f; pt.bq = bq; pt.bqi = bqi;
+        pt.bg = bg; pt.bgi = bgi; pt.pad = 0.f;
+        if (m == -INFINITY) { pt.s = 0.f; pt.t = 0.f; }
+        s_wpart[b][warp] = pt;
+        mbar_arrive(&c.pfull[b]);
+      }
+      __syncwarp();
+    }
+    if (lane == 0) atomicAdd(&c.done, 1);
+  }
+  __syncthreads();
+}
+
+// Finishes each row from its chunk partials, merged in chunk order (one thread per row).
+__global__ void row_merge_kernel(const Part* __restrict__ parts, int64_t rows, int nchunks,
+                                 float* __restrict__ entropy, int64_t* __restrict__ samp,
+                                 int64_t* __restrict__ amax) {
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  const Part* pr = parts + row * nchunks;
+  Part acc = pr[0];
+  for (int ch = 1; ch < nchunks; ++ch) {
+    const Part p = pr[ch];
+    sm_merge(acc.m, acc.s, acc.t, p.m, p.s, p.t);
+    arg_merge(acc.bq, acc.bqi, p.bq, p.bqi);
+    arg_merge(acc.bg, acc.bgi, p.bg, p.bgi);
+  }
+  if (entropy) entropy[row] = log1pf(acc.s) - acc.t / (1.0f + acc.s);
+  if (amax) amax[row] = acc.bqi;
+  if (samp) samp[row] = acc.bgi;
+}
+
+// ------------------------------------------------------------------------------------------
 // Acceptance mask + stop test, one CTA per batch row, one thread per canvas position.
 __global__ void __launch_bounds__(1024)
     accept_stop_kernel(const float* __restrict__ ent, const int64_t* __restrict__ cur,
@@ -430,7 +836,30 @@ extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, f
   uint32_t* ticket = reinterpret_cast<uint32_t*>(ws + o_ticket);
   uint32_t* bound = reinterpret_cast<uint32_t*>(ws + o_bound);
   int* counter = reinterpret_cast<int*>(ws + o_counter);
-  if (vec) {
+  if (vec && (ccols % 4) == 0) {
+    // streaming kernel: one persistent CTA per SM, static item assignment
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+      if (cudaFuncSetAttribute(sampler_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(SX_SMEM)) != cudaSuccess)
+        return KNX_E_DEVICE;
+      attr[dev & 63] = true;
+    }
+    // quarter-row items (the workspace holds rows * nch >= rows * nch_s partials)
+    const int nch_s = static_cast<int>((V + SX_CHUNK - 1) / SX_CHUNK);
+    const int64_t sitems = rows * nch_s;
+    const int64_t sms = num_sms();
+    const int sgrid = static_cast<int>(sitems < sms ? sitems : sms);
+    int* dev_err = counter + 1;  // workspace word next to the counter, zeroed above
+    sampler_stream_kernel<<<sgrid, SX_THREADS, SX_SMEM, s>>>(
+        logits, rows, static_cast<int>(V), temperature, rtemp, do_div, seed, seed_is32, want_g,
+        nch_s, parts, bound, dev_err);
+    if (cudaGetLastError() != cudaSuccess) return KNX_E_LAUNCH;
+    row_merge_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, s>>>(parts, rows, nch_s,
+                                                                             entropy, samp, amax);
+  } else if (vec) {
     sampler_kernel<true><<<grid, SP_THREADS, 0, s>>>(logits, rows, static_cast<int>(V),
                                                      temperature, rtemp, do_div, seed, seed_is32,
                                                      want_g, nch, ccols, parts, ticket, bound,
