@@ -175,6 +175,88 @@ def time_layer_e2e(dev, steps, warmup):
     return ev0.elapsed_time(ev1), host_in.numel() * 2, host_out.numel() * 2
 
 
+class EpLayer:
+    """N > 1: the same configs[1] layer with the 128 experts sharded over the ranks (expert
+    parallelism, NCCL all-to-all dispatch/return); each rank runs its own 256-token canvas."""
+
+    def __init__(self, dev, rank, world):
+        import ep_moe
+        import workloads
+        self.layers = []
+        for i in range(NSETS):
+            Wf = workloads.moe_weights(E, H, I, seed=100 + i, device=dev)
+            local = ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"], Wf["gu_z"], Wf["dn_q"],
+                                         Wf["dn_s"], Wf["dn_z"], rank, world)
+            del Wf
+            self.layers.append(ep_moe.ExpertParallelMoE(*local, E_total=E, int_zeros=False))
+        torch.cuda.empty_cache()
+        self.inp = workloads.moe_inputs(T, H, E, seed=rank, device=dev)  # this rank's canvas
+        self.xp = torch.empty(T, H, dtype=torch.float16, device=dev)
+        self.tpe = T * TOPK * world // E  # job-wide pairs per expert (engine choice)
+
+    def step(self, i, hidden=None):
+        import fused_rmsnorm
+        import moe_router
+        inp = self.inp
+        x = inp["hidden"] if hidden is None else hidden
+        y_norm = fused_rmsnorm.fused_rmsnorm(x, inp["norm_w"], 1e-6, xperm=self.xp)
+        ids, w, _ = moe_router.route_topk(y_norm, inp["router_w"], TOPK, bias=inp["bias"],
+                                          want_logits=False)
+        return self.layers[i % NSETS](self.xp, ids, w, out_dtype=torch.float16,
+                                      tokens_per_expert=self.tpe), ids
+
+
+EP_LAUNCHES_PER_LAYER = 11  # rmsnorm, router x2, align, gather, layout, task list, gate_up, down,
+                            # gather, combine (plus three NCCL all-to-alls)
+
+
+def time_layer_ep(dev, steps, warmup, rank, world):
+    ep = EpLayer(dev, rank, world)
+    for i in range(warmup):
+        ep.step(i)
+    torch.cuda.synchronize(dev)
+    _, ids = ep.step(0)
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    torch.distributed.all_reduce(counts)
+    counts = counts.cpu()
+    torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    clk = Clocks(dev.index)
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(steps):
+        ep.step(i)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    torch.distributed.barrier()
+    clocks = clk.stop()
+    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    # end to end: the canvas from pinned host memory, the layer output back, every step
+    host_in = ep.inp["hidden"].cpu().pin_memory()
+    host_out = torch.empty(T, H, dtype=torch.float16).pin_memory()
+    dev_in = torch.empty_like(ep.inp["hidden"])
+    for i in range(warmup):
+        dev_in.copy_(host_in, non_blocking=True)
+        y, _ = ep.step(i, dev_in)
+        host_out.copy_(y, non_blocking=True)
+    torch.cuda.synchronize(dev)
+    torch.distributed.barrier()
+    ev0.record()
+    for i in range(steps):
+        dev_in.copy_(host_in, non_blocking=True)
+        y, _ = ep.step(i, dev_in)
+        host_out.copy_(y, non_blocking=True)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    return ms, counts, clocks, e2e_ms, host_in.numel() * 2, host_out.numel() * 2
+
+
 def time_sampler(dev, reps=1):
     """48 denoising steps with the temperature schedule; per step one fused pass
     (entropy + Gumbel-max + argmax) and one acceptance/stop launch."""
@@ -303,7 +385,12 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
-    ms, stages, counts, clocks = time_layer(dev, args.steps, args.warmup, dist)
+    if dist:
+        ms, counts, clocks, e2e_ms, h2d, d2h = time_layer_ep(dev, args.steps, args.warmup, rank,
+                                                             world)
+        stages = {}
+    else:
+        ms, stages, counts, clocks = time_layer(dev, args.steps, args.warmup, dist)
     ms_step = ms / args.steps
     value = ms * 1000.0 / (args.steps * world)
     import workloads
@@ -311,8 +398,9 @@ def main():
     touched = int((counts > 0).sum())
     bytes_layer = workloads.moe_layer_bytes(counts.numpy())
     gemm1_bytes = touched * (2 * I * H // 2 + 2 * I * (H // 128) * 4) + T * H * 2
-    gemm1_ms = stages["gate_up_gelu"]
-    e2e_ms, h2d, d2h = time_layer_e2e(dev, args.steps, args.warmup)
+    gemm1_ms = stages.get("gate_up_gelu")
+    if not dist:
+        e2e_ms, h2d, d2h = time_layer_e2e(dev, args.steps, args.warmup)
     samp_step_ms, samp_kern_ms = time_sampler(dev)
     if dist:
         torch.distributed.barrier()
@@ -326,7 +414,8 @@ def main():
         cpu = {"value": us, "unit": "us", "cores": ncores, "kind": "port",
                "sample": "one layer: RMSNorm+router on all 256 tokens, MoE on experts e%16==0 "
                          "(dequant inside the timed region) scaled x16"}
-    achieved = gemm1_bytes / (gemm1_ms * 1e-3) / 1e9
+    # the kernel roofline is the single-GPU layer's (per-stage events exist only there)
+    achieved = gemm1_bytes / (gemm1_ms * 1e-3) / 1e9 if gemm1_ms else None
     engine = os.environ.get("KNX_ENGINE", "auto")
     if engine == "auto":  # the library's rule: ws up to 64 pairs per expert, tcgen05 above
         engine = "ws" if T * TOPK // E <= 64 else "tc"
@@ -337,14 +426,18 @@ def main():
         "config": {"workload": "configs[1]: RMSNorm -> router (Zipf bias) -> W4A16 MoE layer, "
                                "T=256 H=2816 I=704 E=128 top-8, gate_up gs128 / down gs64",
                    "l2": f"{NSETS} rotating weight sets ({NSETS} x 416 MB) > 126 MB L2",
-                   "parallelism": f"replicas x{world}", "touched_experts": touched,
+                   "parallelism": (f"expert-parallel x{world} (128/{world} experts per GPU, "
+                                   f"one 256-token canvas per GPU, NCCL all-to-all)"
+                                   if world > 1 else "single GPU"),
+                   "touched_experts": touched,
                    "max_tokens_per_expert": int(counts.max())},
         "layer_hbm_gbs": bytes_layer / (ms_step * 1e-3) / 1e9,
-        "layer_hbm_frac": bytes_layer / (ms_step * 1e-3) / 1e9 / peak,
+        "layer_hbm_frac": bytes_layer / (ms_step * 1e-3) / 1e9 / (peak * world),
         "layer_bytes": bytes_layer,
         "stages_us": {k: v * 1000.0 for k, v in stages.items()},
         "roofline": {"kernel": GEMM1_KERNEL[engine], "bound": "hbm", "achieved": achieved,
-                     "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                     "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak if achieved else None,
                      "peak_kind": peak_kind, "traffic": GEMM1_NCU_TRAFFIC.get(engine),
                      "algorithmic_bytes": gemm1_bytes},
         "sampler_step_us": samp_step_ms * 1000.0,
@@ -353,9 +446,9 @@ def main():
                              "peak": peak, "unit": "GB/s",
                              "frac": 256 * V_SAMPLER * 4 / (samp_kern_ms * 1e-3) / 1e9 / peak,
                              "kernel_us": samp_kern_ms * 1000.0},
-        "e2e": {"value": e2e_ms * 1000.0 / args.steps, "unit": "us", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
-        "gpu_launches": LAUNCHES_PER_LAYER * args.steps,
+        "e2e": {"value": e2e_ms * 1000.0 / (args.steps * world), "unit": "us",
+                "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world},
+        "gpu_launches": (EP_LAUNCHES_PER_LAYER if dist else LAUNCHES_PER_LAYER) * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }

@@ -137,6 +137,41 @@ KNX_API int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidden_d
                int gs_dn, int flags, void* workspace, size_t workspace_bytes, void* out,
                int32_t* err, void* stream);
 
+/* ---- expert parallelism (experts sharded over ranks, tokens data-parallel) ------------------
+ * No counterpart in the reference (single-GPU only).  The host drives, between two NCCL
+ * all-to-all exchanges: knx_moe_align on the global expert ids (the single-GPU slot order),
+ * knx_gather_rows (dispatch rows in that order), knx_ep_layout + knx_moe_w4_grouped on each
+ * expert rank, knx_gather_rows (rows back to receive order), knx_moe_combine on the source.
+ * The result is bit-identical to knx_moe_w4 on one GPU when tokens_per_expert (the job-wide
+ * average, which picks the engine) is the same.  The combine order follows
+ * fused_moe_w4_v2.py:248-263.
+ *
+ * knx_gather_rows: dst[i, :] = src[idx[i] / div, :] for i < n (idx[i] < 0: a zero row);
+ *   row_bytes % 16 == 0, src/dst 16-byte aligned.
+ * knx_ep_layout: received rows arrive grouped by source s (rank order), then by local expert e,
+ *   then in the source's slot order; recv_counts[s * El + e] (device int32) holds the counts.
+ *   Writes offsets[El + 1] (slots per local expert, expert-major), rows[R] (slot -> received row)
+ *   and inv[R] (received row -> slot), R = sum of recv_counts.  S <= 64, El <= 256.
+ * knx_moe_w4_grouped: gate_up + GELU and down for R rows grouped by expert: slot i of expert e
+ *   (offsets[e] <= i < offsets[e+1]) multiplies row rows[i] of xrows (f16, MoE K-interleave;
+ *   rows NULL = row i); out3[i, :] f16.  Weights, group sizes and flags as knx_moe_w4 (E = the
+ *   local expert count); tokens_per_expert picks the engine.
+ * knx_moe_combine: out[t, :] = sum_{k fixed order} w[t,k] * out3[inv[t*topk+k], :] (inv < 0:
+ *   skipped), as in knx_moe_w4. */
+KNX_API int knx_gather_rows(const void* src, int64_t src_rows, int64_t row_bytes, const int32_t* idx,
+                            int div, int64_t n, void* dst, void* stream);
+KNX_API int knx_ep_layout(const int32_t* recv_counts, int S, int El, int64_t R, int32_t* offsets,
+                          int32_t* rows, int32_t* inv, void* stream);
+KNX_API size_t knx_moe_w4_grouped_workspace_size(int64_t R, int64_t H, int64_t I, int E);
+KNX_API int knx_moe_w4_grouped(const void* xrows, const int32_t* rows, int64_t R,
+                               const int32_t* offsets, const uint8_t* gu_q, const void* gu_s,
+                               const void* gu_z, const uint8_t* dn_q, const void* dn_s,
+                               const void* dn_z, int64_t H, int64_t I, int E, int gs_gu, int gs_dn,
+                               int flags, int64_t tokens_per_expert, void* workspace,
+                               size_t workspace_bytes, void* out3, int32_t* err, void* stream);
+KNX_API int knx_moe_combine(const void* out3, const int32_t* inv, const void* topk_w, int w_dtype,
+                            int64_t T, int topk, int64_t H, int out_dtype, void* out, void* stream);
+
 /* ---- dense W4A16 linear -------------------------------------------------------------------
  * Replaces w4a16_linear (w4a16.py:96-108):  Y[M,N] = X[M,K] . dequant(q,s,z)^T, f16 out.
  * X: f16 [M,K] row-major; q u8 [N,K/2]; s,z f16 [N,K/gs].  K % 64 == 0, gs % 32 == 0, gs | K,

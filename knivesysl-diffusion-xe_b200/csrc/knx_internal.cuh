@@ -43,6 +43,36 @@ int launch_hw_rows(const __half* act, int64_t act_stride, int K, const int32_t* 
                    int gs, bool zint, __half* out, int64_t out_stride, int64_t max_tasks,
                    int32_t* err, cudaStream_t s);
 
+// The grouped expert GEMMs of one MoE layer over a task list (knx_moe.cu).
+struct GemmArgs {
+  const __half* xp;           // activation rows (K-interleaved f16)
+  const int32_t* sorted_pair; // slot -> activation row * topk (+ k); NULL = row = slot
+  int topk;
+  const int32_t* offsets;     // [E + 1] slot offsets per expert
+  const int4* tasks;
+  const int32_t* ntasks;
+  int32_t* counters;          // two work counters, zero at entry
+  const uint8_t* gu_q;
+  const __half* gu_s;
+  const __half* gu_z;
+  const uint8_t* dn_q;
+  const __half* dn_s;
+  const __half* dn_z;
+  int E;
+  int64_t H, I;
+  int gs_gu, gs_dn;
+  bool zint;
+  __half* out2;  // [pairs][I] f16 (K-interleaved)
+  __half* out3;  // [pairs][H] f16
+  int64_t pairs;
+  int32_t* err;
+};
+int moe_engine(int flags, int64_t tokens_per_expert, int64_t H, int64_t I, int gs_gu, int gs_dn);
+int engine_task_tokens(int eng);
+int run_moe_gemms(const GemmArgs& a, int eng, int pc, cudaStream_t s);
+int launch_combine(const __half* out3, const int32_t* inv, const void* w, int w_dtype, int64_t T,
+                   int topk, int64_t H, int out_dtype, void* out, cudaStream_t s);
+
 namespace prof {
 int begin_call();                                  // -1 when stage recording is off
 void mark(int call, int slot, cudaStream_t stream);  // record boundary `slot` of call `call`

@@ -533,7 +533,92 @@ bool set_smem_attrs() {
 }
 
 }  // namespace
+// Engine of a call after the shape checks: tcgen05 / the warp-specialised mma.sync kernels where
+// they support the shape, else the plain mma.sync kernels.
+int moe_engine(int flags, int64_t tokens_per_expert, int64_t H, int64_t I, int gs_gu, int gs_dn) {
+  const int ng1 = static_cast<int>(H / gs_gu), ng2 = static_cast<int>(I / gs_dn);
+  const int eng = engine_choice(flags, tokens_per_expert);
+  if (eng == KNX_W4_WARP_WS && hw_supported(H, gs_gu, ng1, 2 * I, true) &&
+      hw_supported(I, gs_dn, ng2, H, false))
+    return KNX_W4_WARP_WS;
+  if (eng != KNX_W4_WARP_MMA && tc_supported(H, gs_gu, ng1, 2 * I, true) &&
+      tc_supported(I, gs_dn, ng2, H, false))
+    return KNX_W4_TCGEN05;
+  return KNX_W4_WARP_MMA;
+}
+
+int engine_task_tokens(int eng) {
+  return eng == KNX_W4_TCGEN05 ? TC_TASK_TOKENS : eng == KNX_W4_WARP_WS ? HW_TASK_TOKENS : M_MAX;
+}
+
+// gate_up + GELU then down over the task list (stage mark 2 between the two GEMMs).
+int run_moe_gemms(const GemmArgs& a, int eng, int pc, cudaStream_t s) {
+  const int tt = engine_task_tokens(eng);
+  const int64_t max_tasks = (a.pairs + tt - 1) / tt + a.E;
+  const int ng1 = static_cast<int>(a.H / a.gs_gu), ng2 = static_cast<int>(a.I / a.gs_dn);
+  const int H = static_cast<int>(a.H), I = static_cast<int>(a.I);
+  int st;
+  if (eng == KNX_W4_TCGEN05) {
+    st = launch_tc_gateup(a.xp, a.sorted_pair, a.topk, a.offsets, a.tasks, a.ntasks, a.counters,
+                          a.gu_q, a.gu_s, a.gu_z, a.E, H, I, ng1, a.gs_gu, a.zint, a.out2,
+                          max_tasks, a.err, s);
+    if (st != KNX_OK) return st;
+    prof::mark(pc, 2, s);
+    return launch_tc_rows(a.out2, I, I, a.offsets, a.tasks, a.ntasks, 0, a.counters + 1, a.dn_q,
+                          a.dn_s, a.dn_z, a.E, H, ng2, a.gs_dn, a.zint, a.out3, H, max_tasks,
+                          a.err, s);
+  }
+  if (eng == KNX_W4_WARP_WS) {
+    st = launch_hw_gateup(a.xp, a.sorted_pair, a.topk, a.offsets, a.tasks, a.ntasks, a.counters,
+                          a.gu_q, a.gu_s, a.gu_z, a.E, H, I, ng1, a.gs_gu, a.zint, a.out2,
+                          max_tasks, a.err, s);
+    if (st != KNX_OK) return st;
+    prof::mark(pc, 2, s);
+    return launch_hw_rows(a.out2, I, I, a.offsets, a.tasks, a.ntasks, 0, a.counters + 1, a.dn_q,
+                          a.dn_s, a.dn_z, a.E, H, ng2, a.gs_dn, a.zint, a.out3, H, max_tasks,
+                          a.err, s);
+  }
+  if (!set_smem_attrs()) return KNX_E_DEVICE;
+  const int sms = num_sms();
+  {
+    const int64_t work = max_tasks * (I / G1_ROWS);
+    const int grid = static_cast<int>(work < sms ? work : sms);
+    auto kern = a.zint ? gateup_gelu_kernel<true> : gateup_gelu_kernel<false>;
+    kern<<<grid, THREADS, g1_smem(ng1), s>>>(a.xp, a.sorted_pair, a.topk, a.offsets, a.tasks,
+                                             a.ntasks, a.counters, a.gu_q, a.gu_s, a.gu_z, H, I,
+                                             ng1, a.gs_gu, a.out2);
+    st = launch_status();
+    if (st != KNX_OK) return st;
+  }
+  prof::mark(pc, 2, s);
+  {
+    const int64_t work = max_tasks * ((H + G2_ROWS - 1) / G2_ROWS);
+    const int grid = static_cast<int>(work < 2 * sms ? work : 2 * sms);
+    auto kern = a.zint ? rows_gemm_kernel<true> : rows_gemm_kernel<false>;
+    kern<<<grid, THREADS, g2_smem(ng2), s>>>(a.out2, I, I, a.offsets, a.tasks, a.ntasks, 0,
+                                             a.counters + 1, a.dn_q, a.dn_s, a.dn_z, H, ng2,
+                                             a.gs_dn, a.out3, H);
+    return launch_status();
+  }
+}
+
+int launch_combine(const __half* out3, const int32_t* inv, const void* w, int w_dtype, int64_t T,
+                   int topk, int64_t H, int out_dtype, void* out, cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>((H / 8 + 255) / 256), static_cast<unsigned>(T));
+  if (out_dtype == KNX_F16) {
+    combine_kernel<__half><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, static_cast<int>(H),
+                                                static_cast<__half*>(out));
+  } else {
+    combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk,
+                                                       static_cast<int>(H),
+                                                       static_cast<__nv_bfloat16*>(out));
+  }
+  return launch_status();
+}
+
 }  // namespace knx
+
+
 
 // ------------------------------------------------------------------------------------------
 extern "C" size_t knx_moe_w4_workspace_size(int64_t T, int64_t H, int64_t I, int E, int topk) {
@@ -581,83 +666,23 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
     if (st != KNX_OK) return st;
     xp = w.xp;
   }
-  const int eng = engine_choice(flags, T * topk / E);
-  const bool use_ws = eng == KNX_W4_WARP_WS && hw_supported(H, gs_gu, ng1, 2 * I, true) &&
-                      hw_supported(I, gs_dn, ng2, H, false);
-  const bool use_tc = !use_ws && eng != KNX_W4_WARP_MMA &&
-                      tc_supported(H, gs_gu, ng1, 2 * I, true) &&
-                      tc_supported(I, gs_dn, ng2, H, false);
-  const int task_tokens = use_tc ? TC_TASK_TOKENS : use_ws ? HW_TASK_TOKENS : M_MAX;
-  st = launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0, task_tokens, w.counts,
-                    w.offsets, w.sorted_pair, w.inv, nullptr, nullptr, nullptr, w.tasks, w.ntasks,
-                    w.counters, 2, err, s);
+  const int eng = moe_engine(flags, T * topk / E, H, I, gs_gu, gs_dn);
+  st = launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0, engine_task_tokens(eng),
+                    w.counts, w.offsets, w.sorted_pair, w.inv, nullptr, nullptr, nullptr, w.tasks,
+                    w.ntasks, w.counters, 2, err, s);
   if (st != KNX_OK) return st;
-  const int64_t N = T * topk;
-  const int64_t max_tasks = (N + task_tokens - 1) / task_tokens + E;
-  const int sms = num_sms();
   prof::mark(pc, 1, s);
-  if (use_tc) {
-    st = launch_tc_gateup(xp, w.sorted_pair, topk, w.offsets, w.tasks, w.ntasks, w.counters, gu_q,
-                          static_cast<const __half*>(gu_s), static_cast<const __half*>(gu_z), E,
-                          static_cast<int>(H), static_cast<int>(I), ng1, gs_gu, zint, w.out2,
-                          max_tasks, err, s);
-    if (st != KNX_OK) return st;
-    prof::mark(pc, 2, s);
-    st = launch_tc_rows(w.out2, I, static_cast<int>(I), w.offsets, w.tasks, w.ntasks, 0,
-                        w.counters + 1, dn_q, static_cast<const __half*>(dn_s),
-                        static_cast<const __half*>(dn_z), E, static_cast<int>(H), ng2, gs_dn, zint,
-                        w.out3, H, max_tasks, err, s);
-    if (st != KNX_OK) return st;
-  } else if (use_ws) {
-    st = launch_hw_gateup(xp, w.sorted_pair, topk, w.offsets, w.tasks, w.ntasks, w.counters, gu_q,
-                          static_cast<const __half*>(gu_s), static_cast<const __half*>(gu_z), E,
-                          static_cast<int>(H), static_cast<int>(I), ng1, gs_gu, zint, w.out2,
-                          max_tasks, err, s);
-    if (st != KNX_OK) return st;
-    prof::mark(pc, 2, s);
-    st = launch_hw_rows(w.out2, I, static_cast<int>(I), w.offsets, w.tasks, w.ntasks, 0,
-                        w.counters + 1, dn_q, static_cast<const __half*>(dn_s),
-                        static_cast<const __half*>(dn_z), E, static_cast<int>(H), ng2, gs_dn, zint,
-                        w.out3, H, max_tasks, err, s);
-    if (st != KNX_OK) return st;
-  } else {
-  {
-    const int64_t work = max_tasks * (I / G1_ROWS);
-    const int grid = static_cast<int>(work < sms ? work : sms);
-    auto kern = zint ? gateup_gelu_kernel<true> : gateup_gelu_kernel<false>;
-    kern<<<grid, THREADS, g1_smem(ng1), s>>>(
-        xp, w.sorted_pair, topk, w.offsets, w.tasks, w.ntasks, w.counters,
-        gu_q, static_cast<const __half*>(gu_s), static_cast<const __half*>(gu_z),
-        static_cast<int>(H), static_cast<int>(I), ng1, gs_gu, w.out2);
-    st = launch_status();
-    if (st != KNX_OK) return st;
-  }
-  prof::mark(pc, 2, s);
-  {
-    const int64_t work = max_tasks * ((H + G2_ROWS - 1) / G2_ROWS);
-    const int grid = static_cast<int>(work < 2 * sms ? work : 2 * sms);
-    auto kern = zint ? rows_gemm_kernel<true> : rows_gemm_kernel<false>;
-    kern<<<grid, THREADS, g2_smem(ng2), s>>>(
-        w.out2, I, static_cast<int>(I), w.offsets, w.tasks, w.ntasks, 0, w.counters + 1, dn_q,
-        static_cast<const __half*>(dn_s), static_cast<const __half*>(dn_z), static_cast<int>(H),
-        ng2, gs_dn, w.out3, H);
-    st = launch_status();
-    if (st != KNX_OK) return st;
-  }
-  }
+  GemmArgs ga{};
+  ga.xp = xp; ga.sorted_pair = w.sorted_pair; ga.topk = topk; ga.offsets = w.offsets;
+  ga.tasks = w.tasks; ga.ntasks = w.ntasks; ga.counters = w.counters;
+  ga.gu_q = gu_q; ga.gu_s = static_cast<const __half*>(gu_s); ga.gu_z = static_cast<const __half*>(gu_z);
+  ga.dn_q = dn_q; ga.dn_s = static_cast<const __half*>(dn_s); ga.dn_z = static_cast<const __half*>(dn_z);
+  ga.E = E; ga.H = H; ga.I = I; ga.gs_gu = gs_gu; ga.gs_dn = gs_dn; ga.zint = zint;
+  ga.out2 = w.out2; ga.out3 = w.out3; ga.pairs = T * topk; ga.err = err;
+  st = run_moe_gemms(ga, eng, pc, s);
+  if (st != KNX_OK) return st;
   prof::mark(pc, 3, s);
-  {
-    const dim3 grid(static_cast<unsigned>((H / 8 + 255) / 256), static_cast<unsigned>(T));
-    if (hidden_dtype == KNX_F16) {
-      combine_kernel<__half><<<grid, 256, 0, s>>>(w.out3, w.inv, topk_w, w_dtype, topk,
-                                                  static_cast<int>(H), static_cast<__half*>(out));
-    } else {
-      combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
-          w.out3, w.inv, topk_w, w_dtype, topk, static_cast<int>(H),
-          static_cast<__nv_bfloat16*>(out));
-    }
-    st = launch_status();
-  }
+  st = launch_combine(w.out3, w.inv, topk_w, w_dtype, T, topk, H, hidden_dtype, out, s);
   prof::mark(pc, 4, s);
   return st;
 }

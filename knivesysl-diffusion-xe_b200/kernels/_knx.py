@@ -63,6 +63,12 @@ _SIGS = {
     "knx_sampler_fused_static": (_i32, [_vp, _i64, _i64, _f32, _i64, _vp, _vp, _vp, _vp]),
     "knx_accept_stop": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp, _i32, _f32,
                                _vp, _vp]),
+    "knx_gather_rows": (_i32, [_vp, _i64, _i64, _vp, _i32, _i64, _vp, _vp]),
+    "knx_ep_layout": (_i32, [_vp, _i32, _i32, _i64, _vp, _vp, _vp, _vp]),
+    "knx_moe_w4_grouped_workspace_size": (_sz, [_i64, _i64, _i64, _i32]),
+    "knx_moe_w4_grouped": (_i32, [_vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                                  _i32, _i32, _i32, _i32, _i64, _vp, _sz, _vp, _vp, _vp]),
+    "knx_moe_combine": (_i32, [_vp, _vp, _vp, _i32, _i64, _i32, _i64, _i32, _vp, _vp]),
     "knx_prof_start": (_i32, [_i32]),
     "knx_prof_stop": (_i32, [_vp, _i32, _vp]),
 }
