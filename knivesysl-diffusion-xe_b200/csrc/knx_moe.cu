@@ -427,7 +427,10 @@ __global__ void __launch_bounds__(THREADS, 2)
 // ------------------------------------------------------------------------------------------
 // Fixed-order combine (fused_moe_w4_v2.py:248-263): y[t] = sum_{k in order} w[t,k]*out3[inv[t,k]],
 // fp32 accumulate, one rounding to the output dtype.  Dropped pairs (inv < 0) contribute 0.
-template <typename TO>
+// y[t, 8 channels] = sum_{k in order} w[t,k] * f32(out3[inv[t*topk+k], 8 channels]).  TK > 0
+// fixes topk at compile time so the TK row loads are all in flight before the sums (TK = 0: any
+// topk, loop).  Same arithmetic and order in both forms.
+template <typename TO, int TK>
 __global__ void __launch_bounds__(256)
     combine_kernel(const __half* __restrict__ out3, const int32_t* __restrict__ inv,
                    const void* __restrict__ w, int w_dtype, int topk, int H,
@@ -436,17 +439,35 @@ __global__ void __launch_bounds__(256)
   const int v = blockIdx.x * blockDim.x + threadIdx.x;  // 8-channel vector index
   if (v * 8 >= H) return;
   float acc[8] = {};
-  for (int k = 0; k < topk; ++k) {
-    const int s = inv[static_cast<int64_t>(t) * topk + k];
-    if (s < 0) continue;
-    const float wk = load_as_float(w, w_dtype, static_cast<int64_t>(t) * topk + k);
-    const uint4 raw = *reinterpret_cast<const uint4*>(out3 + static_cast<int64_t>(s) * H + v * 8);
+  auto add = [&](float wk, const uint4& raw) {
     const __half2* h = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const float2 f = __half22float2(h[i]);
       acc[2 * i] = fmaf(wk, f.x, acc[2 * i]);
       acc[2 * i + 1] = fmaf(wk, f.y, acc[2 * i + 1]);
+    }
+  };
+  if constexpr (TK > 0) {
+    uint4 raw[TK];
+    float wk[TK];
+#pragma unroll
+    for (int k = 0; k < TK; ++k) {
+      const int s = inv[static_cast<int64_t>(t) * TK + k];
+      wk[k] = s < 0 ? 0.f : load_as_float(w, w_dtype, static_cast<int64_t>(t) * TK + k);
+      raw[k] = s < 0 ? make_uint4(0, 0, 0, 0)
+                     : *reinterpret_cast<const uint4*>(out3 + static_cast<int64_t>(s) * H + v * 8);
+    }
+#pragma unroll
+    for (int k = 0; k < TK; ++k) {
+      if (inv[static_cast<int64_t>(t) * TK + k] >= 0) add(wk[k], raw[k]);
+    }
+  } else {
+    for (int k = 0; k < topk; ++k) {
+      const int s = inv[static_cast<int64_t>(t) * topk + k];
+      if (s < 0) continue;
+      const float wk = load_as_float(w, w_dtype, static_cast<int64_t>(t) * topk + k);
+      add(wk, *reinterpret_cast<const uint4*>(out3 + static_cast<int64_t>(s) * H + v * 8));
     }
   }
   TO o[8];
@@ -605,13 +626,15 @@ int run_moe_gemms(const GemmArgs& a, int eng, int pc, cudaStream_t s) {
 int launch_combine(const __half* out3, const int32_t* inv, const void* w, int w_dtype, int64_t T,
                    int topk, int64_t H, int out_dtype, void* out, cudaStream_t s) {
   const dim3 grid(static_cast<unsigned>((H / 8 + 255) / 256), static_cast<unsigned>(T));
+  const int Hi = static_cast<int>(H);
   if (out_dtype == KNX_F16) {
-    combine_kernel<__half><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, static_cast<int>(H),
-                                                static_cast<__half*>(out));
+    __half* o = static_cast<__half*>(out);
+    if (topk == 8) combine_kernel<__half, 8><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, Hi, o);
+    else combine_kernel<__half, 0><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, Hi, o);
   } else {
-    combine_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk,
-                                                       static_cast<int>(H),
-                                                       static_cast<__nv_bfloat16*>(out));
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+    if (topk == 8) combine_kernel<__nv_bfloat16, 8><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, Hi, o);
+    else combine_kernel<__nv_bfloat16, 0><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, Hi, o);
   }
   return launch_status();
 }

@@ -1,15 +1,18 @@
 // knx_rmsnorm.cu — single-launch RMSNorm (replaces fused_rmsnorm.py:10-32).
 //
-// One warp per row.  A row is read once with 16-byte loads and kept in registers (up to
-// RMS_MAX_VEC vectors per lane, 4096 16-bit elements per row); wider rows are re-read from L2
-// for the second pass.  Math is fp32: ms = sum(x^2)/cols + eps, y = x * (1/sqrt(ms)) * w.
-// HBM-bound: 2 * rows * cols * 2 bytes + cols * 2 bytes of weight per launch.
+// One warp per row, two rows per CTA (a 256-row canvas spreads over 128 SMs).  A row is read
+// once with 16-byte loads and kept in registers (up to RMS_MAX_VEC vectors per lane, 4096 16-bit
+// elements per row); wider rows are re-read from L2 for the second pass.  The weight is read with
+// 16-byte loads in its own dtype.  Math is fp32: ms = sum(x^2)/cols + eps,
+// y = x * (1/sqrt(ms)) * w.  HBM-bound: 2 * rows * cols * 2 bytes + cols * 2 bytes of weight.
+#include <type_traits>
+
 #include "knx_common.cuh"
 
 namespace knx {
 namespace {
 
-constexpr int RMS_WARPS = 8;
+constexpr int RMS_WARPS = 2;
 constexpr int RMS_MAX_VEC = 16;  // 16 lanes-vectors * 8 elements * 32 lanes = 4096 elements
 
 template <typename T>
@@ -35,6 +38,21 @@ KNX_DEVINL void unpack8<__nv_bfloat16>(const uint4& v, float (&f)[8]) {
   }
 }
 
+// Eight weights starting at element 8v, as fp32 (WT = void: no weight, all ones).
+template <typename WT>
+KNX_DEVINL void load_w8(const void* w, int v, float (&f)[8]) {
+  if constexpr (std::is_same<WT, void>::value) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] = 1.0f;
+  } else if constexpr (std::is_same<WT, float>::value) {
+    const float4* p = reinterpret_cast<const float4*>(w) + 2 * v;
+    const float4 a = __ldg(p), b = __ldg(p + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    unpack8<WT>(__ldg(reinterpret_cast<const uint4*>(w) + v), f);
+  }
+}
+
 template <typename T>
 KNX_DEVINL T from_f32(float v, bool round_bf16) {
   if (round_bf16) v = __bfloat162float(__float2bfloat16_rn(v));
@@ -45,9 +63,9 @@ KNX_DEVINL T from_f32(float v, bool round_bf16) {
   }
 }
 
-template <typename T>
+template <typename T, typename WT>
 __global__ void __launch_bounds__(RMS_WARPS * 32)
-    rmsnorm_kernel(const T* __restrict__ x, const void* __restrict__ w, int w_dtype,
+    rmsnorm_kernel(const T* __restrict__ x, const void* __restrict__ w,
                    T* __restrict__ y, __half* __restrict__ xperm, int64_t rows, int cols,
                    float eps, bool round_bf16) {
   const int lane = threadIdx.x & 31;
@@ -81,13 +99,14 @@ __global__ void __launch_bounds__(RMS_WARPS * 32)
   uint4* yr = reinterpret_cast<uint4*>(y + row * cols);
   uint4* pr = xperm ? reinterpret_cast<uint4*>(xperm + row * cols) : nullptr;
   auto emit = [&](int v, const uint4& c) {
-    float f[8];
+    float f[8], wf[8];
     unpack8<T>(c, f);
+    load_w8<WT>(w, v, wf);
     T out[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float t = __fmul_rn(f[j], inv);
-      if (w != nullptr) t = __fmul_rn(t, load_as_float(w, w_dtype, static_cast<int64_t>(v) * 8 + j));
+      if constexpr (!std::is_same<WT, void>::value) t = __fmul_rn(t, wf[j]);
       out[j] = from_f32<T>(t, round_bf16);
     }
     yr[v] = *reinterpret_cast<uint4*>(out);
@@ -129,16 +148,23 @@ extern "C" int knx_rmsnorm(const void* x, const void* w, int w_dtype, void* y, v
   if (!aligned(x, 16) || !aligned(y, 16) || (xperm && !aligned(xperm, 16))) return KNX_E_ALIGN;
   if (rows == 0) return KNX_OK;
   const bool rb = (flags & KNX_RMS_ROUND_BF16) != 0;
+  if (w != nullptr && !aligned(w, 16)) return KNX_E_ALIGN;
   const dim3 grid(static_cast<unsigned>((rows + RMS_WARPS - 1) / RMS_WARPS));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == KNX_F16) {
-    rmsnorm_kernel<__half><<<grid, RMS_WARPS * 32, 0, s>>>(
-        static_cast<const __half*>(x), w, w_dtype, static_cast<__half*>(y),
-        static_cast<__half*>(xperm), rows, static_cast<int>(cols), eps, rb);
-  } else {
-    rmsnorm_kernel<__nv_bfloat16><<<grid, RMS_WARPS * 32, 0, s>>>(
-        static_cast<const __nv_bfloat16*>(x), w, w_dtype, static_cast<__nv_bfloat16*>(y),
-        static_cast<__half*>(xperm), rows, static_cast<int>(cols), eps, rb);
-  }
+  auto launch = [&](auto xt, auto wt) {
+    using T = decltype(xt);
+    using WT = std::remove_pointer_t<decltype(wt)>;
+    rmsnorm_kernel<T, WT><<<grid, RMS_WARPS * 32, 0, s>>>(
+        static_cast<const T*>(x), w, static_cast<T*>(y), static_cast<__half*>(xperm), rows,
+        static_cast<int>(cols), eps, rb);
+  };
+  auto with_w = [&](auto xt) {
+    if (w == nullptr) launch(xt, static_cast<void*>(nullptr));
+    else if (w_dtype == KNX_F16) launch(xt, static_cast<__half*>(nullptr));
+    else if (w_dtype == KNX_BF16) launch(xt, static_cast<__nv_bfloat16*>(nullptr));
+    else launch(xt, static_cast<float*>(nullptr));
+  };
+  if (dtype == KNX_F16) with_w(__half{});
+  else with_w(__nv_bfloat16{});
   return launch_status();
 }
