@@ -257,6 +257,108 @@ def time_layer_ep(dev, steps, warmup, rank, world):
     return ms, counts, clocks, e2e_ms, host_in.numel() * 2, host_out.numel() * 2
 
 
+def time_stack(dev, steps=48):
+    """one denoising-step forward of a 60-block stack (30 encoder + 30 decoder) of
+    RMSNorm -> W4A16 MoE -> residual on a 256-token canvas, then the configs[2] sampler step;
+    decoder block b reuses encoder block b's expert weights (the checkpoint's aliasing,
+    load_w4_checkpoint.py:56-59), so 30 weight sets (12.5 GB) stream per step.  Steps/s over
+    `steps` steps with the temperature schedule."""
+    import fused_moe_w4_v2
+    import fused_rmsnorm
+    import fused_sampler_ops
+    import moe_router
+    import workloads
+    sets = [workloads.moe_weights(E, H, I, seed=200 + i, device=dev) for i in range(30)]
+    blocks = [workloads.moe_inputs(T, H, E, seed=300 + b, device=dev) for b in range(60)]
+    h0 = blocks[0]["hidden"]
+    logits = workloads.sampler_logits(256, V_SAMPLER, seed=5, device=dev)
+    xp = torch.empty(T, H, dtype=torch.float16, device=dev)
+
+    def step(k):
+        h = h0
+        for b in range(60):
+            W, inp = sets[b % 30], blocks[b]
+            yn = fused_rmsnorm.fused_rmsnorm(h, inp["norm_w"], 1e-6, xperm=xp)
+            ids, w, _ = moe_router.route_topk(yn, inp["router_w"], TOPK, bias=inp["bias"],
+                                              want_logits=False)
+            h = h + fused_moe_w4_v2.moe_forward(yn, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"],
+                                                W["dn_s"], W["dn_z"], ids, w, hidden_perm=xp,
+                                                int_zeros=False)
+        return fused_sampler_ops.sample_step(logits, workloads.step_seed(1234, k),
+                                             workloads.temperature(k))
+    step(0)
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for k in range(steps):
+        step(k)
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    ms = ev0.elapsed_time(ev1)
+    del sets
+    torch.cuda.empty_cache()
+    return {"steps_per_s": steps / (ms * 1e-3), "ms_per_step": ms / steps, "steps": steps,
+            "blocks": 60, "weight_sets": 30, "canvas_tokens": T,
+            "data": "synthetic (random-init weights of configs[0] shapes; sampler logits N(0,3))"}
+
+
+PREFILL_TOKENS = 2048 + 16384  # configs[4]: 8 canvases + one 16384-token prefill chunk
+
+
+def time_prefill(dev, steps, rank, world):
+    """18432 tokens (8 canvases + a 16384-token prefill chunk), Zipf routing, through
+    RMSNorm -> router -> MoE; with N > 1 each rank holds 128/N experts and 18432/N tokens
+    (expert parallelism).  Job-wide tokens/s and per-GPU HBM GB/s."""
+    import fused_moe_w4_v2
+    import fused_rmsnorm
+    import moe_router
+    import workloads
+    Tr = PREFILL_TOKENS // world
+    Wf = workloads.moe_weights(E, H, I, seed=400, device=dev)
+    inp = workloads.moe_inputs(Tr, H, E, seed=500 + rank, device=dev)
+    xp = torch.empty(Tr, H, dtype=torch.float16, device=dev)
+    if world > 1:
+        import ep_moe
+        layer = ep_moe.ExpertParallelMoE(*ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"], Wf["gu_z"],
+                                                                 Wf["dn_q"], Wf["dn_s"], Wf["dn_z"],
+                                                                 rank, world),
+                                         E_total=E, int_zeros=False)
+        del Wf
+    tpe = PREFILL_TOKENS * TOPK // E
+
+    def step():
+        yn = fused_rmsnorm.fused_rmsnorm(inp["hidden"], inp["norm_w"], 1e-6, xperm=xp)
+        ids, w, _ = moe_router.route_topk(yn, inp["router_w"], TOPK, bias=inp["bias"],
+                                          want_logits=False)
+        if world > 1:
+            return layer(xp, ids, w, out_dtype=torch.float16, tokens_per_expert=tpe), ids
+        return fused_moe_w4_v2.moe_forward(yn, Wf["gu_q"], Wf["gu_s"], Wf["gu_z"], Wf["dn_q"],
+                                           Wf["dn_s"], Wf["dn_z"], ids, w, hidden_perm=xp,
+                                           int_zeros=False), ids
+    _, ids = step()
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    if world > 1:
+        torch.distributed.all_reduce(counts)
+        torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(steps):
+        step()
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item()) / steps
+    layer_bytes = workloads.moe_layer_bytes(counts.cpu().numpy(), T=PREFILL_TOKENS)
+    return {"tokens_per_s": PREFILL_TOKENS / (ms * 1e-3), "ms_per_step": ms, "steps": steps,
+            "tokens": PREFILL_TOKENS, "n_gpus": world,
+            "per_gpu_hbm_gbs": layer_bytes / world / (ms * 1e-3) / 1e9,
+            "max_tokens_per_expert": int(counts.max()),
+            "engine": "tc" if tpe > 64 else "ws"}
+
+
 def time_sampler(dev, reps=1):
     """48 denoising steps with the temperature schedule; per step one fused pass
     (entropy + Gumbel-max + argmax) and one acceptance/stop launch."""
@@ -357,6 +459,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the configs[3] stack and configs[4] prefill measurements")
     ap.add_argument("--only", choices=("layer", "sampler"), default=None,
                     help="run just one workload (used for profiling captures); prints its timing")
     args = ap.parse_args()
@@ -402,6 +506,8 @@ def main():
     if not dist:
         e2e_ms, h2d, d2h = time_layer_e2e(dev, args.steps, args.warmup)
     samp_step_ms, samp_kern_ms = time_sampler(dev)
+    cfg4 = None if args.no_extra else time_prefill(dev, max(2, args.steps // 4), rank, world)
+    cfg3 = None if (args.no_extra or dist) else time_stack(dev)
     if dist:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
@@ -451,6 +557,8 @@ def main():
         "gpu_launches": (EP_LAUNCHES_PER_LAYER if dist else LAUNCHES_PER_LAYER) * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
+        "configs3_stack": cfg3,
+        "configs4_prefill": cfg4,
     }
     print(json.dumps(line), flush=True)
 

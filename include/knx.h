@@ -109,6 +109,14 @@ KNX_API int knx_moe_align(const void* topk_ids, int ids_dtype, int64_t T, int to
                   int32_t* sorted_rows, int32_t* expert_ids, int32_t* padded_inv, int32_t* err,
                   void* stream);
 
+/* The same unpadded permutation (counts, offsets, sorted_pair, inv as above) for any pair count
+ * up to 2^30, by a multi-CTA counting sort (knx_moe_align's single CTA holds T*topk <= 32768).
+ * scratch: >= knx_moe_align_large_scratch_size(T*topk, E) bytes, 16-byte aligned. */
+KNX_API size_t knx_moe_align_large_scratch_size(int64_t N, int E);
+KNX_API int knx_moe_align_large(const void* topk_ids, int ids_dtype, int64_t T, int topk, int E,
+                                int32_t* counts, int32_t* offsets, int32_t* sorted_pair, int32_t* inv,
+                                void* scratch, size_t scratch_bytes, int32_t* err, void* stream);
+
 /* ---- one W4A16 MoE layer ------------------------------------------------------------------
  * Replaces fused_moe_w4_v2 (fused_moe_w4_v2.py:319-371) and fused_moe_w4 (fused_moe_w4.py:104-128).
  * Weight buffers are the pack_experts layout, read unchanged (pack_experts.py:34-41, 87-106):
@@ -127,7 +135,7 @@ KNX_API int knx_moe_align(const void* topk_ids, int ids_dtype, int64_t T, int to
  *   RN16(RN16(q - z) * s), the fp16 arithmetic of the reference kernel (fused_moe_w4_v2.py:126-128).
  * Contracts (fused_moe_w4_v2.py:325-328): H % 256 == 0, I % 64 == 0, gs_gu % 32 == 0 and
  *   divides H, gs_dn % 32 == 0 and divides I, H/gs_gu <= 56, I/gs_dn <= 56, topk <= 16,
- *   E <= 256, T*topk <= 32768.
+ *   E <= 256, T*topk <= 2^30 (above 32768 pairs the permutation is a multi-CTA sort).
  * workspace: >= knx_moe_w4_workspace_size(T, H, I, E, topk) bytes, 256-byte aligned. */
 KNX_API size_t knx_moe_w4_workspace_size(int64_t T, int64_t H, int64_t I, int E, int topk);
 KNX_API int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidden_dtype, const void* topk_ids,

@@ -93,46 +93,6 @@ __global__ void ep_layout_kernel(const int32_t* __restrict__ cnt, int S, int El,
   }
 }
 
-// Task list (expert token chunks of at most m) from per-expert slot offsets, largest chunks first
-// (full chunks in expert order, then remainders by size, in expert order within a size), plus the
-// task count and two zeroed work counters: the same list the align kernel builds.  One CTA.
-__global__ void tasks_from_offsets_kernel(const int32_t* __restrict__ offsets, int E, int m,
-                                          int4* __restrict__ tasks, int32_t* __restrict__ ntasks,
-                                          int32_t* __restrict__ counters) {
-  __shared__ int full_pre[257];
-  __shared__ int rem_of[256];
-  __shared__ int rem_start[65];
-  const int tid = threadIdx.x;
-  if (tid < E) rem_of[tid] = (offsets[tid + 1] - offsets[tid]) % m;
-  __syncthreads();
-  if (tid == 0) {
-    int acc = 0;
-    for (int e = 0; e < E; ++e) {
-      full_pre[e] = acc;
-      acc += (offsets[e + 1] - offsets[e]) / m;
-    }
-    full_pre[E] = acc;
-    for (int r = m - 1; r >= 1; --r) {
-      rem_start[r] = acc;
-      for (int e = 0; e < E; ++e) acc += rem_of[e] == r;
-    }
-    *ntasks = acc;
-    counters[0] = 0;
-    counters[1] = 0;
-  }
-  __syncthreads();
-  if (tid < E) {
-    const int cnt = offsets[tid + 1] - offsets[tid];
-    const int nfull = cnt / m, rem = cnt % m;
-    for (int j = 0; j < nfull; ++j) tasks[full_pre[tid] + j] = make_int4(tid, j * m, m, 0);
-    if (rem > 0) {
-      int before = 0;
-      for (int e = 0; e < tid; ++e) before += rem_of[e] == rem;
-      tasks[rem_start[rem] + before] = make_int4(tid, nfull * m, rem, 0);
-    }
-  }
-}
-
 struct GroupedWs {
   int4* tasks;
   int32_t* ntasks;
@@ -219,9 +179,8 @@ extern "C" int knx_moe_w4_grouped(const void* xrows, const int32_t* rows, int64_
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   GroupedWs w = carve_grouped(static_cast<uint8_t*>(workspace), R, I, E);
   const int eng = moe_engine(flags, tokens_per_expert, H, I, gs_gu, gs_dn);
-  tasks_from_offsets_kernel<<<1, 256, 0, s>>>(offsets, E, engine_task_tokens(eng), w.tasks,
-                                             w.ntasks, w.counters);
-  int st = launch_status();
+  int st = launch_tasks_from_offsets(offsets, E, engine_task_tokens(eng), w.tasks, w.ntasks,
+                                     w.counters, s);
   if (st != KNX_OK) return st;
   GemmArgs ga{};
   ga.xp = static_cast<const __half*>(xrows);

@@ -493,6 +493,7 @@ struct MoeWs {
   int32_t* counters;
   __half* out2;
   __half* out3;
+  void* align_scratch;  // multi-CTA counting sort (N > ALIGN_MAX_PAIRS only)
   size_t bytes;
 };
 
@@ -528,6 +529,7 @@ MoeWs carve_moe_ws(uint8_t* base, int64_t T, int64_t H, int64_t I, int E, int to
   w.counters = reinterpret_cast<int32_t*>(take(16));
   w.out2 = reinterpret_cast<__half*>(take(size_t(N) * I * 2));
   w.out3 = reinterpret_cast<__half*>(take(size_t(N) * H * 2));
+  w.align_scratch = N > ALIGN_MAX_PAIRS ? take(align_large_scratch_bytes(N, E)) : nullptr;
   w.bytes = o;
   return w;
 }
@@ -669,7 +671,7 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
   if (hidden_dtype != KNX_F16 && hidden_dtype != KNX_BF16) return KNX_E_INVALID;
   if (ids_dtype != KNX_I32 && ids_dtype != KNX_I64) return KNX_E_INVALID;
   if (w_dtype != KNX_F16 && w_dtype != KNX_BF16 && w_dtype != KNX_F32) return KNX_E_INVALID;
-  if (!align_supported(T * topk, E)) return KNX_E_UNSUPPORTED;
+  if (E > ALIGN_MAX_EXPERTS || T * topk > (1LL << 30)) return KNX_E_UNSUPPORTED;
   if (!aligned(hidden, 16) || !aligned(out, 16) || (hidden_perm && !aligned(hidden_perm, 16)) ||
       !aligned(gu_q, 16) || !aligned(dn_q, 16) || !aligned(gu_s, 16) || !aligned(gu_z, 16) ||
       !aligned(dn_s, 16) || !aligned(dn_z, 16) || !aligned(workspace, 256))
@@ -690,9 +692,17 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
     xp = w.xp;
   }
   const int eng = moe_engine(flags, T * topk / E, H, I, gs_gu, gs_dn);
-  st = launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0, engine_task_tokens(eng),
-                    w.counts, w.offsets, w.sorted_pair, w.inv, nullptr, nullptr, nullptr, w.tasks,
-                    w.ntasks, w.counters, 2, err, s);
+  if (align_supported(T * topk, E)) {
+    st = launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0,
+                      engine_task_tokens(eng), w.counts, w.offsets, w.sorted_pair, w.inv, nullptr,
+                      nullptr, nullptr, w.tasks, w.ntasks, w.counters, 2, err, s);
+  } else {
+    st = launch_align_large(topk_ids, ids_dtype, T * topk, E, w.counts, w.offsets, w.sorted_pair,
+                            w.inv, w.align_scratch, err, s);
+    if (st == KNX_OK)
+      st = launch_tasks_from_offsets(w.offsets, E, engine_task_tokens(eng), w.tasks, w.ntasks,
+                                     w.counters, s);
+  }
   if (st != KNX_OK) return st;
   prof::mark(pc, 1, s);
   GemmArgs ga{};

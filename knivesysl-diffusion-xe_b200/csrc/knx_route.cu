@@ -357,6 +357,160 @@ __global__ void __launch_bounds__(AL_THREADS)
   }
 }
 
+// Task list (expert token chunks of at most m) from per-expert slot offsets, largest chunks first
+// (full chunks in expert order, then remainders by size, in expert order within a size), plus the
+// task count and two zeroed work counters: the same list the align kernel builds.  One CTA.
+__global__ void tasks_from_offsets_kernel(const int32_t* __restrict__ offsets, int E, int m,
+                                          int4* __restrict__ tasks, int32_t* __restrict__ ntasks,
+                                          int32_t* __restrict__ counters) {
+  __shared__ int full_pre[257];
+  __shared__ int rem_of[256];
+  __shared__ int rem_start[65];
+  const int tid = threadIdx.x;
+  if (tid < E) rem_of[tid] = (offsets[tid + 1] - offsets[tid]) % m;
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) {
+      full_pre[e] = acc;
+      acc += (offsets[e + 1] - offsets[e]) / m;
+    }
+    full_pre[E] = acc;
+    for (int r = m - 1; r >= 1; --r) {
+      rem_start[r] = acc;
+      for (int e = 0; e < E; ++e) acc += rem_of[e] == r;
+    }
+    *ntasks = acc;
+    counters[0] = 0;
+    counters[1] = 0;
+  }
+  __syncthreads();
+  if (tid < E) {
+    const int cnt = offsets[tid + 1] - offsets[tid];
+    const int nfull = cnt / m, rem = cnt % m;
+    for (int j = 0; j < nfull; ++j) tasks[full_pre[tid] + j] = make_int4(tid, j * m, m, 0);
+    if (rem > 0) {
+      int before = 0;
+      for (int e = 0; e < tid; ++e) before += rem_of[e] == rem;
+      tasks[rem_start[rem] + before] = make_int4(tid, nfull * m, rem, 0);
+    }
+  }
+}
+
+// ---- counting sort for more pairs than one CTA holds (N > ALIGN_MAX_PAIRS), unpadded form ----
+// LA1: each CTA of AL_THREADS takes LB consecutive pairs and writes its per-expert counts and
+//      every pair's stable rank inside the block (warp ranks by __match_any_sync, warp prefixes);
+// LA2: one CTA turns the block counts into expert offsets and per-(block, expert) slot bases;
+// LA3: pair p of block b with expert e goes to slot base[b][e] + rank.  Stable in p overall.
+constexpr int LB = 4096;  // pairs per block
+
+__global__ void __launch_bounds__(AL_THREADS)
+    align_large_count_kernel(const void* __restrict__ ids, int ids_dtype, int64_t N, int E,
+                             int32_t* __restrict__ blkcnt, int32_t* __restrict__ lrank,
+                             int32_t* __restrict__ err) {
+  __shared__ int whist[32 * 256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t b0 = static_cast<int64_t>(blockIdx.x) * LB;
+  for (int i = tid; i < 32 * E; i += AL_THREADS) whist[i] = 0;
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  constexpr int PER_WARP = LB / 32;
+  int my_e[PER_WARP / 32], my_r[PER_WARP / 32];
+  int bad = 0;
+#pragma unroll
+  for (int r = 0; r < PER_WARP / 32; ++r) {
+    const int64_t p = b0 + warp * PER_WARP + r * 32 + lane;
+    int e = E;
+    if (p < N) {
+      int64_t v = load_as_i64(ids, ids_dtype, p);
+      if (v < 0 || v > E) {
+        bad = 1;
+        v = E;
+      }
+      e = static_cast<int>(v);
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int before = __popc(peers & lt_mask);
+    const int leader = __ffs(peers) - 1;
+    const int prev = e < E ? whist[warp * E + e] : 0;
+    __syncwarp();
+    if (e < E && lane == leader) whist[warp * E + e] = prev + __popc(peers);
+    __syncwarp();
+    my_e[r] = e;
+    my_r[r] = prev + before;
+  }
+  if (bad && err) atomicOr(err, KNX_DEV_BAD_EXPERT_ID);
+  __syncthreads();
+  if (tid < E) {  // exclusive prefix over warps, block total
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = whist[w * E + tid];
+      whist[w * E + tid] = run;
+      run += c;
+    }
+    blkcnt[static_cast<int64_t>(blockIdx.x) * E + tid] = run;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < PER_WARP / 32; ++r) {
+    const int64_t p = b0 + warp * PER_WARP + r * 32 + lane;
+    if (p < N) lrank[p] = my_e[r] < E ? whist[warp * E + my_e[r]] + my_r[r] : -1;
+  }
+}
+
+__global__ void __launch_bounds__(256)
+    align_large_scan_kernel(const int32_t* __restrict__ blkcnt, int nblk, int E,
+                            int32_t* __restrict__ blkbase, int32_t* __restrict__ counts,
+                            int32_t* __restrict__ offsets) {
+  __shared__ int tot[257];
+  const int e = threadIdx.x;
+  int c = 0;
+  if (e < E)
+    for (int b = 0; b < nblk; ++b) c += blkcnt[static_cast<int64_t>(b) * E + e];
+  if (e < E) tot[e] = c;
+  __syncthreads();
+  if (e == 0) {
+    int acc = 0;
+    for (int i = 0; i < E; ++i) {
+      const int t = tot[i];
+      tot[i] = acc;
+      acc += t;
+    }
+    tot[E] = acc;
+    if (offsets) offsets[E] = acc;
+  }
+  __syncthreads();
+  if (e < E) {
+    if (counts) counts[e] = c;
+    if (offsets) offsets[e] = tot[e];
+    int a = tot[e];
+    for (int b = 0; b < nblk; ++b) {
+      blkbase[static_cast<int64_t>(b) * E + e] = a;
+      a += blkcnt[static_cast<int64_t>(b) * E + e];
+    }
+  }
+}
+
+__global__ void align_large_scatter_kernel(const void* __restrict__ ids, int ids_dtype, int64_t N,
+                                           int E, const int32_t* __restrict__ blkbase,
+                                           const int32_t* __restrict__ lrank,
+                                           const int32_t* __restrict__ offsets,
+                                           int32_t* __restrict__ sorted_pair,
+                                           int32_t* __restrict__ inv) {
+  const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (p >= N) return;
+  const int r = lrank[p];
+  if (r < 0) {
+    if (inv) inv[p] = -1;
+  } else {
+    const int e = static_cast<int>(load_as_i64(ids, ids_dtype, p));
+    const int slot = blkbase[(p / LB) * E + e] + r;
+    if (sorted_pair) sorted_pair[slot] = static_cast<int32_t>(p);
+    if (inv) inv[p] = slot;
+  }
+  if (sorted_pair && p >= offsets[E]) sorted_pair[p] = static_cast<int32_t>(N);  // tail
+}
+
 // Activation copy into the MoE K-interleave (f16 out; f16 or bf16 in).  One thread per 16 bytes.
 template <typename T>
 __global__ void permute_act_kernel(const T* __restrict__ x, __half* __restrict__ xp, int64_t nvec) {
@@ -426,6 +580,34 @@ int launch_permute(const void* x, int dtype, __half* xp, int64_t elems, cudaStre
   return launch_status();
 }
 
+size_t align_large_scratch_bytes(int64_t N, int E) {
+  const int64_t nblk = (N + LB - 1) / LB;
+  return static_cast<size_t>(N) * 4 + 2 * static_cast<size_t>(nblk) * E * 4 + 256;
+}
+
+int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t* counts,
+                       int32_t* offsets, int32_t* sorted_pair, int32_t* inv, void* scratch,
+                       int32_t* err, cudaStream_t s) {
+  if (E > 256 || N > (1LL << 30)) return KNX_E_UNSUPPORTED;
+  if (N == 0) return KNX_OK;
+  const int nblk = static_cast<int>((N + LB - 1) / LB);
+  int32_t* lrank = static_cast<int32_t*>(scratch);
+  int32_t* blkcnt = lrank + ((N + 63) & ~int64_t(63));
+  int32_t* blkbase = blkcnt + static_cast<int64_t>(nblk) * E;
+  align_large_count_kernel<<<nblk, AL_THREADS, 0, s>>>(ids, ids_dtype, N, E, blkcnt, lrank, err);
+  align_large_scan_kernel<<<1, 256, 0, s>>>(blkcnt, nblk, E, blkbase, counts, offsets);
+  align_large_scatter_kernel<<<static_cast<unsigned>((N + 255) / 256), 256, 0, s>>>(
+      ids, ids_dtype, N, E, blkbase, lrank, offsets, sorted_pair, inv);
+  return launch_status();
+}
+
+int launch_tasks_from_offsets(const int32_t* offsets, int E, int m, int4* tasks, int32_t* ntasks,
+                              int32_t* counters, cudaStream_t s) {
+  if (E > 256 || m > 64) return KNX_E_UNSUPPORTED;
+  tasks_from_offsets_kernel<<<1, 256, 0, s>>>(offsets, E, m, tasks, ntasks, counters);
+  return launch_status();
+}
+
 }  // namespace knx
 
 // ------------------------------------------------------------------------------------------
@@ -457,6 +639,27 @@ extern "C" int knx_router_topk(const void* x, const void* wr, const float* bias,
   router_topk_kernel<<<static_cast<unsigned>((T + 7) / 8), 256, 0, s>>>(
       part, bias, static_cast<int>(T), E, topk, logits_out, ids, weights);
   return launch_status();
+}
+
+extern "C" size_t knx_moe_align_large_scratch_size(int64_t N, int E) {
+  if (N < 0 || E <= 0) return 0;
+  return knx::align_large_scratch_bytes(N, E);
+}
+
+extern "C" int knx_moe_align_large(const void* topk_ids, int ids_dtype, int64_t T, int topk, int E,
+                                   int32_t* counts, int32_t* offsets, int32_t* sorted_pair,
+                                   int32_t* inv, void* scratch, size_t scratch_bytes, int32_t* err,
+                                   void* stream) {
+  using namespace knx;
+  if (T < 0 || topk < 1 || topk > 64 || E < 1 || E > ALIGN_MAX_EXPERTS) return KNX_E_INVALID;
+  if (ids_dtype != KNX_I32 && ids_dtype != KNX_I64) return KNX_E_INVALID;
+  const int64_t N = T * topk;
+  if (N > (1LL << 30)) return KNX_E_UNSUPPORTED;
+  if (N == 0) return KNX_OK;
+  if (scratch == nullptr || scratch_bytes < align_large_scratch_bytes(N, E)) return KNX_E_WORKSPACE;
+  if (!aligned(scratch, 16)) return KNX_E_ALIGN;
+  return launch_align_large(topk_ids, ids_dtype, N, E, counts, offsets, sorted_pair, inv, scratch,
+                            err, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int knx_moe_align(const void* topk_ids, int ids_dtype, int64_t T, int topk, int E,

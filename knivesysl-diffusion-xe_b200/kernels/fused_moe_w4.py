@@ -10,7 +10,7 @@ fused_moe_w4(hidden, exp, topk_ids, topk_w) runs the same sm_100a layer as fused
 """
 import torch
 
-from _knx import check, dtype_code, load, ptr, require_device, stream_of
+from _knx import check, dtype_code, load, ptr, require_device, stream_of, workspace
 
 BLOCK_M = 64
 
@@ -57,9 +57,16 @@ def moe_align_unpadded(topk_ids, E):
     offsets = torch.empty(E + 1, **i32)
     sorted_pair = torch.empty(N, **i32)
     inv = torch.empty(N, **i32)
-    check(load().knx_moe_align(ptr(ids), dtype_code(ids.dtype), T, tk, E, 0, ptr(counts),
-                               ptr(offsets), ptr(sorted_pair), ptr(inv), None, None, None, None,
-                               stream_of(dev)), "knx_moe_align")
+    lib = load()
+    if N <= 32768:
+        check(lib.knx_moe_align(ptr(ids), dtype_code(ids.dtype), T, tk, E, 0, ptr(counts),
+                                ptr(offsets), ptr(sorted_pair), ptr(inv), None, None, None, None,
+                                stream_of(dev)), "knx_moe_align")
+    else:  # more pairs than one CTA holds: the multi-CTA counting sort
+        scratch = workspace(dev, lib.knx_moe_align_large_scratch_size(N, E), "align_large")
+        check(lib.knx_moe_align_large(ptr(ids), dtype_code(ids.dtype), T, tk, E, ptr(counts),
+                                      ptr(offsets), ptr(sorted_pair), ptr(inv), ptr(scratch),
+                                      scratch.numel(), None, stream_of(dev)), "knx_moe_align_large")
     return counts, offsets, sorted_pair, inv
 
 

@@ -339,3 +339,42 @@ def test_accept_ties_and_batches_vs_oracle(cuda):
     mask, out = accept_ops.accept_canvas(H.to(cuda), cur.to(cuda), prop.to(cuda), 0.1)
     rm, ro = ref.accept_canvas(H, cur, prop, 0.1)
     assert torch.equal(mask.cpu(), rm) and torch.equal(out.cpu(), ro)
+
+
+def test_align_large_matches_unpadded_reference(cuda):
+    """More pairs than one CTA holds: the multi-CTA counting sort gives the same stable
+    permutation (experts ascending, pairs ascending within an expert; bad ids dropped)."""
+    import fused_moe_w4
+    g = torch.Generator().manual_seed(77)
+    for T, tk, E in ((4608, 8, 128), (20000, 8, 256), (5000, 7, 64)):
+        ids = torch.randint(0, E, (T, tk), generator=g, dtype=torch.int32)
+        ids[3, 2] = E  # dropped
+        counts, offsets, sp, inv = fused_moe_w4.moe_align_unpadded(ids.to(cuda), E)
+        flat = ids.flatten().long()
+        valid = flat < E
+        order = torch.argsort(torch.where(valid, flat, torch.full_like(flat, E)), stable=True)
+        nv = int(valid.sum())
+        assert torch.equal(counts.cpu().long(), torch.bincount(flat[valid], minlength=E))
+        assert torch.equal(sp.cpu()[:nv].long(), order[:nv])
+        assert (sp.cpu()[nv:] == T * tk).all()
+        want_inv = torch.full((T * tk,), -1, dtype=torch.long)
+        want_inv[order[:nv]] = torch.arange(nv)
+        assert torch.equal(inv.cpu().long(), want_inv)
+
+
+def test_moe_layer_large_batch_matches_small_batches(cuda):
+    """A 4608-token layer (36864 pairs, multi-CTA permutation) equals the same tokens run as
+    256-token layers, row for row, with the same engine."""
+    import fused_moe_w4_v2
+    import workloads
+    W = workloads.moe_weights(128, 2816, 704, seed=61, device=cuda)
+    args = (W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"], W["dn_z"])
+    T = 4608
+    g = torch.Generator(device=cuda).manual_seed(62)
+    hidden = (torch.randn(T, 2816, generator=g, device=cuda) * 0.5).half()
+    ids, w = workloads.random_routing(T, 128, 8, seed=63, device=cuda)
+    for eng in ("ws", "tc"):
+        big = fused_moe_w4_v2.moe_forward(hidden, *args, ids, w, engine=eng)
+        parts = [fused_moe_w4_v2.moe_forward(hidden[i:i + 256], *args, ids[i:i + 256],
+                                             w[i:i + 256], engine=eng) for i in range(0, T, 256)]
+        assert torch.equal(big.view(torch.int16), torch.cat(parts).view(torch.int16)), eng
