@@ -547,7 +547,7 @@ def main():
                      "peak_kind": peak_kind, "traffic": GEMM1_NCU_TRAFFIC.get(engine),
                      "algorithmic_bytes": gemm1_bytes},
         "sampler_step_us": samp_step_ms * 1000.0,
-        "sampler_roofline": {"kernel": "sampler_kernel", "bound": "hbm",
+        "sampler_roofline": {"kernel": "sampler_stream_kernel + row_merge_kernel", "bound": "hbm",
                              "achieved": 256 * V_SAMPLER * 4 / (samp_kern_ms * 1e-3) / 1e9,
                              "peak": peak, "unit": "GB/s",
                              "frac": 256 * V_SAMPLER * 4 / (samp_kern_ms * 1e-3) / 1e9 / peak,

@@ -37,8 +37,8 @@ int launch_tc_rows(const __half* act, int64_t act_stride, int K, const int32_t* 
                    int gs, bool zint, __half* out, int64_t out_stride, int64_t max_tasks,
                    int32_t* err, cudaStream_t s);
 
-// warp-specialised mma.sync grouped W4A16 GEMMs (knx_moe_hw.cu), 16 tokens per task
-constexpr int HW_TASK_TOKENS = 16;
+// warp-specialised mma.sync grouped W4A16 GEMMs (knx_moe_hw.cu), 32 tokens per task
+constexpr int HW_TASK_TOKENS = 32;
 constexpr int MIN_TASK_TOKENS = 16;  // smallest task size of any engine (sizes the task list)
 bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated);
 int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, const int32_t* offsets,

@@ -1,23 +1,25 @@
 // knx_moe_hw.cu — warp-specialised grouped W4A16 GEMMs on the warp-level tensor-core path
-// (mma.sync m16n8k16) for the small-token regime (<= 16 tokens per task).
+// (mma.sync m16n8k16) for the small-token regime (<= 32 tokens per task).
 //
 // Why this shape (measured on B200): a tcgen05 M128 x K16 instruction costs ~108 ns whatever N
 // is, which caps a weights-as-M tcgen05 GEMM at ~1.4 TB/s of nibbles when N (tokens) is small,
 // while mma.sync has no such floor; and HBM only streams at full rate with >= ~128 KB of loads
 // in flight per SM.  So:
-//   * one persistent CTA per SM; a work item is (task of <= 16 tokens of one expert, slice of 256
+//   * one persistent CTA per SM; a work item is (task of <= 32 tokens of one expert, slice of 256
 //     weight rows) — gated: 128 gate rows + the matching 128 up rows;
 //   * warp 16 (scheduler + weights): per item the slice's scale/zero rows by 1-D bulk copies, then
 //     the packed nibbles by 2-D TMA (128-byte swizzle) in 32 KB stages (256 rows x 256 k) into a
 //     ring of up to 4 stages (128 KB in flight);
 //   * warp 17 (activations): per stage, one 1-D bulk copy per token of 256 k (512 B) gathered
-//     by token id into a 4-stage ring (rows padded to 576 B: conflict-free fragment loads);
+//     by token id into a ring of 2-4 stages (rows padded to 576 B: conflict-free fragment loads);
 //   * warps 0-15 (math): warp w owns one m16 row tile — gated: gate rows 8w..8w+7 on tile rows
 //     0-7 and the matching up rows on tile rows 8-15, so each lane ends with gate and up of one
 //     intermediate column; plain: rows 16w..16w+15 — over the full K.  Nibbles are dequantised in
 //     registers into A fragments (dequant8: bit-identical to dequant_w4 for integer zero-points,
-//     the reference kernel's f16 arithmetic otherwise) and multiplied with the tokens' B
-//     fragments.  No split-K: every output is one warp's fixed-order sum (deterministic).
+//     the reference kernel's f16 arithmetic otherwise) and multiplied with the B fragments of
+//     the task's 1-4 n8 token tiles, so one dequantisation serves up to 32 tokens.  No split-K:
+//     every output is one warp's fixed-order sum (deterministic), and a token's sum does not
+//     depend on the other tokens of its task.
 //   * GELU(gate) * up (gated) or the plain result goes through a shared-memory tile to
 //     coalesced 16-byte stores; the gated output is written in the K-interleave the down GEMM
 //     reads.
@@ -33,17 +35,17 @@ namespace hw {
 
 using namespace sm100;
 
-constexpr int TOK = HW_TASK_TOKENS;      // tokens per task (16)
+constexpr int TOK = HW_TASK_TOKENS;      // tokens per task (32)
 constexpr int NT = TOK / 8;              // n8 tiles per task
 constexpr int BK = 256;                  // k per stage
 constexpr int WROW = BK / 2;             // 128 bytes of nibbles per row per stage
 constexpr int ROWS = 256;                // weight rows per item
 constexpr int GROWS = ROWS / 2;          // gated: gate rows per item
 constexpr int BOX_ROWS = 128;            // rows per TMA box
-constexpr int SW_MAX = 4, SA = 4, IR = 2;
+constexpr int SW_MAX = 4, SA_MAX = 4, IR = 2;
 constexpr int W_STAGE = ROWS * WROW;     // 32 KB
 constexpr int AROW = BK * 2 + 64;        // 576 B per token row per stage
-constexpr int A_STAGE = TOK * AROW;      // 9 KB
+constexpr int A_STAGE = TOK * AROW;      // 18 KB
 constexpr int MATH_WARPS = 16;
 constexpr int NUM_WARPS = MATH_WARPS + 2;
 constexpr int NTHREADS = NUM_WARPS * 32;
@@ -54,11 +56,13 @@ constexpr int OT_BYTES = TOK * OT * 2;
 constexpr size_t SMEM_LIMIT = 232448;    // 227 KB opt-in per block
 constexpr size_t STATIC_RESERVE = 1024;  // Ctrl + alignment of the dynamic base
 
-static_assert(NT == 2, "the math loop is written for 16-token tasks");
+static_assert(NT == 4, "the math loop is written for 32-token tasks");
+// Accumulator sets per n8 tile (1, 2 or 4).  One set: 18 warps put 5 on two SM sub-partitions,
+// which caps a thread at 96 registers, and 4 token tiles x 2 sets spill there.
 #ifndef KNX_HW_NACC
-#define KNX_HW_NACC 2
+#define KNX_HW_NACC 1
 #endif
-constexpr int NACC = KNX_HW_NACC;  // accumulator sets per n8 tile (2 or 4)
+constexpr int NACC = KNX_HW_NACC;
 // The producers run stages ahead of the math warps and share their SM sub-partitions (warp 16
 // with warps 0/4/8/12, warp 17 with 1/5/9/13): they back off between polls of their "empty"
 // barriers instead of spinning, which would take issue slots from those math warps.
@@ -74,7 +78,7 @@ struct Item {
 
 struct Ctrl {
   uint64_t w_full[SW_MAX], w_empty[SW_MAX];
-  uint64_t a_full[SA], a_empty[SA];
+  uint64_t a_full[SA_MAX], a_empty[SA_MAX];
   uint64_t i_full[IR], i_empty[IR];
   Item items[IR];
   int abort;
@@ -97,18 +101,23 @@ struct Params {
   int64_t out_stride;
   int nslices;
   int sw;  // weight ring depth (stages)
+  int sa;  // activation ring depth (stages)
   int32_t* err;
 };
 
 KNX_HOST_DEVINL size_t sz_slot_bytes(int ng) { return static_cast<size_t>(ROWS) * ng * 4; }
-inline size_t smem_bytes(int ng, int sw) {
-  return 1024 + static_cast<size_t>(sw) * W_STAGE + SA * A_STAGE + ((OT_BYTES + 127) & ~127) +
-         IR * sz_slot_bytes(ng);
+inline size_t smem_bytes(int ng, int sw, int sa) {
+  return 1024 + static_cast<size_t>(sw) * W_STAGE + static_cast<size_t>(sa) * A_STAGE +
+         ((OT_BYTES + 127) & ~127) + IR * sz_slot_bytes(ng);
 }
-inline int ring_depth(int ng) {
-  for (int sw = SW_MAX; sw >= 2; --sw)
-    if (smem_bytes(ng, sw) + STATIC_RESERVE <= SMEM_LIMIT) return sw;
-  return 0;
+// Ring depths that fit: the weight ring first (it streams from HBM; 4 stages = 128 KB in
+// flight), then the activation ring (its rows are L2-resident), each at least 2 stages.
+inline bool ring_depths(int ng, int& sw, int& sa) {
+  for (sw = SW_MAX; sw >= 2; --sw)
+    for (sa = SA_MAX; sa >= 2; --sa)
+      if (smem_bytes(ng, sw, sa) + STATIC_RESERVE <= SMEM_LIMIT) return true;
+  sw = sa = 0;
+  return false;
 }
 
 KNX_DEVINL void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
@@ -149,30 +158,38 @@ KNX_DEVINL void group_consts(__half s, __half z, __half2& s2, __half2& s16, __ha
 
 // One stage (256 k) of one warp's m16 tile: 8 k32 steps (jmax in the K tail), NTT n8 token
 // tiles.  Scale-group boundaries are compile-time (GPJ k32 steps per group; GPJ = 8 also serves
-// groups that span several stages), so the unrolled loop carries no per-step bookkeeping.
+// groups that span several stages): the steps of one group are unrolled, the groups are a loop
+// (unrolling across groups lets the scheduler keep more steps in flight than 112 registers
+// hold at 4 token tiles).
 template <bool ZINT, int NTT, int GPJ, bool TAIL>
 KNX_DEVINL void mma_stage(uint32_t wa, uint32_t wb, uint32_t ab, int g, int jmax, int grp0,
                           const __half* sA, const __half* zA, const __half* sB, const __half* zB,
                           float (&acc)[NT][NACC][4]) {
-  __half2 sa2, sa16, ca2, ca16, sb2, sb16, cb2, cb16;
+  constexpr int UJ = NACC >= 2 ? NACC / 2 : 1;
+  static_assert(GPJ % UJ == 0 || UJ == 1, "accumulator sets must repeat within a group");
+#pragma unroll 1
+  for (int j0 = 0; j0 < 8; j0 += GPJ) {
+    if (TAIL && j0 >= jmax) break;
+    __half2 sa2, sa16, ca2, ca16, sb2, sb16, cb2, cb16;
+    const int grp = grp0 + j0 / GPJ;
+    group_consts<ZINT>(sA[grp], zA[grp], sa2, sa16, ca2, ca16);
+    group_consts<ZINT>(sB[grp], zB[grp], sb2, sb16, cb2, cb16);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    if (!TAIL || j < jmax) {
-      if (j % GPJ == 0) {
-        const int grp = grp0 + j / GPJ;
-        group_consts<ZINT>(sA[grp], zA[grp], sa2, sa16, ca2, ca16);
-        group_consts<ZINT>(sB[grp], zB[grp], sb2, sb16, cb2, cb16);
-      }
-      const uint32_t sw_off = static_cast<uint32_t>((j ^ g) << 4);
-      uint32_t fa[4], fb[4];
-      dequant8<ZINT>(lds32(wa + sw_off), sa2, sa16, ca2, ca16, fa);
-      dequant8<ZINT>(lds32(wb + sw_off), sb2, sb16, cb2, cb16, fb);
+    for (int jj = 0; jj < GPJ; ++jj) {
+      const int j = j0 + jj;
+      if (!TAIL || j < jmax) {
+        const uint32_t sw_off = static_cast<uint32_t>((j ^ g) << 4);
+        uint32_t fa[4], fb[4];
+        dequant8<ZINT>(lds32(wa + sw_off), sa2, sa16, ca2, ca16, fa);
+        dequant8<ZINT>(lds32(wb + sw_off), sb2, sb16, cb2, cb16, fb);
 #pragma unroll
-      for (int t = 0; t < NTT; ++t) {
-        const uint4 b = lds128(ab + t * 8 * AROW + j * 64);
-        constexpr int UJ = NACC / 2;
-        mma_16816(acc[t][2 * (j % UJ)], fa[0], fb[0], fa[1], fb[1], b.x, b.y);
-        mma_16816(acc[t][2 * (j % UJ) + 1], fa[2], fb[2], fa[3], fb[3], b.z, b.w);
+        for (int t = 0; t < NTT; ++t) {
+          const uint4 b = lds128(ab + t * 8 * AROW + j * 64);
+          // k16 halves into sets 2 * (jj % UJ) and +1 (NACC >= 2), both into set 0 (NACC 1)
+          constexpr int S0 = NACC >= 2 ? 2 : 0, H1 = NACC >= 2 ? 1 : 0;
+          mma_16816(acc[t][S0 * (jj % UJ)], fa[0], fb[0], fa[1], fb[1], b.x, b.y);
+          mma_16816(acc[t][S0 * (jj % UJ) + H1], fa[2], fb[2], fa[3], fb[3], b.z, b.w);
+        }
       }
     }
   }
@@ -184,18 +201,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   extern __shared__ uint8_t dsm_raw[];
   __shared__ Ctrl ctrl;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-  const int sw = p.sw;
+  const int sw = p.sw, sa = p.sa;
   uint8_t* w_ring = base;
   uint8_t* a_ring = base + sw * W_STAGE;
-  __half* otile = reinterpret_cast<__half*>(a_ring + SA * A_STAGE);
-  uint8_t* sz_ring = a_ring + SA * A_STAGE + ((OT_BYTES + 127) & ~127);
+  __half* otile = reinterpret_cast<__half*>(a_ring + sa * A_STAGE);
+  uint8_t* sz_ring = a_ring + sa * A_STAGE + ((OT_BYTES + 127) & ~127);
   const size_t szr = sz_slot_bytes(p.ng);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nst = (p.K + BK - 1) / BK;
 
   if (tid == 0) {
     for (int s = 0; s < sw; ++s) { mbar_init(&ctrl.w_full[s], 1); mbar_init(&ctrl.w_empty[s], MATH_WARPS); }
-    for (int s = 0; s < SA; ++s) { mbar_init(&ctrl.a_full[s], 1); mbar_init(&ctrl.a_empty[s], MATH_WARPS); }
+    for (int s = 0; s < sa; ++s) { mbar_init(&ctrl.a_full[s], 1); mbar_init(&ctrl.a_empty[s], MATH_WARPS); }
     for (int i = 0; i < IR; ++i) {
       mbar_init(&ctrl.i_full[i], 1);
       mbar_init(&ctrl.i_empty[i], MATH_WARPS + 1);
@@ -315,8 +332,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                      : static_cast<int64_t>(it.slot0 + lane)) * p.act_stride;
       bool ok = true;
       for (int st = 0; st < nst; ++st, ++ast) {
-        const int s = ast % SA;
-        if (!wait(&ctrl.a_empty[s], ((ast / SA) & 1) ^ 1, PROD_BACKOFF_NS)) {
+        const int s = ast % sa;
+        if (!wait(&ctrl.a_empty[s], ((ast / sa) & 1) ^ 1, PROD_BACKOFF_NS)) {
           ok = false;
           break;
         }
@@ -332,8 +349,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     // bulk copies already issued must land before the CTA exits (bounded)
     if (lane == 0)
-      for (uint32_t x = ast > static_cast<uint32_t>(SA) ? ast - SA : 0; x < ast; ++x)
-        mbar_wait(&ctrl.a_full[x % SA], (x / SA) & 1);
+      for (uint32_t x = ast > static_cast<uint32_t>(sa) ? ast - sa : 0; x < ast; ++x)
+        mbar_wait(&ctrl.a_full[x % sa], (x / sa) & 1);
     __syncwarp();
   } else {
     // ---------------------------------------------------------------- math warps
@@ -384,8 +401,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[t][u][i] = 0.f;
       for (int st = 0; st < nst; ++st, ++wst, ++ast) {
-        const int ws = wst % sw, as = ast % SA;
-        const bool ready = wait(&ctrl.w_full[ws], (wst / sw) & 1) && wait(&ctrl.a_full[as], (ast / SA) & 1);
+        const int ws = wst % sw, as = ast % sa;
+        const bool ready = wait(&ctrl.w_full[ws], (wst / sw) & 1) && wait(&ctrl.a_full[as], (ast / sa) & 1);
         if (ready && active) {
           const uint32_t wa = smem_u32(w_ring + ws * W_STAGE) + rA * WROW + 4 * q;
           const uint32_t wb = smem_u32(w_ring + ws * W_STAGE) + rB * WROW + 4 * q;
@@ -393,11 +410,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const int jmax = min(8, (p.K - st * BK) >> 5);
           const int grp0 = (st * BK) / p.gs;
           if (jmax == 8) {
-            if (ntl == 2) mma_stage<ZINT, 2, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc);
-            else mma_stage<ZINT, 1, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc);
+            switch (ntl) {
+              case 4: mma_stage<ZINT, 4, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc); break;
+              case 3: mma_stage<ZINT, 3, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc); break;
+              case 2: mma_stage<ZINT, 2, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc); break;
+              default: mma_stage<ZINT, 1, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc);
+            }
           } else {
-            if (ntl == 2) mma_stage<ZINT, 2, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc);
-            else mma_stage<ZINT, 1, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc);
+            switch (ntl) {
+              case 4: mma_stage<ZINT, 4, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc); break;
+              case 3: mma_stage<ZINT, 3, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc); break;
+              case 2: mma_stage<ZINT, 2, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc); break;
+              default: mma_stage<ZINT, 1, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc);
+            }
           }
         }
         __syncwarp();
@@ -494,15 +519,14 @@ int launch_hw_g(const hw::Params& p, const CUtensorMap& map, int grid, cudaStrea
       return KNX_E_DEVICE;
     attr[dev & 63] = true;
   }
-  hw::hw_gemm_kernel<GATED, ZINT, GPJ><<<grid, hw::NTHREADS, hw::smem_bytes(p.ng, p.sw), s>>>(map, p);
+  hw::hw_gemm_kernel<GATED, ZINT, GPJ><<<grid, hw::NTHREADS, hw::smem_bytes(p.ng, p.sw, p.sa), s>>>(map, p);
   return launch_status();
 }
 
 template <bool GATED, bool ZINT>
 int launch_hw(hw::Params p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
               int64_t work_bound, cudaStream_t s) {
-  p.sw = hw::ring_depth(p.ng);
-  if (p.sw == 0) return KNX_E_UNSUPPORTED;
+  if (!hw::ring_depths(p.ng, p.sw, p.sa)) return KNX_E_UNSUPPORTED;
   CUtensorMap map;
   if (!encode_map_hw(&map, wq, total_rows, row_bytes)) return KNX_E_DEVICE;
   const int sms = num_sms();
@@ -520,7 +544,8 @@ int launch_hw(hw::Params p, const uint8_t* wq, int64_t total_rows, int64_t row_b
 bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated) {
   // scale groups must not straddle a 256-k stage unless they cover whole stages
   if (!(gs == 32 || gs == 64 || gs == 128 || (gs > 0 && gs % 256 == 0))) return false;
-  if (ng > hw::SZ_MAX || (K % 64) != 0 || hw::ring_depth(ng) == 0) return false;
+  int sw, sa;
+  if (ng > hw::SZ_MAX || (K % 64) != 0 || !hw::ring_depths(ng, sw, sa)) return false;
   if (gated) return (rows_per_expert / 2) % 64 == 0;
   return rows_per_expert % 16 == 0;
 }
