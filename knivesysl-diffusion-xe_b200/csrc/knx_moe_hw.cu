@@ -237,7 +237,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // ---------------------------------------------------------------- scheduler + weights
     if (lane == 0) {
       const int nwork = (p.tasks ? *p.ntasks : (p.dense_rows + TOK - 1) / TOK) * p.nslices;
-      uint32_t wst = 0;
+      uint32_t wst = 0;            // stages issued
+      uint32_t wsl = 0, wph = 0;   // next ring slot and its phase parity
       int last_on_slot[IR];  // newest item per slot whose scale/zero copies were issued (-1: none)
       for (int i = 0; i < IR; ++i) last_on_slot[i] = -1;
       for (int n = 0;; ++n) {
@@ -289,8 +290,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           bulk_load(szs + reg, p.wz + r0, b, &ctrl.i_full[slot]);
         }
         for (int st = 0; st < nst; ++st, ++wst) {
-          const int s = wst % sw;
-          if (!wait(&ctrl.w_empty[s], ((wst / sw) & 1) ^ 1, PROD_BACKOFF_NS)) break;
+          const int s = static_cast<int>(wsl);
+          if (!wait(&ctrl.w_empty[s], wph ^ 1u, PROD_BACKOFF_NS)) break;
+          if (++wsl == static_cast<uint32_t>(sw)) { wsl = 0; wph ^= 1u; }
           uint8_t* dst = w_ring + s * W_STAGE;
           mbar_arrive_expect_tx(&ctrl.w_full[s], W_STAGE);
           const int x = st * WROW;
@@ -316,10 +318,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     __syncwarp();
   } else if (warp == WARP_APROD) {
     // ---------------------------------------------------------------- activation gather
-    uint32_t ast = 0;
+    uint32_t ast = 0;            // stages issued
+    uint32_t asl = 0, aph = 0;   // next ring slot and its phase parity
     for (int n = 0;; ++n) {
       const int slot = n % IR;
-      if (!wait(&ctrl.i_full[slot], (n / IR) & 1, PROD_BACKOFF_NS)) break;
+      // lane 0 waits and the warp follows its answer (a timeout is seen by every lane alike)
+      bool got = true;
+      if (lane == 0) got = wait(&ctrl.i_full[slot], (n / IR) & 1, PROD_BACKOFF_NS);
+      if (!__shfl_sync(0xffffffffu, got, 0)) break;
       const Item it = ctrl.items[slot];
       if (!it.valid) {
         __syncwarp();
@@ -332,11 +338,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                      : static_cast<int64_t>(it.slot0 + lane)) * p.act_stride;
       bool ok = true;
       for (int st = 0; st < nst; ++st, ++ast) {
-        const int s = ast % sa;
-        if (!wait(&ctrl.a_empty[s], ((ast / sa) & 1) ^ 1, PROD_BACKOFF_NS)) {
+        const int s = static_cast<int>(asl);
+        bool free_ = true;
+        if (lane == 0) free_ = wait(&ctrl.a_empty[s], aph ^ 1u, PROD_BACKOFF_NS);
+        if (!__shfl_sync(0xffffffffu, free_, 0)) {
           ok = false;
           break;
         }
+        if (++asl == static_cast<uint32_t>(sa)) { asl = 0; aph ^= 1u; }
         const int k0 = st * BK;
         const uint32_t kb = static_cast<uint32_t>(min(BK, p.K - k0)) * 2u;
         if (lane == 0) mbar_arrive_expect_tx(&ctrl.a_full[s], kb * it.cnt);
@@ -360,7 +369,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int rA = GATED ? 8 * warp + g : 16 * warp + g;
     const int rB = GATED ? GROWS + 8 * warp + g : 16 * warp + 8 + g;
     const int first_row = GATED ? 8 * warp : 16 * warp;  // tile's first row (validity)
-    uint32_t wst = 0, ast = 0;
+    // ring slots and phase parities, carried across items (no runtime divisions in the loop)
+    uint32_t wsl = 0, wph = 0, asl = 0, aph = 0;
+    const int spg = GPJ < 8 ? 1 : p.gs / BK;  // stages per scale group when groups span stages
     for (int n = 0;; ++n) {
       const int slot = n % IR;
       const bool got = wait(&ctrl.i_full[slot], (n / IR) & 1, 64);
@@ -400,15 +411,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         for (int u = 0; u < NACC; ++u)
 #pragma unroll
           for (int i = 0; i < 4; ++i) acc[t][u][i] = 0.f;
-      for (int st = 0; st < nst; ++st, ++wst, ++ast) {
-        const int ws = wst % sw, as = ast % sa;
-        const bool ready = wait(&ctrl.w_full[ws], (wst / sw) & 1) && wait(&ctrl.a_full[as], (ast / sa) & 1);
+      int grp0 = 0, spg_left = spg;  // first scale group of the stage
+      for (int st = 0; st < nst; ++st) {
+        const int ws = static_cast<int>(wsl), as = static_cast<int>(asl);
+        // mma.sync needs the whole warp: every lane follows the same answer
+        const bool ready = __all_sync(0xffffffffu, wait(&ctrl.w_full[ws], wph) &&
+                                                       wait(&ctrl.a_full[as], aph));
         if (ready && active) {
           const uint32_t wa = smem_u32(w_ring + ws * W_STAGE) + rA * WROW + 4 * q;
           const uint32_t wb = smem_u32(w_ring + ws * W_STAGE) + rB * WROW + 4 * q;
           const uint32_t ab = smem_u32(a_ring + as * A_STAGE) + g * AROW + q * 16;
           const int jmax = min(8, (p.K - st * BK) >> 5);
-          const int grp0 = (st * BK) / p.gs;
           if (jmax == 8) {
             switch (ntl) {
               case 4: mma_stage<ZINT, 4, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc); break;
@@ -430,6 +443,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           mbar_arrive(&ctrl.w_empty[ws]);
           mbar_arrive(&ctrl.a_empty[as]);
         }
+        if (++wsl == static_cast<uint32_t>(sw)) { wsl = 0; wph ^= 1u; }
+        if (++asl == static_cast<uint32_t>(sa)) { asl = 0; aph ^= 1u; }
+        if (GPJ < 8) grp0 += 8 / GPJ;
+        else if (--spg_left == 0) { ++grp0; spg_left = spg; }
       }
       float res[NT][4];
 #pragma unroll
