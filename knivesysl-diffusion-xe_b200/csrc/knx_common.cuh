@@ -59,6 +59,14 @@ KNX_DEVINL uint32_t lds32(uint32_t addr) {
   asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(r) : "r"(addr));
   return r;
 }
+KNX_DEVINL __half lds16h(uint32_t addr) {
+  unsigned short r;
+  asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(r) : "r"(addr));
+  return __ushort_as_half(r);
+}
+KNX_DEVINL void sts16h(uint32_t addr, __half v) {
+  asm volatile("st.shared.u16 [%0], %1;\n" ::"r"(addr), "h"(__half_as_ushort(v)) : "memory");
+}
 KNX_DEVINL uint4 lds128(uint32_t addr) {
   uint4 r;
   asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n"

@@ -110,12 +110,16 @@ inline size_t smem_bytes(int ng, int sw, int sa) {
   return 1024 + static_cast<size_t>(sw) * W_STAGE + static_cast<size_t>(sa) * A_STAGE +
          ((OT_BYTES + 127) & ~127) + IR * sz_slot_bytes(ng);
 }
-// Ring depths that fit: the weight ring first (it streams from HBM; 4 stages = 128 KB in
-// flight), then the activation ring (its rows are L2-resident), each at least 2 stages.
+// Ring depths that fit, in order of preference: at least 3 activation stages (their copies come
+// from L2 but each is gathered token by token), then the deepest weight ring (it streams from
+// HBM; 4 stages = 128 KB in flight).  Measured on the configs[1] gate_up: 3 + 3 beats 4 + 2.
 inline bool ring_depths(int ng, int& sw, int& sa) {
-  for (sw = SW_MAX; sw >= 2; --sw)
-    for (sa = SA_MAX; sa >= 2; --sa)
-      if (smem_bytes(ng, sw, sa) + STATIC_RESERVE <= SMEM_LIMIT) return true;
+  static const int pref[][2] = {{4, 4}, {4, 3}, {3, 4}, {3, 3}, {4, 2}, {3, 2}, {2, 4}, {2, 3}, {2, 2}};
+  for (const auto& c : pref) {
+    sw = c[0];
+    sa = c[1];
+    if (smem_bytes(ng, sw, sa) + STATIC_RESERVE <= SMEM_LIMIT) return true;
+  }
   sw = sa = 0;
   return false;
 }
@@ -163,7 +167,7 @@ KNX_DEVINL void group_consts(__half s, __half z, __half2& s2, __half2& s16, __ha
 // hold at 4 token tiles).
 template <bool ZINT, int NTT, int GPJ, bool TAIL>
 KNX_DEVINL void mma_stage(uint32_t wa, uint32_t wb, uint32_t ab, int g, int jmax, int grp0,
-                          const __half* sA, const __half* zA, const __half* sB, const __half* zB,
+                          uint32_t sA, uint32_t zA, uint32_t sB, uint32_t zB,
                           float (&acc)[NT][NACC][4]) {
   constexpr int UJ = NACC >= 2 ? NACC / 2 : 1;
   static_assert(GPJ % UJ == 0 || UJ == 1, "accumulator sets must repeat within a group");
@@ -172,8 +176,8 @@ KNX_DEVINL void mma_stage(uint32_t wa, uint32_t wb, uint32_t ab, int g, int jmax
     if (TAIL && j0 >= jmax) break;
     __half2 sa2, sa16, ca2, ca16, sb2, sb16, cb2, cb16;
     const int grp = grp0 + j0 / GPJ;
-    group_consts<ZINT>(sA[grp], zA[grp], sa2, sa16, ca2, ca16);
-    group_consts<ZINT>(sB[grp], zB[grp], sb2, sb16, cb2, cb16);
+    group_consts<ZINT>(lds16h(sA + 2 * grp), lds16h(zA + 2 * grp), sa2, sa16, ca2, ca16);
+    group_consts<ZINT>(lds16h(sB + 2 * grp), lds16h(zB + 2 * grp), sb2, sb16, cb2, cb16);
 #pragma unroll
     for (int jj = 0; jj < GPJ; ++jj) {
       const int j = j0 + jj;
@@ -200,11 +204,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     hw_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const Params p) {
   extern __shared__ uint8_t dsm_raw[];
   __shared__ Ctrl ctrl;
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base (the 128-byte swizzle needs it), by an offset from dsm_raw so that the
+  // pointers derived from it stay recognisably shared
+  uint8_t* base = dsm_raw + ((1024u - (smem_u32(dsm_raw) & 1023u)) & 1023u);
   const int sw = p.sw, sa = p.sa;
   uint8_t* w_ring = base;
   uint8_t* a_ring = base + sw * W_STAGE;
-  __half* otile = reinterpret_cast<__half*>(a_ring + sa * A_STAGE);
+  const uint32_t ot = smem_u32(a_ring + sa * A_STAGE);  // output tile (shared address)
   uint8_t* sz_ring = a_ring + sa * A_STAGE + ((OT_BYTES + 127) & ~127);
   const size_t szr = sz_slot_bytes(p.ng);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -382,23 +388,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0 && got) mbar_arrive(&ctrl.i_empty[slot]);
         break;
       }
-      const __half* szs = reinterpret_cast<const __half*>(sz_ring + slot * szr);
-      const int ng = p.ng;
-      // scale/zero rows of this lane's two fragment rows
-      const __half* sA;
-      const __half* zA;
-      const __half* sB;
-      const __half* zB;
+      const uint32_t szs = smem_u32(sz_ring + slot * szr);
+      const uint32_t ng2 = static_cast<uint32_t>(p.ng) * 2u;  // bytes per scale/zero row
+      // shared addresses of the scale/zero rows of this lane's two fragment rows
+      uint32_t sA, zA, sB, zB;
       if (GATED) {
-        sA = szs + (8 * warp + g) * ng;
-        zA = sA + GROWS * ng;
-        sB = sA + 2 * GROWS * ng;
-        zB = sA + 3 * GROWS * ng;
+        sA = szs + (8 * warp + g) * ng2;
+        zA = sA + GROWS * ng2;
+        sB = sA + 2 * GROWS * ng2;
+        zB = sA + 3 * GROWS * ng2;
       } else {
-        sA = szs + (16 * warp + g) * ng;
-        zA = sA + ROWS * ng;
-        sB = sA + 8 * ng;
-        zB = zA + 8 * ng;
+        sA = szs + (16 * warp + g) * ng2;
+        zA = sA + ROWS * ng2;
+        sB = sA + 8 * ng2;
+        zB = zA + 8 * ng2;
       }
       const bool active = first_row < it.nvalid;
       const int ntl = (it.cnt + 7) >> 3;
@@ -469,10 +472,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const int tok = 8 * t + 2 * q + h;
               if (GATED) {
                 const float v = gelu_tanh(res[t][h]) * res[t][2 + h];
-                otile[tok * OT + perm_pos(8 * warp + g)] = __float2half_rn(v);
+                sts16h(ot + 2u * (tok * OT + perm_pos(8 * warp + g)), __float2half_rn(v));
               } else {
-                otile[tok * OT + 16 * warp + g] = __float2half_rn(res[t][h]);
-                otile[tok * OT + 16 * warp + 8 + g] = __float2half_rn(res[t][2 + h]);
+                sts16h(ot + 2u * (tok * OT + 16 * warp + g), __float2half_rn(res[t][h]));
+                sts16h(ot + 2u * (tok * OT + 16 * warp + 8 + g), __float2half_rn(res[t][2 + h]));
               }
             }
           }
@@ -486,7 +489,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const int t = c / vch, ch = c - t * vch;
           *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(it.slot0 + t) * p.out_stride +
                                     col0 + ch * 8) =
-              *reinterpret_cast<const uint4*>(otile + t * OT + ch * 8);
+              lds128(ot + 2u * (t * OT + ch * 8));
         }
       }
       __syncwarp();
