@@ -461,7 +461,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the configs[3] stack and configs[4] prefill measurements")
-    ap.add_argument("--only", choices=("layer", "sampler"), default=None,
+    ap.add_argument("--only", choices=("layer", "sampler", "prefill", "stack"), default=None,
                     help="run just one workload (used for profiling captures); prints its timing")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
@@ -484,6 +484,13 @@ def main():
         step_ms, kern_ms = time_sampler(dev)
         print(json.dumps({"only": "sampler", "step_us": step_ms * 1000.0,
                           "kernel_us": kern_ms * 1000.0}), flush=True)
+        return
+    if args.only == "prefill":
+        print(json.dumps({"only": "prefill", **time_prefill(dev, max(2, args.steps // 4), 0, 1)}),
+              flush=True)
+        return
+    if args.only == "stack":
+        print(json.dumps({"only": "stack", **time_stack(dev)}), flush=True)
         return
     if dist:
         import datetime

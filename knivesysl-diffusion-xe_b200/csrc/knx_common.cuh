@@ -59,6 +59,9 @@ KNX_DEVINL uint32_t lds32(uint32_t addr) {
   asm volatile("ld.shared.u32 %0, [%1];\n" : "=r"(r) : "r"(addr));
   return r;
 }
+KNX_DEVINL void sts32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
 KNX_DEVINL __half lds16h(uint32_t addr) {
   unsigned short r;
   asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(r) : "r"(addr));

@@ -370,9 +370,12 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
   extern __shared__ uint8_t sx_raw[];
   __shared__ SxCtrl c;
   __shared__ Part s_wpart[2][SX_WARPS];
-  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sx_raw) + 127) & ~uintptr_t(127));
-  int* cq_col = reinterpret_cast<int*>(ring + SX_RING * SX_BYTES);          // [SX_WARPS][SP_TILE]
-  float* cq_q = reinterpret_cast<float*>(cq_col + SX_WARPS * SP_TILE);     // [SX_WARPS][SP_TILE]
+  // 128-byte aligned ring, by an offset from sx_raw; the math warps read it and their candidate
+  // buffers through explicit shared-memory loads and stores (shared addresses)
+  uint8_t* ring = sx_raw + ((128u - (smem_u32(sx_raw) & 127u)) & 127u);
+  const uint32_t ring_s = smem_u32(ring);
+  const uint32_t cq_col = ring_s + SX_RING * SX_BYTES;      // int [SX_WARPS][SP_TILE]
+  const uint32_t cq_q = cq_col + SX_WARPS * SP_TILE * 4;    // float [SX_WARPS][SP_TILE]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t nitems = rows * nchunks;
   if (tid == 0) {
@@ -461,8 +464,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     uint32_t u = 0;
     const float L = LOG2E;
     int k = 0;
-    int* wcol = cq_col + warp * SP_TILE;   // this warp's deferred Gumbel candidates
-    float* wq = cq_q + warp * SP_TILE;
+    const uint32_t wcol = cq_col + warp * SP_TILE * 4;  // this warp's deferred Gumbel candidates
+    const uint32_t wq = cq_q + warp * SP_TILE * 4;
     for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++k) {
       const int64_t row = item / nchunks;
       const int chunk = static_cast<int>(item - row * nchunks);
@@ -496,8 +499,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
 #pragma unroll
           for (int r = 0; r < 4; ++r) {
             const int i = i0 + 32 * r + lane;
-            qv[r] = i < nbuf ? wq[i] : -INFINITY;
-            colv[r] = i < nbuf ? wcol[i] : 0;
+            qv[r] = i < nbuf ? __uint_as_float(lds32(wq + 4 * i)) : -INFINITY;
+            colv[r] = i < nbuf ? static_cast<int>(lds32(wcol + 4 * i)) : 0;
             wv[r] = qv[r] < thr_now ? 0u : philox_w0(static_cast<uint32_t>(colv[r]), k0, k1);
           }
 #pragma unroll
@@ -531,14 +534,15 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
         const int scols = min(SX_COLS, c_end - c0);
         const int base = warp * SP_TILE;  // this warp's columns inside the stage
         if (ok && base < scols) {
-          const float* sx = reinterpret_cast<const float*>(ring + slot * SX_BYTES);
+          const uint32_t sx = ring_s + slot * SX_BYTES;
           float q[16];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int cl = base + 128 * j + 4 * lane;
             if (cl < scols) {  // scols - cl is a multiple of 4
-              const float4 v = *reinterpret_cast<const float4*>(sx + cl);
-              q[4 * j] = v.x; q[4 * j + 1] = v.y; q[4 * j + 2] = v.z; q[4 * j + 3] = v.w;
+              const uint4 v = lds128(sx + 4 * cl);
+              q[4 * j] = __uint_as_float(v.x); q[4 * j + 1] = __uint_as_float(v.y);
+              q[4 * j + 2] = __uint_as_float(v.z); q[4 * j + 3] = __uint_as_float(v.w);
             } else {
               q[4 * j] = q[4 * j + 1] = q[4 * j + 2] = q[4 * j + 3] = -INFINITY;
             }
@@ -652,8 +656,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
                 if (cm & (1u << i)) {
-                  wcol[pos] = col0 + 128 * (i >> 2) + (i & 3);
-                  wq[pos] = q[i];
+                  sts32(wcol + 4 * pos, static_cast<uint32_t>(col0 + 128 * (i >> 2) + (i & 3)));
+                  sts32(wq + 4 * pos, __float_as_uint(q[i]));
                   ++pos;
                 }
               }
