@@ -8,6 +8,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "knx.h"
 
 #define KNX_DEVINL __device__ __forceinline__
@@ -23,9 +25,37 @@ inline int launch_status() {
   return e == cudaSuccess ? KNX_OK : KNX_E_LAUNCH;
 }
 
+// Programmatic dependent launch.  Every kernel of libknx.so is launched with launch_pdl, which
+// lets it start (CTA launch, prologue) while the previous kernel on the stream finishes, and calls
+// pdl_wait_trigger() before it touches global memory: that waits until the previous kernel has
+// completed and its writes are visible (at once when the previous launch was an ordinary one),
+// then allows the next kernel to start launching in turn.  The next kernel is only scheduled once
+// every CTA of this one has started, so an early start never takes an SM this kernel still needs.
+template <typename... KArgs, typename... Args>
+inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? KNX_OK
+                                                                                      : KNX_E_LAUNCH;
+}
+
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // ---- small PTX wrappers -------------------------------------------------------------------
+
+KNX_DEVINL void pdl_wait_trigger() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 KNX_DEVINL uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -21,6 +21,7 @@ namespace {
 // dst[i, :] = src[idx[i] / div, :] (16-byte vectors; idx < 0: a zero row)
 __global__ void gather_rows_kernel(const uint4* __restrict__ src, const int32_t* __restrict__ idx,
                                    int div, int64_t n, int vec_per_row, uint4* __restrict__ dst) {
+  pdl_wait_trigger();
   const int64_t i = blockIdx.y * static_cast<int64_t>(gridDim.x) + blockIdx.x;
   if (i >= n) return;
   const int r = idx[i];
@@ -41,6 +42,7 @@ constexpr int EPL_MAX = 4096;  // sources x local experts handled by the layout 
 __global__ void ep_layout_kernel(const int32_t* __restrict__ cnt, int S, int El, int64_t R,
                                  int32_t* __restrict__ offsets, int32_t* __restrict__ rows,
                                  int32_t* __restrict__ inv) {
+  pdl_wait_trigger();
   __shared__ int slot_base[EPL_MAX];  // [e][s]: first slot of (e, s)
   __shared__ int recv_base[EPL_MAX];  // [e][s]: first received row of (s, e)
   __shared__ int off[257];
@@ -132,8 +134,8 @@ extern "C" int knx_gather_rows(const void* src, int64_t src_rows, int64_t row_by
   const unsigned gx = static_cast<unsigned>(n < 65535 ? n : 65535);
   const unsigned gy = static_cast<unsigned>((n + gx - 1) / gx);
   const int threads = vpr < 256 ? ((vpr + 31) / 32) * 32 : 256;
-  gather_rows_kernel<<<dim3(gx, gy), threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint4*>(src), idx, div, n, vpr, static_cast<uint4*>(dst));
+  (void)launch_pdl(gather_rows_kernel, dim3(gx, gy), threads, 0, static_cast<cudaStream_t>(stream),
+                   static_cast<const uint4*>(src), idx, div, n, vpr, static_cast<uint4*>(dst));
   return launch_status();
 }
 
@@ -143,8 +145,8 @@ extern "C" int knx_ep_layout(const int32_t* recv_counts, int S, int El, int64_t 
   if (S <= 0 || S > 64 || El <= 0 || El > 256 || S * El > EPL_MAX || R < 0 || R > (1LL << 30))
     return KNX_E_INVALID;
   const int64_t blocks = R > 0 ? (R + 255) / 256 : 1;
-  ep_layout_kernel<<<static_cast<unsigned>(blocks < 1184 ? blocks : 1184), 256, 0,
-                     static_cast<cudaStream_t>(stream)>>>(recv_counts, S, El, R, offsets, rows, inv);
+  (void)launch_pdl(ep_layout_kernel, static_cast<unsigned>(blocks < 1184 ? blocks : 1184), 256, 0,
+                   static_cast<cudaStream_t>(stream), recv_counts, S, El, R, offsets, rows, inv);
   return launch_status();
 }
 

@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                        int* __restrict__ work_counter, const uint8_t* __restrict__ gu_q,
                        const __half* __restrict__ gu_s, const __half* __restrict__ gu_z, int H,
                        int I, int ng, int gs, __half* __restrict__ out2) {
+  pdl_wait_trigger();
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_tok[M_MAX];
   __shared__ int s_work;
@@ -267,6 +268,7 @@ __global__ void __launch_bounds__(THREADS, 2)
                      int* __restrict__ work_counter, const uint8_t* __restrict__ wq,
                      const __half* __restrict__ ws, const __half* __restrict__ wz, int N, int ng,
                      int gs, __half* __restrict__ out, int64_t out_stride) {
+  pdl_wait_trigger();
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int s_work;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -435,6 +437,7 @@ __global__ void __launch_bounds__(256)
     combine_kernel(const __half* __restrict__ out3, const int32_t* __restrict__ inv,
                    const void* __restrict__ w, int w_dtype, int topk, int H,
                    TO* __restrict__ y) {
+  pdl_wait_trigger();
   const int t = blockIdx.y;
   const int v = blockIdx.x * blockDim.x + threadIdx.x;  // 8-channel vector index
   if (v * 8 >= H) return;
@@ -607,9 +610,9 @@ int run_moe_gemms(const GemmArgs& a, int eng, int pc, cudaStream_t s) {
     const int64_t work = max_tasks * (I / G1_ROWS);
     const int grid = static_cast<int>(work < sms ? work : sms);
     auto kern = a.zint ? gateup_gelu_kernel<true> : gateup_gelu_kernel<false>;
-    kern<<<grid, THREADS, g1_smem(ng1), s>>>(a.xp, a.sorted_pair, a.topk, a.offsets, a.tasks,
-                                             a.ntasks, a.counters, a.gu_q, a.gu_s, a.gu_z, H, I,
-                                             ng1, a.gs_gu, a.out2);
+    (void)launch_pdl(kern, grid, THREADS, g1_smem(ng1), s, a.xp, a.sorted_pair, a.topk, a.offsets,
+                     a.tasks, a.ntasks, a.counters, a.gu_q, a.gu_s, a.gu_z, H, I, ng1, a.gs_gu,
+                     a.out2);
     st = launch_status();
     if (st != KNX_OK) return st;
   }
@@ -618,9 +621,9 @@ int run_moe_gemms(const GemmArgs& a, int eng, int pc, cudaStream_t s) {
     const int64_t work = max_tasks * ((H + G2_ROWS - 1) / G2_ROWS);
     const int grid = static_cast<int>(work < 2 * sms ? work : 2 * sms);
     auto kern = a.zint ? rows_gemm_kernel<true> : rows_gemm_kernel<false>;
-    kern<<<grid, THREADS, g2_smem(ng2), s>>>(a.out2, I, I, a.offsets, a.tasks, a.ntasks, 0,
-                                             a.counters + 1, a.dn_q, a.dn_s, a.dn_z, H, ng2,
-                                             a.gs_dn, a.out3, H);
+    (void)launch_pdl(kern, grid, THREADS, g2_smem(ng2), s, a.out2, I, I, a.offsets, a.tasks,
+                     a.ntasks, 0, a.counters + 1, a.dn_q, a.dn_s, a.dn_z, H, ng2, a.gs_dn, a.out3,
+                     H);
     return launch_status();
   }
 }
@@ -631,12 +634,16 @@ int launch_combine(const __half* out3, const int32_t* inv, const void* w, int w_
   const int Hi = static_cast<int>(H);
   if (out_dtype == KNX_F16) {
     __half* o = static_cast<__half*>(out);
-    if (topk == 8) combine_kernel<__half, 8><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, Hi, o);
-    else combine_kernel<__half, 0><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, Hi, o);
+    if (topk == 8) (void)launch_pdl(combine_kernel<__half, 8>, grid, 256, 0, s, out3, inv, w,
+                                    w_dtype, topk, Hi, o);
+    else (void)launch_pdl(combine_kernel<__half, 0>, grid, 256, 0, s, out3, inv, w, w_dtype, topk,
+                          Hi, o);
   } else {
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
-    if (topk == 8) combine_kernel<__nv_bfloat16, 8><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, Hi, o);
-    else combine_kernel<__nv_bfloat16, 0><<<grid, 256, 0, s>>>(out3, inv, w, w_dtype, topk, Hi, o);
+    if (topk == 8) (void)launch_pdl(combine_kernel<__nv_bfloat16, 8>, grid, 256, 0, s, out3, inv, w,
+                                    w_dtype, topk, Hi, o);
+    else (void)launch_pdl(combine_kernel<__nv_bfloat16, 0>, grid, 256, 0, s, out3, inv, w, w_dtype,
+                          topk, Hi, o);
   }
   return launch_status();
 }
@@ -770,9 +777,9 @@ extern "C" int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, 
   const int sms = num_sms();
   const int grid = static_cast<int>(work < 2 * sms ? work : 2 * sms);
   auto kern = zint ? rows_gemm_kernel<true> : rows_gemm_kernel<false>;
-  kern<<<grid, THREADS, g2_smem(ng), st>>>(
-      xp, K, static_cast<int>(K), nullptr, nullptr, nullptr, static_cast<int>(M), nullptr, q,
-      static_cast<const __half*>(s), static_cast<const __half*>(z), static_cast<int>(N), ng, gs,
-      static_cast<__half*>(Y), N);
+  (void)launch_pdl(kern, grid, THREADS, g2_smem(ng), st, xp, K, static_cast<int>(K), nullptr,
+                   nullptr, nullptr, static_cast<int>(M), nullptr, q, static_cast<const __half*>(s),
+                   static_cast<const __half*>(z), static_cast<int>(N), ng, gs,
+                   static_cast<__half*>(Y), N);
   return launch_status();
 }

@@ -202,6 +202,7 @@ KNX_DEVINL void mma_stage(uint32_t wa, uint32_t wb, uint32_t ab, int g, int jmax
 template <bool GATED, bool ZINT, int GPJ>
 __global__ void __launch_bounds__(NTHREADS, 1)
     hw_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const Params p) {
+  pdl_wait_trigger();
   extern __shared__ uint8_t dsm_raw[];
   __shared__ Ctrl ctrl;
   // 1024-byte aligned base (the 128-byte swizzle needs it), by an offset from dsm_raw so that the
@@ -539,7 +540,8 @@ int launch_hw_g(const hw::Params& p, const CUtensorMap& map, int grid, cudaStrea
       return KNX_E_DEVICE;
     attr[dev & 63] = true;
   }
-  hw::hw_gemm_kernel<GATED, ZINT, GPJ><<<grid, hw::NTHREADS, hw::smem_bytes(p.ng, p.sw, p.sa), s>>>(map, p);
+  (void)launch_pdl(hw::hw_gemm_kernel<GATED, ZINT, GPJ>, grid, hw::NTHREADS,
+                   hw::smem_bytes(p.ng, p.sw, p.sa), s, map, p);
   return launch_status();
 }
 

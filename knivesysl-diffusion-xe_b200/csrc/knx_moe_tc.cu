@@ -115,6 +115,7 @@ KNX_DEVINL int perm_pos(int n) { return (n & ~7) + 2 * (n & 3) + ((n >> 2) & 1);
 template <bool GATED, bool ZINT>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const Params p) {
+  pdl_wait_trigger();
   extern __shared__ uint8_t dsm_raw[];
   __shared__ Ctrl ctrl;
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
@@ -547,7 +548,7 @@ int launch_tc(const tc::Params& p, const uint8_t* wq, int64_t total_rows, int64_
   if (!encode_weight_map(&map, wq, total_rows, row_bytes, GATED ? 64 : tc::ROWS)) return KNX_E_DEVICE;
   const int sms = num_sms();
   const int grid = static_cast<int>(work_bound < sms ? (work_bound > 0 ? work_bound : 1) : sms);
-  tc::tc_gemm_kernel<GATED, ZINT><<<grid, tc::NTHREADS, smem, s>>>(map, p);
+  (void)launch_pdl(tc::tc_gemm_kernel<GATED, ZINT>, grid, tc::NTHREADS, smem, s, map, p);
   return launch_status();
 }
 

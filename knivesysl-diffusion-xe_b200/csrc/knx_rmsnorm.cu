@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(RMS_WARPS * 32)
     rmsnorm_kernel(const T* __restrict__ x, const void* __restrict__ w,
                    T* __restrict__ y, __half* __restrict__ xperm, int64_t rows, int cols,
                    float eps, bool round_bf16) {
+  pdl_wait_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RMS_WARPS + (threadIdx.x >> 5);
   if (row >= rows) return;
@@ -154,9 +155,9 @@ extern "C" int knx_rmsnorm(const void* x, const void* w, int w_dtype, void* y, v
   auto launch = [&](auto xt, auto wt) {
     using T = decltype(xt);
     using WT = std::remove_pointer_t<decltype(wt)>;
-    rmsnorm_kernel<T, WT><<<grid, RMS_WARPS * 32, 0, s>>>(
-        static_cast<const T*>(x), w, static_cast<T*>(y), static_cast<__half*>(xperm), rows,
-        static_cast<int>(cols), eps, rb);
+    (void)launch_pdl(rmsnorm_kernel<T, WT>, grid, RMS_WARPS * 32, 0, s, static_cast<const T*>(x), w,
+                     static_cast<T*>(y), static_cast<__half*>(xperm), rows, static_cast<int>(cols),
+                     eps, rb);
   };
   auto with_w = [&](auto xt) {
     if (w == nullptr) launch(xt, static_cast<void*>(nullptr));

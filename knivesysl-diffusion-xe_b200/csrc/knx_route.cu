@@ -22,6 +22,7 @@ constexpr int RT_ROWB = RT_BK * 2 + 16;  // 144-byte padded smem rows: conflict-
 __global__ void __launch_bounds__(128)
     router_logits_kernel(const __half* __restrict__ x, const __half* __restrict__ wr, int T,
                          int H, int E, float* __restrict__ part) {
+  pdl_wait_trigger();
   __shared__ __align__(16) uint8_t sx[2][RT_TOK * RT_ROWB];
   __shared__ __align__(16) uint8_t sw[2][RT_EXP * RT_ROWB];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(256)
     router_topk_kernel(const float* __restrict__ part, const float* __restrict__ bias, int T,
                        int E, int topk, float* __restrict__ logits_out, int32_t* __restrict__ ids,
                        float* __restrict__ weights) {
+  pdl_wait_trigger();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -214,6 +216,7 @@ __global__ void __launch_bounds__(AL_THREADS)
                  int32_t* __restrict__ padded_inv, int4* __restrict__ tasks,
                  int32_t* __restrict__ ntasks, int32_t* __restrict__ work_counters,
                  int n_work_counters, int32_t* __restrict__ err) {
+  pdl_wait_trigger();
   extern __shared__ __align__(16) uint8_t sm_raw[];
   const int N = T * topk;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -363,6 +366,7 @@ __global__ void __launch_bounds__(AL_THREADS)
 __global__ void tasks_from_offsets_kernel(const int32_t* __restrict__ offsets, int E, int m,
                                           int4* __restrict__ tasks, int32_t* __restrict__ ntasks,
                                           int32_t* __restrict__ counters) {
+  pdl_wait_trigger();
   __shared__ int full_pre[257];
   __shared__ int rem_of[256];
   __shared__ int rem_start[65];
@@ -408,6 +412,7 @@ __global__ void __launch_bounds__(AL_THREADS)
     align_large_count_kernel(const void* __restrict__ ids, int ids_dtype, int64_t N, int E,
                              int32_t* __restrict__ blkcnt, int32_t* __restrict__ lrank,
                              int32_t* __restrict__ err) {
+  pdl_wait_trigger();
   __shared__ int whist[32 * 256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t b0 = static_cast<int64_t>(blockIdx.x) * LB;
@@ -462,6 +467,7 @@ __global__ void __launch_bounds__(256)
     align_large_scan_kernel(const int32_t* __restrict__ blkcnt, int nblk, int E,
                             int32_t* __restrict__ blkbase, int32_t* __restrict__ counts,
                             int32_t* __restrict__ offsets) {
+  pdl_wait_trigger();
   __shared__ int tot[257];
   const int e = threadIdx.x;
   int c = 0;
@@ -497,6 +503,7 @@ __global__ void align_large_scatter_kernel(const void* __restrict__ ids, int ids
                                            const int32_t* __restrict__ offsets,
                                            int32_t* __restrict__ sorted_pair,
                                            int32_t* __restrict__ inv) {
+  pdl_wait_trigger();
   const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (p >= N) return;
   const int r = lrank[p];
@@ -514,6 +521,7 @@ __global__ void align_large_scatter_kernel(const void* __restrict__ ids, int ids
 // Activation copy into the MoE K-interleave (f16 out; f16 or bf16 in).  One thread per 16 bytes.
 template <typename T>
 __global__ void permute_act_kernel(const T* __restrict__ x, __half* __restrict__ xp, int64_t nvec) {
+  pdl_wait_trigger();
   const int64_t v = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (v >= nvec) return;
   const uint4 raw = ldg_nc_v4(reinterpret_cast<const uint4*>(x) + v);
@@ -559,10 +567,9 @@ int launch_align(const void* ids, int ids_dtype, int T, int topk, int E, int blo
     cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
     attr_set[dev & 63] = true;
   }
-  align_kernel<<<1, AL_THREADS, smem, stream>>>(ids, ids_dtype, T, topk, E, block_m, m_max, counts,
-                                                offsets, sorted_pair, inv, sorted_rows, expert_ids,
-                                                padded_inv, tasks, ntasks, work_counters,
-                                                n_work_counters, err);
+  (void)launch_pdl(align_kernel, 1, AL_THREADS, smem, stream, ids, ids_dtype, T, topk, E, block_m,
+                   m_max, counts, offsets, sorted_pair, inv, sorted_rows, expert_ids, padded_inv,
+                   tasks, ntasks, work_counters, n_work_counters, err);
   return launch_status();
 }
 
@@ -572,10 +579,11 @@ int launch_permute(const void* x, int dtype, __half* xp, int64_t elems, cudaStre
   const int threads = 256;
   const unsigned blocks = static_cast<unsigned>((nvec + threads - 1) / threads);
   if (dtype == KNX_F16) {
-    permute_act_kernel<__half><<<blocks, threads, 0, stream>>>(static_cast<const __half*>(x), xp, nvec);
+    (void)launch_pdl(permute_act_kernel<__half>, blocks, threads, 0, stream,
+                     static_cast<const __half*>(x), xp, nvec);
   } else {
-    permute_act_kernel<__nv_bfloat16>
-        <<<blocks, threads, 0, stream>>>(static_cast<const __nv_bfloat16*>(x), xp, nvec);
+    (void)launch_pdl(permute_act_kernel<__nv_bfloat16>, blocks, threads, 0, stream,
+                     static_cast<const __nv_bfloat16*>(x), xp, nvec);
   }
   return launch_status();
 }
@@ -594,17 +602,19 @@ int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t
   int32_t* lrank = static_cast<int32_t*>(scratch);
   int32_t* blkcnt = lrank + ((N + 63) & ~int64_t(63));
   int32_t* blkbase = blkcnt + static_cast<int64_t>(nblk) * E;
-  align_large_count_kernel<<<nblk, AL_THREADS, 0, s>>>(ids, ids_dtype, N, E, blkcnt, lrank, err);
-  align_large_scan_kernel<<<1, 256, 0, s>>>(blkcnt, nblk, E, blkbase, counts, offsets);
-  align_large_scatter_kernel<<<static_cast<unsigned>((N + 255) / 256), 256, 0, s>>>(
-      ids, ids_dtype, N, E, blkbase, lrank, offsets, sorted_pair, inv);
+  (void)launch_pdl(align_large_count_kernel, nblk, AL_THREADS, 0, s, ids, ids_dtype, N, E, blkcnt,
+                   lrank, err);
+  (void)launch_pdl(align_large_scan_kernel, 1, 256, 0, s, blkcnt, nblk, E, blkbase, counts,
+                   offsets);
+  (void)launch_pdl(align_large_scatter_kernel, static_cast<unsigned>((N + 255) / 256), 256, 0, s,
+                   ids, ids_dtype, N, E, blkbase, lrank, offsets, sorted_pair, inv);
   return launch_status();
 }
 
 int launch_tasks_from_offsets(const int32_t* offsets, int E, int m, int4* tasks, int32_t* ntasks,
                               int32_t* counters, cudaStream_t s) {
   if (E > 256 || m > 64) return KNX_E_UNSUPPORTED;
-  tasks_from_offsets_kernel<<<1, 256, 0, s>>>(offsets, E, m, tasks, ntasks, counters);
+  (void)launch_pdl(tasks_from_offsets_kernel, 1, 256, 0, s, offsets, E, m, tasks, ntasks, counters);
   return launch_status();
 }
 
@@ -631,13 +641,13 @@ extern "C" int knx_router_topk(const void* x, const void* wr, const float* bias,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   const dim3 g1(static_cast<unsigned>((T + RT_TOK - 1) / RT_TOK), E / RT_EXP, RT_KSPLIT);
-  router_logits_kernel<<<g1, 128, 0, s>>>(static_cast<const __half*>(x),
-                                          static_cast<const __half*>(wr), static_cast<int>(T),
-                                          static_cast<int>(H), E, part);
+  (void)launch_pdl(router_logits_kernel, g1, 128, 0, s, static_cast<const __half*>(x),
+                   static_cast<const __half*>(wr), static_cast<int>(T), static_cast<int>(H), E,
+                   part);
   int st = launch_status();
   if (st != KNX_OK) return st;
-  router_topk_kernel<<<static_cast<unsigned>((T + 7) / 8), 256, 0, s>>>(
-      part, bias, static_cast<int>(T), E, topk, logits_out, ids, weights);
+  (void)launch_pdl(router_topk_kernel, static_cast<unsigned>((T + 7) / 8), 256, 0, s, part, bias,
+                   static_cast<int>(T), E, topk, logits_out, ids, weights);
   return launch_status();
 }
 

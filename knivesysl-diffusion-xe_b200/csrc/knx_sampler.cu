@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
                    uint32_t* __restrict__ row_bound, int* __restrict__ work_counter,
                    float* __restrict__ entropy, int64_t* __restrict__ samp,
                    int64_t* __restrict__ amax) {
+  pdl_wait_trigger();
   __shared__ int s_item;
   __shared__ int s_last;
   __shared__ Part s_wpart[SP_WARPS];
@@ -366,6 +367,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
                           float rtemp, int do_div, int64_t seed, int seed_is32, int want_gumbel,
                           int nchunks, Part* __restrict__ parts, uint32_t* __restrict__ row_bound,
                           int* __restrict__ err) {
+  pdl_wait_trigger();
   using namespace sm100;
   extern __shared__ uint8_t sx_raw[];
   __shared__ SxCtrl c;
@@ -704,6 +706,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
 __global__ void row_merge_kernel(const Part* __restrict__ parts, int64_t rows, int nchunks,
                                  float* __restrict__ entropy, int64_t* __restrict__ samp,
                                  int64_t* __restrict__ amax) {
+  pdl_wait_trigger();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (row >= rows) return;
   const Part* pr = parts + row * nchunks;
@@ -727,6 +730,7 @@ __global__ void __launch_bounds__(1024)
                        uint8_t* __restrict__ mask, int64_t* __restrict__ out,
                        const int64_t* __restrict__ argmax, int64_t* __restrict__ history, int S,
                        float conf, uint8_t* __restrict__ finished) {
+  pdl_wait_trigger();
   __shared__ float sh[1024];
   __shared__ float sorted[1024];
   __shared__ uint8_t msorted[1024];
@@ -857,22 +861,20 @@ extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, f
     const int64_t sms = num_sms();
     const int sgrid = static_cast<int>(sitems < sms ? sitems : sms);
     int* dev_err = counter + 1;  // workspace word next to the counter, zeroed above
-    sampler_stream_kernel<<<sgrid, SX_THREADS, SX_SMEM, s>>>(
-        logits, rows, static_cast<int>(V), temperature, rtemp, do_div, seed, seed_is32, want_g,
-        nch_s, parts, bound, dev_err);
+    (void)launch_pdl(sampler_stream_kernel, sgrid, SX_THREADS, SX_SMEM, s, logits, rows,
+                     static_cast<int>(V), temperature, rtemp, do_div, seed, seed_is32, want_g,
+                     nch_s, parts, bound, dev_err);
     if (cudaGetLastError() != cudaSuccess) return KNX_E_LAUNCH;
-    row_merge_kernel<<<static_cast<unsigned>((rows + 127) / 128), 128, 0, s>>>(parts, rows, nch_s,
-                                                                             entropy, samp, amax);
+    (void)launch_pdl(row_merge_kernel, static_cast<unsigned>((rows + 127) / 128), 128, 0, s, parts,
+                     rows, nch_s, entropy, samp, amax);
   } else if (vec) {
-    sampler_kernel<true><<<grid, SP_THREADS, 0, s>>>(logits, rows, static_cast<int>(V),
-                                                     temperature, rtemp, do_div, seed, seed_is32,
-                                                     want_g, nch, ccols, parts, ticket, bound,
-                                                     counter, entropy, samp, amax);
+    (void)launch_pdl(sampler_kernel<true>, grid, SP_THREADS, 0, s, logits, rows,
+                     static_cast<int>(V), temperature, rtemp, do_div, seed, seed_is32, want_g, nch,
+                     ccols, parts, ticket, bound, counter, entropy, samp, amax);
   } else {
-    sampler_kernel<false><<<grid, SP_THREADS, 0, s>>>(logits, rows, static_cast<int>(V),
-                                                      temperature, rtemp, do_div, seed, seed_is32,
-                                                      want_g, nch, ccols, parts, ticket, bound,
-                                                      counter, entropy, samp, amax);
+    (void)launch_pdl(sampler_kernel<false>, grid, SP_THREADS, 0, s, logits, rows,
+                     static_cast<int>(V), temperature, rtemp, do_div, seed, seed_is32, want_g, nch,
+                     ccols, parts, ticket, bound, counter, entropy, samp, amax);
   }
   return launch_status();
 }
@@ -889,8 +891,9 @@ extern "C" int knx_accept_stop(const float* entropy, const int64_t* cur, const i
   if (out && (cur == nullptr || proposal == nullptr)) return KNX_E_INVALID;
   if (B == 0) return KNX_OK;
   const int threads = static_cast<int>(((L + 31) / 32) * 32);
-  accept_stop_kernel<<<static_cast<unsigned>(B), threads, 0, static_cast<cudaStream_t>(stream)>>>(
-      entropy, cur, proposal, static_cast<int>(B), static_cast<int>(L), entropy_bound, mask, out,
-      argmax, history, stability_threshold, confidence_threshold, finished);
+  (void)launch_pdl(accept_stop_kernel, static_cast<unsigned>(B), threads, 0,
+                   static_cast<cudaStream_t>(stream), entropy, cur, proposal, static_cast<int>(B),
+                   static_cast<int>(L), entropy_bound, mask, out, argmax, history,
+                   stability_threshold, confidence_threshold, finished);
   return launch_status();
 }
