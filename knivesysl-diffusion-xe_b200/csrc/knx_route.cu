@@ -14,37 +14,65 @@ namespace {
 
 // ------------------------------------------------------------------------------------------
 // Router logits: grid (ceil(T/32), E/32, RT_KSPLIT); each CTA computes a [32 token x 32 expert]
-// partial over one K split with m16n8k16 MMAs from a cp.async double buffer.  Partials go to
-// part[split][T][E]; the top-k kernel sums the splits in fixed order (deterministic).
+// partial over one K split with m16n8k16 MMAs.  The split's 64-k chunks stream through a
+// cp.async ring of up to RT_RING chunks, all issued up front (at H = 2816 the whole split is in
+// flight at once: one memory round trip instead of one per chunk); chunks are consumed in order.
+// Partials go to part[split][T][E]; the top-k kernel sums the splits in fixed order
+// (deterministic).
 constexpr int RT_TOK = 32, RT_EXP = 32, RT_BK = 64, RT_KSPLIT = 4;
 constexpr int RT_ROWB = RT_BK * 2 + 16;  // 144-byte padded smem rows: conflict-free u32 loads
+constexpr int RT_RING = 16;              // chunks in flight at most
+constexpr int RT_CHUNK_BYTES = (RT_TOK + RT_EXP) * RT_ROWB;
+
+// cp.async.wait_group with a run-time count (0..15): the instruction takes an immediate.
+KNX_DEVINL void cp_async_wait_upto(int n) {
+  switch (n) {
+    case 0: cp_async_wait<0>(); break;
+    case 1: cp_async_wait<1>(); break;
+    case 2: cp_async_wait<2>(); break;
+    case 3: cp_async_wait<3>(); break;
+    case 4: cp_async_wait<4>(); break;
+    case 5: cp_async_wait<5>(); break;
+    case 6: cp_async_wait<6>(); break;
+    case 7: cp_async_wait<7>(); break;
+    case 8: cp_async_wait<8>(); break;
+    case 9: cp_async_wait<9>(); break;
+    case 10: cp_async_wait<10>(); break;
+    case 11: cp_async_wait<11>(); break;
+    case 12: cp_async_wait<12>(); break;
+    case 13: cp_async_wait<13>(); break;
+    case 14: cp_async_wait<14>(); break;
+    default: cp_async_wait<15>(); break;
+  }
+}
 
 __global__ void __launch_bounds__(128)
     router_logits_kernel(const __half* __restrict__ x, const __half* __restrict__ wr, int T,
                          int H, int E, float* __restrict__ part) {
   pdl_wait_trigger();
-  __shared__ __align__(16) uint8_t sx[2][RT_TOK * RT_ROWB];
-  __shared__ __align__(16) uint8_t sw[2][RT_EXP * RT_ROWB];
+  extern __shared__ __align__(16) uint8_t rt_ring[];  // [ring][x rows | w rows]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
   const int t0 = blockIdx.x * RT_TOK, e0 = blockIdx.y * RT_EXP;
   const int kper = H / RT_KSPLIT;  // multiple of RT_BK (host checks H % 256 == 0)
   const int kbeg = blockIdx.z * kper;
   const int nchunk = kper / RT_BK;
+  const int ring = nchunk < RT_RING ? nchunk : RT_RING;
 
-  auto load = [&](int c, int buf) {
+  // chunk c -> ring slot c % ring: token rows then expert rows, RT_ROWB bytes each
+  auto load = [&](int c) {
+    uint8_t* slot = rt_ring + (c % ring) * RT_CHUNK_BYTES;
     const int k0 = kbeg + c * RT_BK;
     for (int i = tid; i < (RT_TOK + RT_EXP) * 8; i += 128) {
       const int r = i >> 3, ch = i & 7;
+      const __half* src;
       if (r < RT_TOK) {
         const int t = t0 + r;
-        cp_async16(&sx[buf][r * RT_ROWB + ch * 16],
-                   x + static_cast<int64_t>(t < T ? t : T - 1) * H + k0 + ch * 8);
+        src = x + static_cast<int64_t>(t < T ? t : T - 1) * H + k0 + ch * 8;
       } else {
-        const int e = e0 + r - RT_TOK;
-        cp_async16(&sw[buf][(r - RT_TOK) * RT_ROWB + ch * 16],
-                   wr + static_cast<int64_t>(e) * H + k0 + ch * 8);
+        src = wr + static_cast<int64_t>(e0 + r - RT_TOK) * H + k0 + ch * 8;
       }
+      cp_async16(slot + r * RT_ROWB + ch * 16, src);
     }
     cp_async_commit();
   };
@@ -52,16 +80,13 @@ __global__ void __launch_bounds__(128)
   // warp tile: tokens [16*(warp&1), +16) as MMA rows, experts [16*(warp>>1), +16) as 2 n8 tiles
   const int tm = 16 * (warp & 1), en = 16 * (warp >> 1);
   float acc[2][4] = {};
-  load(0, 0);
+  int issued = 0;
+  for (; issued < ring; ++issued) load(issued);
   for (int c = 0; c < nchunk; ++c) {
-    if (c + 1 < nchunk) {
-      load(c + 1, (c + 1) & 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+    cp_async_wait_upto(issued - 1 - c);  // chunk c has landed (newer chunks may be in flight)
     __syncthreads();
-    const uint32_t bx = smem_u32(sx[c & 1]), bw = smem_u32(sw[c & 1]);
+    const uint32_t bx = smem_u32(rt_ring + (c % ring) * RT_CHUNK_BYTES);
+    const uint32_t bw = bx + RT_TOK * RT_ROWB;
 #pragma unroll
     for (int ks = 0; ks < RT_BK / 16; ++ks) {
       const int kb = ks * 32 + q * 4;  // byte offset of k = 16*ks + 2q
@@ -76,7 +101,8 @@ __global__ void __launch_bounds__(128)
         mma_16816(acc[nt], a0, a1, a2, a3, b0, b1);
       }
     }
-    __syncthreads();
+    __syncthreads();  // every warp is done with the slot before it is refilled
+    if (issued < nchunk) load(issued++);
   }
   float* out = part + static_cast<int64_t>(blockIdx.z) * T * E;
 #pragma unroll
@@ -127,9 +153,10 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
   for (int i = 0; i < PER; ++i) den += (lane + 32 * i < E) ? expf(l[i] - mx) : 0.f;
   den = warp_sum(den);
-  // top-k selection: k rounds of a warp-wide (max value, min index) reduction
-  float psel[16];
-  int isel[16];
+  // top-k selection: k rounds of a warp-wide (max value, min index) reduction; lane k keeps
+  // selection k (topk <= 16), so nothing goes through local memory
+  float my_p = 0.f;
+  int my_i = 0;
   float psum = 0.f;
   for (int k = 0; k < topk; ++k) {
     float bv = -INFINITY;
@@ -155,15 +182,15 @@ __global__ void __launch_bounds__(256)
     for (int i = 0; i < PER; ++i)
       if (lane + 32 * i == bi) l[i] = -INFINITY;  // remove the winner
     const float p = expf(bv - mx) / den;
-    psel[k] = p;
-    isel[k] = bi;
+    if (lane == k) {
+      my_p = p;
+      my_i = bi;
+    }
     psum += p;
   }
-  if (lane == 0) {
-    for (int k = 0; k < topk; ++k) {
-      ids[static_cast<int64_t>(t) * topk + k] = isel[k];
-      weights[static_cast<int64_t>(t) * topk + k] = psel[k] / psum;
-    }
+  if (lane < topk) {
+    ids[static_cast<int64_t>(t) * topk + lane] = my_i;
+    weights[static_cast<int64_t>(t) * topk + lane] = my_p / psum;
   }
 }
 
@@ -176,36 +203,44 @@ __global__ void __launch_bounds__(256)
 // dynamic work counters.
 constexpr int AL_THREADS = 1024;
 
-__device__ __forceinline__ int* scnt_buf(int* whist, int) { return whist; }
-
-__device__ int block_excl_scan(int v, int* sbuf, int* total) {
-  // sbuf: >= 32 ints.  Exclusive scan over blockDim.x threads in thread order.
+// Exclusive scans of three values at once over blockDim.x threads in thread order (one pass, two
+// barriers).  sbuf: >= 99 ints.
+__device__ void block_excl_scan3(const int (&v)[3], int* sbuf, int (&ex)[3], int (&tot)[3]) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  int incl = v;
+  int incl[3] = {v[0], v[1], v[2]};
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
-    const int n = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += n;
+#pragma unroll
+    for (int k = 0; k < 3; ++k) {
+      const int n = __shfl_up_sync(0xffffffffu, incl[k], o);
+      if (lane >= o) incl[k] += n;
+    }
   }
-  if (lane == 31) sbuf[warp] = incl;
+  if (lane == 31)
+    for (int k = 0; k < 3; ++k) sbuf[33 * k + warp] = incl[k];
   __syncthreads();
   if (warp == 0) {
     const int nw = blockDim.x >> 5;
-    int wv = lane < nw ? sbuf[lane] : 0;
-    int wi = wv;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, wi, o);
-      if (lane >= o) wi += n;
+    for (int k = 0; k < 3; ++k) {
+      const int wv = lane < nw ? sbuf[33 * k + lane] : 0;
+      int wi = wv;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += n;
+      }
+      if (lane < nw) sbuf[33 * k + lane] = wi - wv;
+      if (lane == 31) sbuf[33 * k + 32] = wi;
     }
-    if (lane < nw) sbuf[lane] = wi - wv;
-    if (lane == 31) sbuf[32] = wi;
   }
   __syncthreads();
-  const int res = sbuf[warp] + incl - v;
-  if (total) *total = sbuf[32];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    ex[k] = sbuf[33 * k + warp] + incl[k] - v[k];
+    tot[k] = sbuf[33 * k + 32];
+  }
   __syncthreads();
-  return res;
 }
 
 __global__ void __launch_bounds__(AL_THREADS)
@@ -227,8 +262,10 @@ __global__ void __launch_bounds__(AL_THREADS)
   int* whist = reinterpret_cast<int*>(srank + npad);  // [32][E]
   int* soff = whist + 32 * E;                          // [E+1]
   int* spblk = soff + E + 1;                           // [E+1]
-  int* scan_buf = spblk + E + 1;                       // [33]
-  int* size_hist = scan_buf + 40;                      // [m_max+1]
+  int* scan_buf = spblk + E + 1;                       // [100]
+  int* size_hist = scan_buf + 100;                     // [m_max+1]
+  int* scnt = size_hist + m_max + 1;                   // [E] pairs per expert
+  int* rhist = scnt + E;                               // [8][65] remainder counts per warp
 
   for (int i = tid; i < 32 * E; i += AL_THREADS) whist[i] = 0;
   for (int i = tid; i <= m_max; i += AL_THREADS) size_hist[i] = 0;
@@ -262,25 +299,47 @@ __global__ void __launch_bounds__(AL_THREADS)
   }
   __syncthreads();
 
-  // per expert: exclusive prefix over warps (in place) and the expert's total count
+  // per expert: exclusive prefix of the 32 warps' counts (in place) and the expert's total.  C
+  // consecutive lanes share an expert (C = 8 for E <= 128, else 4), each summing 32 / C warps in
+  // order, then a segmented shuffle scan across the C lanes.
+  {
+    const int lc = E <= 128 ? 3 : 2;
+    const int C = 1 << lc, wpc = 32 >> lc;
+    const int e = tid >> lc, c = tid & (C - 1);
+    int part[8];
+    int run = 0;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      part[w] = run;
+      if (w < wpc && e < E) run += whist[(c * wpc + w) * E + e];
+    }
+    int incl = run;
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o, C);
+      if (o < C && c >= o) incl += n;
+    }
+    const int excl = incl - run;
+#pragma unroll
+    for (int w = 0; w < 8; ++w)
+      if (w < wpc && e < E) whist[(c * wpc + w) * E + e] = excl + part[w];
+    const int tot = __shfl_sync(0xffffffffu, incl, C - 1, C);
+    if (c == 0 && e < E) scnt[e] = tot;
+  }
+  __syncthreads();
+
   int cnt = 0, nblk = 0, nfull = 0, rem = 0;
   const int e_me = tid;  // E <= AL_THREADS
   if (e_me < E) {
-    int run = 0;
-    for (int w = 0; w < 32; ++w) {
-      const int c = whist[w * E + e_me];
-      whist[w * E + e_me] = run;
-      run += c;
-    }
-    cnt = run;
+    cnt = scnt[e_me];
     nblk = block_m > 0 ? (cnt + block_m - 1) / block_m : 0;
     nfull = cnt / m_max;
     rem = cnt % m_max;
   }
-  int total_valid = 0, total_blk = 0, total_full = 0;
-  const int off = block_excl_scan(cnt, scan_buf, &total_valid);
-  const int pblk = block_excl_scan(nblk, scan_buf, &total_blk);
-  const int fpre = block_excl_scan(nfull, scan_buf, &total_full);
+  int ex[3], tot3[3];
+  block_excl_scan3({cnt, nblk, nfull}, scan_buf, ex, tot3);
+  const int off = ex[0], pblk = ex[1], fpre = ex[2];
+  const int total_valid = tot3[0], total_blk = tot3[1], total_full = tot3[2];
   if (e_me < E) {
     soff[e_me] = off;
     spblk[e_me] = pblk;
@@ -335,25 +394,39 @@ __global__ void __launch_bounds__(AL_THREADS)
 
   // task list: sizes descending; size_hist[s] becomes the number of tasks with size > s
   if (tasks) {
-    __syncthreads();  // placement above still reads whist
-    if (tid == 0) {
-      int run = 0;
-      for (int s = m_max; s >= 1; --s) {
-        const int h = size_hist[s];
-        size_hist[s] = run;
-        run += h;
+    for (int i = tid; i < 8 * 65; i += AL_THREADS) rhist[i] = 0;
+    __syncthreads();  // placement above still reads whist; rhist zeroed
+    // rank of this expert's remainder task among the experts with the same remainder, in expert
+    // order: lanes of one warp by __match_any_sync, earlier warps through rhist
+    const int r = (e_me < E && rem > 0) ? rem : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, r);
+    const int rank_w = __popc(peers & lt_mask);
+    if (r > 0 && lane == __ffs(peers) - 1) rhist[warp * 65 + r] = __popc(peers);
+    __syncthreads();
+    if (warp == 0) {
+      // reverse exclusive scan over sizes s = m_max .. 1 (position i = m_max - s), two per lane
+      const int i0 = 2 * lane, i1 = i0 + 1;
+      const int v0 = i0 < m_max ? size_hist[m_max - i0] : 0;
+      const int v1 = i1 < m_max ? size_hist[m_max - i1] : 0;
+      const int a = v0 + v1;
+      int incl = a;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
       }
-      *ntasks = run;
+      const int base = incl - a;
+      if (i0 < m_max) size_hist[m_max - i0] = base;
+      if (i1 < m_max) size_hist[m_max - i1] = base + v0;
+      if (lane == 31) *ntasks = incl;
     }
-    if (e_me < E) scnt_buf(whist, E)[e_me] = cnt;  // whist is free again: reuse as count table
     __syncthreads();
     if (e_me < E && cnt > 0) {
       for (int j = 0; j < nfull; ++j)
         tasks[size_hist[m_max] + fpre + j] = make_int4(e_me, j * m_max, m_max, 0);
       if (rem > 0) {
-        const int* sc = scnt_buf(whist, E);
-        int before_same = 0;
-        for (int e2 = 0; e2 < e_me; ++e2) before_same += (sc[e2] % m_max) == rem;
+        int before_same = rank_w;
+        for (int w2 = 0; w2 < warp; ++w2) before_same += rhist[w2 * 65 + rem];
         tasks[size_hist[rem] + before_same] = make_int4(e_me, nfull * m_max, rem, 0);
       }
     }
@@ -546,7 +619,8 @@ constexpr int RT_KSPLIT_PUBLIC = RT_KSPLIT;
 
 size_t align_smem_bytes(int N, int E, int m_max) {
   const int npad = (N + 7) & ~7;
-  return static_cast<size_t>(npad) * 4 + static_cast<size_t>(32 * E + 2 * (E + 1) + 40 + m_max + 1) * 4;
+  return static_cast<size_t>(npad) * 4 +
+         static_cast<size_t>(32 * E + 2 * (E + 1) + 100 + m_max + 1 + E + 8 * 65) * 4;
 }
 
 bool align_supported(int64_t N, int E) {
@@ -559,6 +633,7 @@ int launch_align(const void* ids, int ids_dtype, int T, int topk, int E, int blo
                  int32_t* ntasks, int32_t* work_counters, int n_work_counters, int32_t* err,
                  cudaStream_t stream) {
   const int N = T * topk;
+  if (tasks && (m_max < 1 || m_max > 64)) return KNX_E_UNSUPPORTED;  // task sizes: one warp scan
   const size_t smem = align_smem_bytes(N, E, m_max);
   static bool attr_set[64] = {};
   int dev = 0;
@@ -641,7 +716,18 @@ extern "C" int knx_router_topk(const void* x, const void* wr, const float* bias,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   float* part = static_cast<float*>(workspace);
   const dim3 g1(static_cast<unsigned>((T + RT_TOK - 1) / RT_TOK), E / RT_EXP, RT_KSPLIT);
-  (void)launch_pdl(router_logits_kernel, g1, 128, 0, s, static_cast<const __half*>(x),
+  const int nchunk = static_cast<int>(H / RT_KSPLIT / RT_BK);
+  const size_t smem = static_cast<size_t>(nchunk < RT_RING ? nchunk : RT_RING) * RT_CHUNK_BYTES;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             RT_RING * RT_CHUNK_BYTES) != cudaSuccess)
+      return KNX_E_DEVICE;
+    attr_set[dev & 63] = true;
+  }
+  (void)launch_pdl(router_logits_kernel, g1, 128, smem, s, static_cast<const __half*>(x),
                    static_cast<const __half*>(wr), static_cast<int>(T), static_cast<int>(H), E,
                    part);
   int st = launch_status();
