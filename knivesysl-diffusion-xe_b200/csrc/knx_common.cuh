@@ -92,6 +92,13 @@ KNX_DEVINL uint32_t lds32(uint32_t addr) {
 KNX_DEVINL void sts32(uint32_t addr, uint32_t v) {
   asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
 }
+// 32-bit shared load at addr + OFF (the offset folded into the instruction's immediate)
+template <int OFF>
+KNX_DEVINL uint32_t lds32_at(uint32_t addr) {
+  uint32_t r;
+  asm volatile("ld.shared.u32 %0, [%1+%2];\n" : "=r"(r) : "r"(addr), "n"(OFF));
+  return r;
+}
 KNX_DEVINL __half lds16h(uint32_t addr) {
   unsigned short r;
   asm volatile("ld.shared.u16 %0, [%1];\n" : "=h"(r) : "r"(addr));

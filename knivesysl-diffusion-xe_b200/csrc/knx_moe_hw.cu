@@ -20,12 +20,13 @@
 //     the task's 1-4 n8 token tiles, so one dequantisation serves up to 32 tokens.  No split-K:
 //     every output is one warp's fixed-order sum (deterministic), and a token's sum does not
 //     depend on the other tokens of its task.
-//   * GELU(gate) * up (gated) or the plain result goes through a shared-memory tile to
-//     coalesced 16-byte stores; the gated output is written in the K-interleave the down GEMM
-//     reads.
+//   * GELU(gate) * up (gated) or the plain result: each warp stages its own 8 (gated) or 16
+//     output columns per token in a private shared area and writes 16-byte chunks, so the math
+//     warps never wait for one another; the gated output is written in the K-interleave the
+//     down GEMM reads.
 // All waits are bounded (2 s): on a timeout the kernel sets KNX_DEV_TIMEOUT and every role
-// leaves at the next work-item boundary (the math warps agree through bar.red first); the
-// producers wait (bounded) for their copies in flight before the CTA exits.
+// leaves at the next work-item boundary (each math warp decides by a warp vote); the producers
+// wait (bounded) for their copies in flight before the CTA exits.
 #include "knx_common.cuh"
 #include "knx_internal.cuh"
 #include "knx_sm100.cuh"
@@ -51,8 +52,8 @@ constexpr int NUM_WARPS = MATH_WARPS + 2;
 constexpr int NTHREADS = NUM_WARPS * 32;
 constexpr int WARP_WPROD = MATH_WARPS, WARP_APROD = MATH_WARPS + 1;
 constexpr int SZ_MAX = 32;               // groups per row
-constexpr int OT = ROWS + 8;             // output tile row (halfs)
-constexpr int OT_BYTES = TOK * OT * 2;
+// per-warp output staging: 8 (gated) or 16 (plain) columns x 32 tokens of f16 per warp
+constexpr int ot_bytes(bool gated) { return MATH_WARPS * TOK * (gated ? 8 : 16) * 2; }
 constexpr size_t SMEM_LIMIT = 232448;    // 227 KB opt-in per block
 constexpr size_t STATIC_RESERVE = 1024;  // Ctrl + alignment of the dynamic base
 
@@ -106,36 +107,22 @@ struct Params {
 };
 
 KNX_HOST_DEVINL size_t sz_slot_bytes(int ng) { return static_cast<size_t>(ROWS) * ng * 4; }
-inline size_t smem_bytes(int ng, int sw, int sa) {
+inline size_t smem_bytes(bool gated, int ng, int sw, int sa) {
   return 1024 + static_cast<size_t>(sw) * W_STAGE + static_cast<size_t>(sa) * A_STAGE +
-         ((OT_BYTES + 127) & ~127) + IR * sz_slot_bytes(ng);
+         ot_bytes(gated) + IR * sz_slot_bytes(ng);
 }
 // Ring depths that fit, in order of preference: at least 3 activation stages (their copies come
 // from L2 but each is gathered token by token), then the deepest weight ring (it streams from
 // HBM; 4 stages = 128 KB in flight).  Measured on the configs[1] gate_up: 3 + 3 beats 4 + 2.
-inline bool ring_depths(int ng, int& sw, int& sa) {
+inline bool ring_depths(bool gated, int ng, int& sw, int& sa) {
   static const int pref[][2] = {{4, 4}, {4, 3}, {3, 4}, {3, 3}, {4, 2}, {3, 2}, {2, 4}, {2, 3}, {2, 2}};
   for (const auto& c : pref) {
     sw = c[0];
     sa = c[1];
-    if (smem_bytes(ng, sw, sa) + STATIC_RESERVE <= SMEM_LIMIT) return true;
+    if (smem_bytes(gated, ng, sw, sa) + STATIC_RESERVE <= SMEM_LIMIT) return true;
   }
   sw = sa = 0;
   return false;
-}
-
-KNX_DEVINL void named_bar(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
-// Named barrier that also ORs a predicate over the participating threads: every thread gets the
-// same answer, so warps that decide together whether to leave cannot disagree.
-KNX_DEVINL bool bar_any(int id, int n, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %3, 0;\n\tbar.red.or.pred p, %1, %2, q;\n\t"
-      "selp.u32 %0, 1, 0, p;\n\t}"
-      : "=r"(r)
-      : "r"(id), "r"(n), "r"(static_cast<uint32_t>(v))
-      : "memory");
-  return r != 0;
 }
 
 KNX_DEVINL float gelu_tanh(float x) {
@@ -165,8 +152,11 @@ KNX_DEVINL void group_consts(__half s, __half z, __half2& s2, __half2& s16, __ha
 // groups that span several stages): the steps of one group are unrolled, the groups are a loop
 // (unrolling across groups lets the scheduler keep more steps in flight than 112 registers
 // hold at 4 token tiles).
-template <bool ZINT, int NTT, int GPJ, bool TAIL>
-KNX_DEVINL void mma_stage(uint32_t wa, uint32_t wb, uint32_t ab, int g, int jmax, int grp0,
+// wa: shared address of the lane's word of fragment row A in chunk 0 with the row's swizzle
+// applied (stage base + row * 128 + (g << 4) + 4q): chunk j of the row is at wa ^ (j << 4).
+// Fragment row B lies BOFF bytes further (same swizzle phase).
+template <bool ZINT, int NTT, int GPJ, bool TAIL, int BOFF>
+KNX_DEVINL void mma_stage(uint32_t wa, uint32_t ab, int jmax, int grp0,
                           uint32_t sA, uint32_t zA, uint32_t sB, uint32_t zB,
                           float (&acc)[NT][NACC][4]) {
   constexpr int UJ = NACC >= 2 ? NACC / 2 : 1;
@@ -182,10 +172,10 @@ KNX_DEVINL void mma_stage(uint32_t wa, uint32_t wb, uint32_t ab, int g, int jmax
     for (int jj = 0; jj < GPJ; ++jj) {
       const int j = j0 + jj;
       if (!TAIL || j < jmax) {
-        const uint32_t sw_off = static_cast<uint32_t>((j ^ g) << 4);
+        const uint32_t aj = wa ^ static_cast<uint32_t>(j << 4);
         uint32_t fa[4], fb[4];
-        dequant8<ZINT>(lds32(wa + sw_off), sa2, sa16, ca2, ca16, fa);
-        dequant8<ZINT>(lds32(wb + sw_off), sb2, sb16, cb2, cb16, fb);
+        dequant8<ZINT>(lds32(aj), sa2, sa16, ca2, ca16, fa);
+        dequant8<ZINT>(lds32_at<BOFF>(aj), sb2, sb16, cb2, cb16, fb);
 #pragma unroll
         for (int t = 0; t < NTT; ++t) {
           const uint4 b = lds128(ab + t * 8 * AROW + j * 64);
@@ -212,7 +202,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint8_t* w_ring = base;
   uint8_t* a_ring = base + sw * W_STAGE;
   const uint32_t ot = smem_u32(a_ring + sa * A_STAGE);  // output tile (shared address)
-  uint8_t* sz_ring = a_ring + sa * A_STAGE + ((OT_BYTES + 127) & ~127);
+  uint8_t* sz_ring = a_ring + sa * A_STAGE + ot_bytes(GATED);
   const size_t szr = sz_slot_bytes(p.ng);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nst = (p.K + BK - 1) / BK;
@@ -374,17 +364,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // smem rows of this lane's two fragment rows (tile rows g and g+8); both are = g (mod 8),
     // which the 128-byte swizzle uses: 16-byte chunk j of row r sits at chunk j ^ (r & 7)
     const int rA = GATED ? 8 * warp + g : 16 * warp + g;
-    const int rB = GATED ? GROWS + 8 * warp + g : 16 * warp + 8 + g;
+    constexpr int BOFF = (GATED ? GROWS : 8) * WROW;  // row B = row A + GROWS (gated) or + 8
     const int first_row = GATED ? 8 * warp : 16 * warp;  // tile's first row (validity)
     // ring slots and phase parities, carried across items (no runtime divisions in the loop)
     uint32_t wsl = 0, wph = 0, asl = 0, aph = 0;
     const int spg = GPJ < 8 ? 1 : p.gs / BK;  // stages per scale group when groups span stages
     for (int n = 0;; ++n) {
       const int slot = n % IR;
-      const bool got = wait(&ctrl.i_full[slot], (n / IR) & 1, 64);
+      const bool got = __all_sync(0xffffffffu, wait(&ctrl.i_full[slot], (n / IR) & 1, 64));
       const Item it = ctrl.items[slot];
-      // all math warps leave together (the named barriers below need every one of them)
-      if (bar_any(2, MATH_WARPS * 32, !got || !it.valid || *abort_flag)) {
+      // each warp decides alone (no barrier among the math warps inside the loop); the vote
+      // keeps the lanes of a warp together
+      if (__any_sync(0xffffffffu, !got || !it.valid || *abort_flag)) {
         __syncwarp();
         if (lane == 0 && got) mbar_arrive(&ctrl.i_empty[slot]);
         break;
@@ -422,23 +413,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const bool ready = __all_sync(0xffffffffu, wait(&ctrl.w_full[ws], wph) &&
                                                        wait(&ctrl.a_full[as], aph));
         if (ready && active) {
-          const uint32_t wa = smem_u32(w_ring + ws * W_STAGE) + rA * WROW + 4 * q;
-          const uint32_t wb = smem_u32(w_ring + ws * W_STAGE) + rB * WROW + 4 * q;
+          const uint32_t wa = smem_u32(w_ring + ws * W_STAGE) + rA * WROW + (g << 4) + 4 * q;
           const uint32_t ab = smem_u32(a_ring + as * A_STAGE) + g * AROW + q * 16;
           const int jmax = min(8, (p.K - st * BK) >> 5);
           if (jmax == 8) {
             switch (ntl) {
-              case 4: mma_stage<ZINT, 4, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc); break;
-              case 3: mma_stage<ZINT, 3, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc); break;
-              case 2: mma_stage<ZINT, 2, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc); break;
-              default: mma_stage<ZINT, 1, GPJ, false>(wa, wb, ab, g, 8, grp0, sA, zA, sB, zB, acc);
+              case 4: mma_stage<ZINT, 4, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, zA, sB, zB, acc); break;
+              case 3: mma_stage<ZINT, 3, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, zA, sB, zB, acc); break;
+              case 2: mma_stage<ZINT, 2, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, zA, sB, zB, acc); break;
+              default: mma_stage<ZINT, 1, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, zA, sB, zB, acc);
             }
           } else {
             switch (ntl) {
-              case 4: mma_stage<ZINT, 4, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc); break;
-              case 3: mma_stage<ZINT, 3, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc); break;
-              case 2: mma_stage<ZINT, 2, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc); break;
-              default: mma_stage<ZINT, 1, GPJ, true>(wa, wb, ab, g, jmax, grp0, sA, zA, sB, zB, acc);
+              case 4: mma_stage<ZINT, 4, GPJ, true, BOFF>(wa, ab, jmax, grp0, sA, zA, sB, zB, acc); break;
+              case 3: mma_stage<ZINT, 3, GPJ, true, BOFF>(wa, ab, jmax, grp0, sA, zA, sB, zB, acc); break;
+              case 2: mma_stage<ZINT, 2, GPJ, true, BOFF>(wa, ab, jmax, grp0, sA, zA, sB, zB, acc); break;
+              default: mma_stage<ZINT, 1, GPJ, true, BOFF>(wa, ab, jmax, grp0, sA, zA, sB, zB, acc);
             }
           }
         }
@@ -462,8 +452,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int u = 1; u < NACC; ++u) v += acc[t][u][i];
           res[t][i] = v;
         }
-      // ---- epilogue: shared tile -> coalesced 16-byte stores
-      named_bar(1, MATH_WARPS * 32);  // the previous item's stores have read the tile
+      // ---- epilogue: each warp stages its own columns (gated: 8 per token, the K-interleave
+      // inside the 8-group; plain: 16) in a private shared area, then writes 16-byte chunks
+      constexpr int WCOLS = GATED ? 8 : 16;
+      const uint32_t stg = ot + static_cast<uint32_t>(warp) * (TOK * WCOLS * 2);
+      __syncwarp();  // this warp's reads of the previous item's staging are done
       if (active) {
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -473,24 +466,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               const int tok = 8 * t + 2 * q + h;
               if (GATED) {
                 const float v = gelu_tanh(res[t][h]) * res[t][2 + h];
-                sts16h(ot + 2u * (tok * OT + perm_pos(8 * warp + g)), __float2half_rn(v));
+                sts16h(stg + 2u * (tok * WCOLS + perm_pos(g)), __float2half_rn(v));
               } else {
-                sts16h(ot + 2u * (tok * OT + 16 * warp + g), __float2half_rn(res[t][h]));
-                sts16h(ot + 2u * (tok * OT + 16 * warp + 8 + g), __float2half_rn(res[t][2 + h]));
+                sts16h(stg + 2u * (tok * WCOLS + g), __float2half_rn(res[t][h]));
+                sts16h(stg + 2u * (tok * WCOLS + 8 + g), __float2half_rn(res[t][2 + h]));
               }
             }
           }
         }
       }
-      named_bar(1, MATH_WARPS * 32);
-      {
-        const int vch = it.nvalid >> 3;  // 16-byte chunks per token row
-        const int col0 = GATED ? it.slice * GROWS : it.slice * ROWS;
-        for (int c = tid; c < it.cnt * vch; c += MATH_WARPS * 32) {
-          const int t = c / vch, ch = c - t * vch;
+      __syncwarp();
+      if (active) {
+        const int col0 = (GATED ? it.slice * GROWS : it.slice * ROWS) + first_row;
+        for (int c = lane; c < it.cnt * (WCOLS / 8); c += 32) {
+          const int t = GATED ? c : c >> 1, ch = GATED ? 0 : c & 1;
           *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(it.slot0 + t) * p.out_stride +
-                                    col0 + ch * 8) =
-              lds128(ot + 2u * (t * OT + ch * 8));
+                                    col0 + ch * 8) = lds128(stg + 16u * c);
         }
       }
       __syncwarp();
@@ -541,14 +532,14 @@ int launch_hw_g(const hw::Params& p, const CUtensorMap& map, int grid, cudaStrea
     attr[dev & 63] = true;
   }
   (void)launch_pdl(hw::hw_gemm_kernel<GATED, ZINT, GPJ>, grid, hw::NTHREADS,
-                   hw::smem_bytes(p.ng, p.sw, p.sa), s, map, p);
+                   hw::smem_bytes(GATED, p.ng, p.sw, p.sa), s, map, p);
   return launch_status();
 }
 
 template <bool GATED, bool ZINT>
 int launch_hw(hw::Params p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
               int64_t work_bound, cudaStream_t s) {
-  if (!hw::ring_depths(p.ng, p.sw, p.sa)) return KNX_E_UNSUPPORTED;
+  if (!hw::ring_depths(GATED, p.ng, p.sw, p.sa)) return KNX_E_UNSUPPORTED;
   CUtensorMap map;
   if (!encode_map_hw(&map, wq, total_rows, row_bytes)) return KNX_E_DEVICE;
   const int sms = num_sms();
@@ -567,7 +558,7 @@ bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated
   // scale groups must not straddle a 256-k stage unless they cover whole stages
   if (!(gs == 32 || gs == 64 || gs == 128 || (gs > 0 && gs % 256 == 0))) return false;
   int sw, sa;
-  if (ng > hw::SZ_MAX || (K % 64) != 0 || !hw::ring_depths(ng, sw, sa)) return false;
+  if (ng > hw::SZ_MAX || (K % 64) != 0 || !hw::ring_depths(gated, ng, sw, sa)) return false;
   if (gated) return (rows_per_expert / 2) % 64 == 0;
   return rows_per_expert % 16 == 0;
 }
