@@ -334,8 +334,11 @@ constexpr int SX_CHUNK = 8 * SX_COLS;       // columns per work item
 constexpr int SX_RING = 4;
 constexpr int SX_WARPS = 16;                // math warps
 constexpr int SX_THREADS = (SX_WARPS + 3) * 32;
+// deferred Gumbel candidates per warp: flushed as soon as 32 are pending, so a tile (at most
+// SP_TILE candidates) always fits on top of the at most 31 left over
+constexpr int SX_CQ = SP_TILE + 32;
 constexpr size_t SX_SMEM = 128 + static_cast<size_t>(SX_RING) * SX_BYTES +
-                           static_cast<size_t>(SX_WARPS) * SP_TILE * 8;
+                           static_cast<size_t>(SX_WARPS) * SX_CQ * 8;
 
 struct SxCtrl {
   uint64_t full[SX_RING], empty[SX_RING];
@@ -376,8 +379,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
   // buffers through explicit shared-memory loads and stores (shared addresses)
   uint8_t* ring = sx_raw + ((128u - (smem_u32(sx_raw) & 127u)) & 127u);
   const uint32_t ring_s = smem_u32(ring);
-  const uint32_t cq_col = ring_s + SX_RING * SX_BYTES;      // int [SX_WARPS][SP_TILE]
-  const uint32_t cq_q = cq_col + SX_WARPS * SP_TILE * 4;    // float [SX_WARPS][SP_TILE]
+  const uint32_t cq_col = ring_s + SX_RING * SX_BYTES;      // int [SX_WARPS][SX_CQ]
+  const uint32_t cq_q = cq_col + SX_WARPS * SX_CQ * 4;      // float [SX_WARPS][SX_CQ]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t nitems = rows * nchunks;
   if (tid == 0) {
@@ -466,8 +469,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     uint32_t u = 0;
     const float L = LOG2E;
     int k = 0;
-    const uint32_t wcol = cq_col + warp * SP_TILE * 4;  // this warp's deferred Gumbel candidates
-    const uint32_t wq = cq_q + warp * SP_TILE * 4;
+    const uint32_t wcol = cq_col + warp * SX_CQ * 4;  // this warp's deferred Gumbel candidates
+    const uint32_t wq = cq_q + warp * SX_CQ * 4;
     for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++k) {
       const int64_t row = item / nchunks;
       const int chunk = static_cast<int>(item - row * nchunks);
@@ -653,7 +656,6 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
                 if (lane >= o) incl += y;
               }
               const int total = __shfl_sync(0xffffffffu, incl, 31);
-              if (nbuf + total > SP_TILE) flush();
               int pos = nbuf + incl - n;
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
