@@ -40,7 +40,7 @@ NSETS = 4
 GEMM1_KERNEL = {"tc": "tc_gemm_kernel<1,0> (gate_up + GELU)",
                 "ws": "hw_gemm_kernel<1,0,4> (gate_up + GELU)",
                 "mma": "gateup_gelu_kernel"}
-GEMM1_NCU_TRAFFIC = {"tc": 276.584960e6 + 6.810624e6, "ws": 356.699904e6 + 8.211712e6}
+GEMM1_NCU_TRAFFIC = {"tc": 276.584960e6 + 6.810624e6, "ws": 288.256512e6 + 5.845248e6}
 
 
 def peaks():
