@@ -334,9 +334,20 @@ constexpr int SX_CHUNK = 8 * SX_COLS;       // columns per work item
 constexpr int SX_RING = 4;
 constexpr int SX_WARPS = 16;                // math warps
 constexpr int SX_THREADS = (SX_WARPS + 3) * 32;
-// deferred Gumbel candidates per warp: flushed as soon as 32 are pending, so a tile (at most
-// SP_TILE candidates) always fits on top of the at most 31 left over
-constexpr int SX_CQ = SP_TILE + 32;
+// deferred Gumbel candidates per warp: flushed as soon as SX_FLUSH are pending, so a tile (at
+// most SP_TILE candidates) always fits on top of the at most SX_FLUSH - 1 left over
+#ifndef KNX_SX_FLUSH
+#define KNX_SX_FLUSH 32
+#endif
+constexpr int SX_FLUSH = KNX_SX_FLUSH;
+constexpr int SX_CQ = SP_TILE + SX_FLUSH;
+// Philox chains per lane in one pass over the deferred candidates (32 candidates each).  Two
+// beat four on B200 (8-10 us per step at T 0.4-0.6): with a flush every 32 candidates, most
+// of a four-chain pass would run on empty slots.
+#ifndef KNX_SX_CHAINS
+#define KNX_SX_CHAINS 2
+#endif
+constexpr int SX_CHAINS = KNX_SX_CHAINS;
 constexpr size_t SX_SMEM = 128 + static_cast<size_t>(SX_RING) * SX_BYTES +
                            static_cast<size_t>(SX_WARPS) * SX_CQ * 8;
 
@@ -496,20 +507,20 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
       auto flush = [&]() {
         __syncwarp();
         const float thr_now = W - GUMBEL_MAX;
-        for (int i0 = 0; i0 < nbuf; i0 += 128) {
-          // four independent Philox chains per lane (latency hiding), taken in column order
-          uint32_t wv[4];
-          float qv[4];
-          int colv[4];
+        for (int i0 = 0; i0 < nbuf; i0 += 32 * SX_CHAINS) {
+          // SX_CHAINS independent Philox chains per lane (latency hiding), in column order
+          uint32_t wv[SX_CHAINS];
+          float qv[SX_CHAINS];
+          int colv[SX_CHAINS];
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
+          for (int r = 0; r < SX_CHAINS; ++r) {
             const int i = i0 + 32 * r + lane;
             qv[r] = i < nbuf ? __uint_as_float(lds32(wq + 4 * i)) : -INFINITY;
             colv[r] = i < nbuf ? static_cast<int>(lds32(wcol + 4 * i)) : 0;
             wv[r] = qv[r] < thr_now ? 0u : philox_w0(static_cast<uint32_t>(colv[r]), k0, k1);
           }
 #pragma unroll
-          for (int r = 0; r < 4; ++r) {
+          for (int r = 0; r < SX_CHAINS; ++r) {
             if (!(qv[r] < thr_now)) {
               const float u = fminf(fmaxf(uint_to_uniform(wv[r]), 0x1.b7cdfep-34f), 0x1.fffffcp-1f);
               const float y = fmaxf(W, bg) - qv[r];
@@ -666,7 +677,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
                 }
               }
               nbuf += total;
-              if (nbuf >= 32) flush();
+              if (nbuf >= SX_FLUSH) flush();
             }
           }
         }
