@@ -105,16 +105,15 @@ def build_layer(dev):
 def layer_step(W, inp, xn, xp):
     """configs[1] step: fused RMSNorm (also writes the MoE K-interleave copy) -> router -> MoE."""
     import fused_moe_w4_v2
-    import fused_rmsnorm
     import moe_router
-    y_norm = fused_rmsnorm.fused_rmsnorm(inp["hidden"], inp["norm_w"], 1e-6, xperm=xp)
-    ids, w, _ = moe_router.route_topk(y_norm, inp["router_w"], TOPK, bias=inp["bias"],
-                                      want_logits=False)
+    y_norm, ids, w, _ = moe_router.rmsnorm_route_topk(inp["hidden"], inp["norm_w"], 1e-6,
+                                                      inp["router_w"], TOPK, bias=inp["bias"],
+                                                      xperm=xp, want_logits=False)
     return fused_moe_w4_v2.moe_forward(y_norm, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"],
                                        W["dn_s"], W["dn_z"], ids, w, hidden_perm=xp), ids
 
 
-LAUNCHES_PER_LAYER = 7  # rmsnorm, router logits, router top-k, align, gate_up, down, combine
+LAUNCHES_PER_LAYER = 5  # RMSNorm + router (one clustered kernel), align, gate_up, down, combine
 
 
 def time_layer(dev, steps, warmup, dist):
@@ -200,19 +199,18 @@ class EpLayer:
         self.tpe = T * TOPK * world // E  # job-wide pairs per expert (engine choice)
 
     def step(self, i, hidden=None):
-        import fused_rmsnorm
         import moe_router
         inp = self.inp
         x = inp["hidden"] if hidden is None else hidden
-        y_norm = fused_rmsnorm.fused_rmsnorm(x, inp["norm_w"], 1e-6, xperm=self.xp)
-        ids, w, _ = moe_router.route_topk(y_norm, inp["router_w"], TOPK, bias=inp["bias"],
-                                          want_logits=False)
+        _, ids, w, _ = moe_router.rmsnorm_route_topk(x, inp["norm_w"], 1e-6, inp["router_w"], TOPK,
+                                                     bias=inp["bias"], xperm=self.xp,
+                                                     want_logits=False)
         return self.layers[i % NSETS](self.xp, ids, w, out_dtype=torch.float16,
                                       tokens_per_expert=self.tpe), ids
 
 
-EP_LAUNCHES_PER_LAYER = 11  # rmsnorm, router x2, align, gather, layout, task list, gate_up, down,
-                            # gather, combine (plus three NCCL all-to-alls)
+EP_LAUNCHES_PER_LAYER = 9  # RMSNorm + router, align, gather, layout, task list, gate_up, down,
+                           # gather, combine (plus three NCCL all-to-alls)
 
 
 def time_layer_ep(dev, steps, warmup, rank, world):
@@ -269,7 +267,6 @@ def time_stack(dev, steps=48):
     load_w4_checkpoint.py:56-59), so 30 weight sets (12.5 GB) stream per step.  Steps/s over
     `steps` steps with the temperature schedule."""
     import fused_moe_w4_v2
-    import fused_rmsnorm
     import fused_sampler_ops
     import moe_router
     import workloads
@@ -283,9 +280,9 @@ def time_stack(dev, steps=48):
         h = h0
         for b in range(60):
             W, inp = sets[b % 30], blocks[b]
-            yn = fused_rmsnorm.fused_rmsnorm(h, inp["norm_w"], 1e-6, xperm=xp)
-            ids, w, _ = moe_router.route_topk(yn, inp["router_w"], TOPK, bias=inp["bias"],
-                                              want_logits=False)
+            yn, ids, w, _ = moe_router.rmsnorm_route_topk(h, inp["norm_w"], 1e-6, inp["router_w"],
+                                                          TOPK, bias=inp["bias"], xperm=xp,
+                                                          want_logits=False)
             h = h + fused_moe_w4_v2.moe_forward(yn, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"],
                                                 W["dn_s"], W["dn_z"], ids, w, hidden_perm=xp,
                                                 int_zeros=False)
@@ -315,7 +312,6 @@ def time_prefill(dev, steps, rank, world):
     RMSNorm -> router -> MoE; with N > 1 each rank holds 128/N experts and 18432/N tokens
     (expert parallelism).  Job-wide tokens/s and per-GPU HBM GB/s."""
     import fused_moe_w4_v2
-    import fused_rmsnorm
     import moe_router
     import workloads
     Tr = PREFILL_TOKENS // world
@@ -332,9 +328,9 @@ def time_prefill(dev, steps, rank, world):
     tpe = PREFILL_TOKENS * TOPK // E
 
     def step():
-        yn = fused_rmsnorm.fused_rmsnorm(inp["hidden"], inp["norm_w"], 1e-6, xperm=xp)
-        ids, w, _ = moe_router.route_topk(yn, inp["router_w"], TOPK, bias=inp["bias"],
-                                          want_logits=False)
+        yn, ids, w, _ = moe_router.rmsnorm_route_topk(inp["hidden"], inp["norm_w"], 1e-6,
+                                                      inp["router_w"], TOPK, bias=inp["bias"],
+                                                      xperm=xp, want_logits=False)
         if world > 1:
             return layer(xp, ids, w, out_dtype=torch.float16, tokens_per_expert=tpe), ids
         return fused_moe_w4_v2.moe_forward(yn, Wf["gu_q"], Wf["gu_s"], Wf["gu_z"], Wf["dn_q"],

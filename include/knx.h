@@ -92,6 +92,18 @@ KNX_API int knx_router_topk(const void* x, const void* wr, const float* bias, in
                     int topk, float* logits_out, int32_t* ids, float* weights, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* ---- RMSNorm + router in one launch ---------------------------------------------------------
+ * knx_rmsnorm (x and w F16, `flags` as there) followed by knx_router_topk on its output, as one
+ * kernel: y, xperm, logits_out, ids and weights are bit-identical to that pair.  No reference
+ * counterpart of its own: it fuses the two calls above.  x, y, xperm: f16 [T,H];
+ * norm_w: f16 [H]; wr: f16 [E,H]; bias: f32 [E] or NULL; logits_out: f32 [T,E] or NULL;
+ * ids: i32 [T,topk]; weights: f32 [T,topk].  No workspace.  Returns KNX_E_UNSUPPORTED unless
+ * E is 64 or 128 and H % 256 == 0 with H <= 3840 (then use the two calls). */
+KNX_API int knx_rmsnorm_router_topk(const void* x, const void* norm_w, float eps, int flags,
+                                    const void* wr, const float* bias, int64_t T, int64_t H, int E,
+                                    int topk, void* y, void* xperm, float* logits_out,
+                                    int32_t* ids, float* weights, void* stream);
+
 /* ---- permutation (moe_align) ------------------------------------------------------------
  * Replaces moe_align (fused_moe_w4.py:15-51) and moe_align_cuda/_align_finalize
  * (fused_moe_w4_v2.py:32-74): a deterministic counting sort of the flat (token, slot) pairs

@@ -8,6 +8,7 @@
 //   * router (DiffusionGemma, not vendored; specified as softmax -> top-k -> renormalise).
 #include "knx_common.cuh"
 #include "knx_internal.cuh"
+#include "knx_topk.cuh"
 
 namespace knx {
 namespace {
@@ -122,7 +123,6 @@ __global__ void __launch_bounds__(128)
 
 // One warp per token: sum the K-split partials in order, add bias, softmax, top-k by logit
 // (ties -> lower expert id), renormalise the selected probabilities.
-constexpr int TK_MAXE = 256;
 __global__ void __launch_bounds__(256)
     router_topk_kernel(const float* __restrict__ part, const float* __restrict__ bias, int T,
                        int E, int topk, float* __restrict__ logits_out, int32_t* __restrict__ ids,
@@ -131,9 +131,8 @@ __global__ void __launch_bounds__(256)
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
   if (t >= T) return;
-  constexpr int PER = TK_MAXE / 32;
+  constexpr int PER = TK_PER;
   float l[PER];
-  float mx = -INFINITY;
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
@@ -145,53 +144,9 @@ __global__ void __launch_bounds__(256)
       if (logits_out) logits_out[static_cast<int64_t>(t) * E + e] = v;
     }
     l[i] = v;
-    mx = fmaxf(mx, v);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float den = 0.f;
-#pragma unroll
-  for (int i = 0; i < PER; ++i) den += (lane + 32 * i < E) ? expf(l[i] - mx) : 0.f;
-  den = warp_sum(den);
-  // top-k selection: k rounds of a warp-wide (max value, min index) reduction; lane k keeps
-  // selection k (topk <= 16), so nothing goes through local memory
-  float my_p = 0.f;
-  int my_i = 0;
-  float psum = 0.f;
-  for (int k = 0; k < topk; ++k) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int e = lane + 32 * i;
-      if (e < E && (l[i] > bv || (l[i] == bv && e < bi))) {
-        bv = l[i];
-        bi = e;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < PER; ++i)
-      if (lane + 32 * i == bi) l[i] = -INFINITY;  // remove the winner
-    const float p = expf(bv - mx) / den;
-    if (lane == k) {
-      my_p = p;
-      my_i = bi;
-    }
-    psum += p;
-  }
-  if (lane < topk) {
-    ids[static_cast<int64_t>(t) * topk + lane] = my_i;
-    weights[static_cast<int64_t>(t) * topk + lane] = my_p / psum;
-  }
+  topk_select(l, E, topk, lane, ids + static_cast<int64_t>(t) * topk,
+              weights + static_cast<int64_t>(t) * topk);
 }
 
 // ------------------------------------------------------------------------------------------

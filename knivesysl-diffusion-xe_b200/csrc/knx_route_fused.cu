@@ -1,0 +1,233 @@
+// knx_route_fused.cu — RMSNorm + router logits + top-k in one launch, for canvases whose router
+// fits one thread-block cluster per 32 tokens (E = 64 or 128).
+//
+// A cluster of E/64 x 4 CTAs owns 32 tokens: CTA (eb, split) computes the partial logits of
+// experts [64 eb, 64 eb + 64) over the K-split `split` (H/4 columns), exactly as
+// router_logits_kernel does (same 64-column chunks, same m16n8k16 sequence per output), so the
+// partials are the same numbers.  The steps:
+//   1. cp.async brings the split's K-slice of the 32 token rows and of the 64 expert rows
+//      (everything in flight at once);
+//   2. meanwhile each warp normalises whole rows with the RMSNorm row routine of
+//      rmsnorm_kernel (rms::rms_row: same loads, same summation order), writing y and the MoE
+//      K-interleaved copy, and publishes 1/rms in shared memory — the cluster's CTAs share the
+//      32 rows, 4 or 8 each;
+//   3. after a cluster barrier every CTA reads the 32 values of 1/rms over distributed shared
+//      memory and normalises its K-slice in place with the same formula as the row routine;
+//   4. the MMAs produce the [32 x 64] partial tile (16 tokens x 16 experts per warp), kept in
+//      shared memory;
+//   5. after a second cluster barrier each warp takes one token, sums the four K-split partials
+//      of every expert in split order over distributed shared memory (router_topk_kernel's
+//      order), adds the bias and runs the shared softmax / top-k routine (topk_select).
+// So y, the interleaved copy, the logits, ids and weights are bit-identical to knx_rmsnorm +
+// knx_router_topk.  A third cluster barrier keeps every CTA's tile alive until all reads are done.
+#include <cooperative_groups.h>
+
+#include "knx_common.cuh"
+#include "knx_rms_row.cuh"
+#include "knx_topk.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace knx {
+namespace {
+
+constexpr int RF_TOK = 32;                        // tokens per cluster (8 clusters: one wave)
+constexpr int RF_EXP = 64;                        // experts per CTA
+constexpr int RF_KSPLIT = 4;                      // K-splits (= router_logits_kernel's)
+constexpr int RF_BK = 64;                         // k per chunk
+constexpr int RF_ROWB = RF_BK * 2 + 16;           // 144-byte padded rows (conflict-free u32 loads)
+constexpr int RF_CHUNK_BYTES = (RF_TOK + RF_EXP) * RF_ROWB;
+constexpr int RF_THREADS = 256;                   // 8 warps
+constexpr int RF_MAX_CHUNKS = 15;                 // H <= 3840
+constexpr size_t rf_smem_bytes(int nchunk) {
+  return static_cast<size_t>(nchunk) * RF_CHUNK_BYTES + (RF_TOK * RF_EXP + 8 + RF_TOK + 8) * 4 +
+         static_cast<size_t>(nchunk) * RF_BK * 2;  // + the norm weights of the K-slice
+}
+
+__global__ void __launch_bounds__(RF_THREADS)
+    route_fused_kernel(const __half* __restrict__ x, const __half* __restrict__ nw, float eps,
+                       bool round_bf16, const __half* __restrict__ wr, const float* __restrict__ bias, int T, int H,
+                       int E, int topk, __half* __restrict__ y, __half* __restrict__ xperm,
+                       float* __restrict__ logits_out, int32_t* __restrict__ ids,
+                       float* __restrict__ weights) {
+  pdl_wait_trigger();
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) uint8_t rf_smem[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int g = lane >> 2, q = lane & 3;
+  const int neb = E / RF_EXP;          // expert blocks (the cluster's y extent)
+  const int csize = neb * RF_KSPLIT;   // CTAs per cluster
+  const int rank = static_cast<int>(cluster.block_rank());  // = eb + neb * split
+  const int eb = blockIdx.y, split = blockIdx.z;
+  const int t0 = blockIdx.x * RF_TOK;
+  const int kper = H / RF_KSPLIT, nchunk = kper / RF_BK, kbeg = split * kper;
+  const int e0 = eb * RF_EXP;
+  uint8_t* slices = rf_smem;                                        // [nchunk][96 rows][144 B]
+  float* part = reinterpret_cast<float*>(rf_smem + nchunk * RF_CHUNK_BYTES);  // [32][64]
+  float* inv_pub = part + RF_TOK * RF_EXP;                          // [8] 1/rms of own rows
+  float* inv_all = inv_pub + 8;                                     // [32] the cluster's rows
+  uint8_t* nws = reinterpret_cast<uint8_t*>(inv_all + RF_TOK + 8); // [kper] norm weights, f16
+
+  // 1. the K-slices (token rows first, then expert rows), all chunks in one cp.async group
+  for (int c = 0; c < nchunk; ++c) {
+    uint8_t* sl = slices + c * RF_CHUNK_BYTES;
+    const int k0 = kbeg + c * RF_BK;
+    for (int i = tid; i < (RF_TOK + RF_EXP) * 8; i += RF_THREADS) {
+      const int r = i >> 3, ch = i & 7;
+      const __half* src;
+      if (r < RF_TOK) {
+        const int t = t0 + r;
+        src = x + static_cast<int64_t>(t < T ? t : T - 1) * H + k0 + ch * 8;
+      } else {
+        src = wr + static_cast<int64_t>(e0 + r - RF_TOK) * H + k0 + ch * 8;
+      }
+      cp_async16(sl + r * RF_ROWB + ch * 16, src);
+    }
+  }
+  for (int i = tid; i < kper / 8; i += RF_THREADS) cp_async16(nws + 16 * i, nw + kbeg + 8 * i);
+  cp_async_commit();
+
+  // 2. RMSNorm of this CTA's rows of the cluster's 32 (whole rows, one warp per row)
+  const int rpc = RF_TOK / csize;  // 4 or 8
+  for (int r = warp; r < rpc; r += RF_THREADS / 32) {
+    const int t = t0 + rank * rpc + r;
+    float inv = 0.f;
+    if (t < T)
+      inv = rms::rms_row<__half, __half>(x + static_cast<int64_t>(t) * H, nw,
+                                         y + static_cast<int64_t>(t) * H,
+                                         xperm ? xperm + static_cast<int64_t>(t) * H : nullptr,
+                                         H, eps, round_bf16, lane);
+    if (lane == 0) inv_pub[r] = inv;
+  }
+  cluster.sync();  // 1/rms of every row of the cluster published
+
+  // 3. the 32 values of 1/rms, then the K-slice normalised in place (the row routine's formula)
+  if (tid < RF_TOK) {
+    const float* src = cluster.map_shared_rank(inv_pub, tid / rpc);
+    inv_all[tid] = src[tid % rpc];
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  for (int i = tid; i < nchunk * RF_TOK * 8; i += RF_THREADS) {
+    const int c = i / (RF_TOK * 8), rem = i - c * (RF_TOK * 8), r = rem >> 3, ch = rem & 7;
+    const uint32_t a = smem_u32(slices + c * RF_CHUNK_BYTES + r * RF_ROWB + ch * 16);
+    float f[8], wf[8];
+    rms::unpack8<__half>(lds128(a), f);
+    rms::unpack8<__half>(lds128(smem_u32(nws) + 16u * (c * (RF_BK / 8) + ch)), wf);
+    const float inv = inv_all[r];
+    __half out[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      out[j] = rms::from_f32<__half>(__fmul_rn(__fmul_rn(f[j], inv), wf[j]), round_bf16);
+    const uint4 o = *reinterpret_cast<const uint4*>(out);
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(o.x), "r"(o.y), "r"(o.z),
+                 "r"(o.w)
+                 : "memory");
+  }
+  __syncthreads();
+
+  // 4. partial logits of this K-split: warp w takes tokens [16 (w & 1), +16) (one m16 tile) and
+  //    experts [16 (w >> 1), +16) (two n8 tiles)
+  const int tm = 16 * (warp & 1), en = 16 * (warp >> 1);
+  float acc[2][4] = {};
+  for (int c = 0; c < nchunk; ++c) {
+    const uint32_t bx = smem_u32(slices + c * RF_CHUNK_BYTES);
+    const uint32_t bw = bx + RF_TOK * RF_ROWB;
+#pragma unroll
+    for (int ks = 0; ks < RF_BK / 16; ++ks) {
+      const int kb = ks * 32 + q * 4;  // byte offset of k = 16*ks + 2q
+      const uint32_t a0 = lds32(bx + (tm + g) * RF_ROWB + kb);
+      const uint32_t a1 = lds32(bx + (tm + g + 8) * RF_ROWB + kb);
+      const uint32_t a2 = lds32(bx + (tm + g) * RF_ROWB + kb + 16);
+      const uint32_t a3 = lds32(bx + (tm + g + 8) * RF_ROWB + kb + 16);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint32_t b0 = lds32(bw + (en + 8 * nt + g) * RF_ROWB + kb);
+        const uint32_t b1 = lds32(bw + (en + 8 * nt + g) * RF_ROWB + kb + 16);
+        mma_16816(acc[nt], a0, a1, a2, a3, b0, b1);
+      }
+    }
+  }
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int e = en + 8 * nt + 2 * q;
+    part[(tm + g) * RF_EXP + e] = acc[nt][0];
+    part[(tm + g) * RF_EXP + e + 1] = acc[nt][1];
+    part[(tm + g + 8) * RF_EXP + e] = acc[nt][2];
+    part[(tm + g + 8) * RF_EXP + e + 1] = acc[nt][3];
+  }
+  cluster.sync();  // every partial tile of the cluster complete
+
+  // 5. one warp per token: split partials in split order, bias, softmax / top-k
+  for (int j = rank * rpc + warp; j < (rank + 1) * rpc; j += RF_THREADS / 32) {
+    const int t = t0 + j;
+    if (t >= T) continue;  // warp-uniform
+    float l[TK_PER];
+#pragma unroll
+    for (int i = 0; i < TK_PER; ++i) {
+      const int e = lane + 32 * i;
+      float v = -INFINITY;
+      if (e < E) {
+        const int ebk = e / RF_EXP, el = e - ebk * RF_EXP;
+        v = 0.f;
+        for (int s = 0; s < RF_KSPLIT; ++s)
+          v += cluster.map_shared_rank(part, ebk + neb * s)[j * RF_EXP + el];
+        if (bias) v += bias[e];
+        if (logits_out) logits_out[static_cast<int64_t>(t) * E + e] = v;
+      }
+      l[i] = v;
+    }
+    topk_select(l, E, topk, lane, ids + static_cast<int64_t>(t) * topk,
+                weights + static_cast<int64_t>(t) * topk);
+  }
+  cluster.sync();  // no CTA leaves while another still reads its tile
+}
+
+}  // namespace
+}  // namespace knx
+
+extern "C" int knx_rmsnorm_router_topk(const void* x, const void* norm_w, float eps, int flags,
+                                       const void* wr, const float* bias, int64_t T, int64_t H, int E, int topk,
+                                       void* y, void* xperm, float* logits_out, int32_t* ids,
+                                       float* weights, void* stream) {
+  using namespace knx;
+  if (T < 0 || H <= 0 || T > (1 << 24) || topk < 1 || topk > 16 || topk > E) return KNX_E_INVALID;
+  if ((H % 256) != 0 || H / 256 > RF_MAX_CHUNKS || (E != 64 && E != 128)) return KNX_E_UNSUPPORTED;
+  if (!aligned(x, 16) || !aligned(norm_w, 16) || !aligned(wr, 16) || !aligned(y, 16) ||
+      (xperm && !aligned(xperm, 16)))
+    return KNX_E_ALIGN;
+  if (T == 0) return KNX_OK;
+  const int nchunk = static_cast<int>(H / RF_KSPLIT / RF_BK);
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    if (cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(rf_smem_bytes(RF_MAX_CHUNKS))) != cudaSuccess)
+      return KNX_E_DEVICE;
+    attr_set[dev & 63] = true;
+  }
+  const int neb = E / RF_EXP;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>((T + RF_TOK - 1) / RF_TOK), neb, RF_KSPLIT);
+  cfg.blockDim = dim3(RF_THREADS);
+  cfg.dynamicSmemBytes = rf_smem_bytes(nchunk);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = static_cast<unsigned>(neb);
+  attr[0].val.clusterDim.z = RF_KSPLIT;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  if (cudaLaunchKernelEx(&cfg, route_fused_kernel, static_cast<const __half*>(x),
+                         static_cast<const __half*>(norm_w), eps,
+                         (flags & KNX_RMS_ROUND_BF16) != 0, static_cast<const __half*>(wr),
+                         bias, static_cast<int>(T), static_cast<int>(H), E, topk,
+                         static_cast<__half*>(y), static_cast<__half*>(xperm), logits_out, ids,
+                         weights) != cudaSuccess)
+    return KNX_E_LAUNCH;
+  return launch_status();
+}

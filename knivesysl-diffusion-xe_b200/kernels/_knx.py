@@ -49,6 +49,8 @@ _SIGS = {
     "knx_rmsnorm": (_i32, [_vp, _vp, _i32, _vp, _vp, _i64, _i64, _f32, _i32, _i32, _vp]),
     "knx_router_workspace_size": (_sz, [_i64, _i32]),
     "knx_router_topk": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "knx_rmsnorm_router_topk": (_i32, [_vp, _vp, _f32, _i32, _vp, _vp, _i64, _i64, _i32, _i32,
+                                       _vp, _vp, _vp, _vp, _vp, _vp]),
     "knx_moe_align": (_i32, [_vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                              _vp, _vp]),
     "knx_moe_align_large_scratch_size": (_sz, [_i64, _i32]),

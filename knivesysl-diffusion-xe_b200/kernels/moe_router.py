@@ -7,7 +7,8 @@ route_topk(x, router_weight, top_k, bias=None) -> (ids i32[T,k], weights f32[T,k
 """
 import torch
 
-from _knx import check, load, ptr, require_device, stream_of, workspace
+from _knx import (KNX_RMS_ROUND_BF16, check, load, ptr, require_device, stream_of,
+                  workspace)
 
 
 def route_topk(x, router_weight, top_k, bias=None, want_logits=True):
@@ -25,3 +26,37 @@ def route_topk(x, router_weight, top_k, bias=None, want_logits=True):
     check(lib.knx_router_topk(ptr(xh), ptr(wr), ptr(b), T, H, E, int(top_k), ptr(logits), ptr(ids),
                               ptr(w), ptr(ws), ws.numel(), stream_of(dev)), "knx_router_topk")
     return ids, w, logits
+
+
+KNX_E_UNSUPPORTED = -5
+
+
+def rmsnorm_route_topk(x, norm_weight, eps, router_weight, top_k, bias=None, xperm=None,
+                       round_bf16=True, want_logits=True):
+    """fused_rmsnorm(x, norm_weight, eps, round_bf16, xperm) then route_topk on its output, as one
+    launch where the shapes allow (f16 x and weights, E in {64, 128}, H % 256 == 0, H <= 3840);
+    otherwise as the two calls.  Same bits either way.  -> (y, ids, weights, logits)."""
+    import fused_rmsnorm
+    dev = require_device(x)
+    T, H = x.shape
+    E = router_weight.shape[0]
+    if (x.dtype == torch.float16 and norm_weight is not None and norm_weight.dtype == torch.float16
+            and router_weight.dtype == torch.float16):
+        xc = x.contiguous()
+        nw = norm_weight.contiguous()
+        wr = router_weight.contiguous()
+        b = bias.contiguous().float() if bias is not None else None
+        y = torch.empty_like(xc)
+        ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+        logits = torch.empty(T, E, dtype=torch.float32, device=x.device) if want_logits else None
+        st = load().knx_rmsnorm_router_topk(ptr(xc), ptr(nw), float(eps),
+                                            KNX_RMS_ROUND_BF16 if round_bf16 else 0, ptr(wr), ptr(b),
+                                            T, H, E, int(top_k), ptr(y), ptr(xperm), ptr(logits),
+                                            ptr(ids), ptr(w), stream_of(dev))
+        if st != KNX_E_UNSUPPORTED:
+            check(st, "knx_rmsnorm_router_topk")
+            return y, ids, w, logits
+    y = fused_rmsnorm.fused_rmsnorm(x, norm_weight, eps, round_bf16=round_bf16, xperm=xperm)
+    ids, w, logits = route_topk(y, router_weight, top_k, bias=bias, want_logits=want_logits)
+    return y, ids, w, logits

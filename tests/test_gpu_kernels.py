@@ -255,6 +255,54 @@ def test_router_topk_exact_given_logits(cuda):
     assert counts.max().item() > 40    # the Zipf bias skews routing
 
 
+@pytest.mark.parametrize("T,H,E,rb,with_bias", [(256, 2816, 128, True, True),
+                                                 (100, 2816, 128, False, True),
+                                                 (7, 1024, 64, True, False),
+                                                 (513, 2816, 128, True, True),
+                                                 (33, 3840, 64, False, True)])
+def test_fused_rmsnorm_router_bit_identical_to_two_calls(cuda, T, H, E, rb, with_bias):
+    """knx_rmsnorm_router_topk (one clustered launch) against knx_rmsnorm + knx_router_topk:
+    y, the K-interleaved copy, logits, ids and weights all bit for bit."""
+    import ctypes
+    import _knx
+    import fused_rmsnorm
+    import moe_router
+    import workloads
+    inp = workloads.moe_inputs(T, H, E, seed=T + H, device=cuda)
+    bias = inp["bias"] if with_bias else None
+    xp1 = torch.empty(T, H, dtype=torch.float16, device=cuda)
+    y1 = fused_rmsnorm.fused_rmsnorm(inp["hidden"], inp["norm_w"], 1e-6, round_bf16=rb, xperm=xp1)
+    ids1, w1, lg1 = moe_router.route_topk(y1, inp["router_w"], 8, bias=bias)
+    # the one-launch path itself (not the two-call fallback of rmsnorm_route_topk)
+    lib = _knx.load()
+    y2 = torch.empty(T, H, dtype=torch.float16, device=cuda)
+    xp2 = torch.empty_like(xp1)
+    ids2 = torch.empty(T, 8, dtype=torch.int32, device=cuda)
+    w2 = torch.empty(T, 8, dtype=torch.float32, device=cuda)
+    lg2 = torch.empty(T, E, dtype=torch.float32, device=cuda)
+    vp = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    st = lib.knx_rmsnorm_router_topk(vp(inp["hidden"]), vp(inp["norm_w"]), 1e-6,
+                                     _knx.KNX_RMS_ROUND_BF16 if rb else 0, vp(inp["router_w"]),
+                                     vp(bias), T, H, E, 8, vp(y2), vp(xp2), vp(lg2), vp(ids2),
+                                     vp(w2), _knx.stream_of(cuda.index or 0))
+    assert st == 0, st
+    torch.cuda.synchronize()
+    assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
+    assert torch.equal(xp1.view(torch.int16), xp2.view(torch.int16))
+    assert torch.equal(lg1.view(torch.int32), lg2.view(torch.int32))
+    assert torch.equal(ids1, ids2)
+    assert torch.equal(w1.view(torch.int32), w2.view(torch.int32))
+
+
+def test_fused_rmsnorm_router_unsupported_shape_falls_back(cuda):
+    import moe_router
+    import workloads
+    inp = workloads.moe_inputs(64, 1024, 256, seed=5, device=cuda)  # E = 256: two-call path
+    y, ids, w, lg = moe_router.rmsnorm_route_topk(inp["hidden"], inp["norm_w"], 1e-6,
+                                                  inp["router_w"], 8, bias=inp["bias"])
+    assert ids.shape == (64, 8) and torch.isfinite(w).all()
+
+
 # ------------------------------------------------------------------------------ sampler
 @pytest.mark.parametrize("tag", ["s0", "s1", "s2"])
 def test_sampler_vs_reference_golden(cuda, tag):
