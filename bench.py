@@ -181,7 +181,8 @@ def time_layer_e2e(dev, steps, warmup):
 
 class EpLayer:
     """N > 1: the same configs[1] layer with the 128 experts sharded over the ranks (expert
-    parallelism, NCCL all-to-all dispatch/return); each rank runs its own 256-token canvas."""
+    parallelism; dispatch and return by device-initiated stores over NVLink); each rank runs its
+    own 256-token canvas."""
 
     def __init__(self, dev, rank, world):
         import ep_moe
@@ -192,7 +193,9 @@ class EpLayer:
             local = ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"], Wf["gu_z"], Wf["dn_q"],
                                          Wf["dn_s"], Wf["dn_z"], rank, world)
             del Wf
-            self.layers.append(ep_moe.ExpertParallelMoE(*local, E_total=E, int_zeros=False))
+            # the exchange runs on the device over NVLink (no host sync per layer)
+            self.layers.append(ep_moe.P2PExpertParallelMoE(*local, E_total=E, int_zeros=False,
+                                                           max_tokens=T, topk=TOPK))
         torch.cuda.empty_cache()
         self.inp = workloads.moe_inputs(T, H, E, seed=rank, device=dev)  # this rank's canvas
         self.xp = torch.empty(T, H, dtype=torch.float16, device=dev)
@@ -320,10 +323,11 @@ def time_prefill(dev, steps, rank, world):
     xp = torch.empty(Tr, H, dtype=torch.float16, device=dev)
     if world > 1:
         import ep_moe
-        layer = ep_moe.ExpertParallelMoE(*ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"], Wf["gu_z"],
-                                                                 Wf["dn_q"], Wf["dn_s"], Wf["dn_z"],
-                                                                 rank, world),
-                                         E_total=E, int_zeros=False)
+        layer = ep_moe.P2PExpertParallelMoE(*ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"],
+                                                                    Wf["gu_z"], Wf["dn_q"],
+                                                                    Wf["dn_s"], Wf["dn_z"], rank,
+                                                                    world),
+                                            E_total=E, int_zeros=False, max_tokens=Tr, topk=TOPK)
         del Wf
     tpe = PREFILL_TOKENS * TOPK // E
 

@@ -192,6 +192,38 @@ KNX_API int knx_moe_w4_grouped(const void* xrows, const int32_t* rows, int64_t R
 KNX_API int knx_moe_combine(const void* out3, const int32_t* inv, const void* topk_w, int w_dtype,
                             int64_t T, int topk, int64_t H, int out_dtype, void* out, void* stream);
 
+/* ---- expert parallelism over NVLink, device-initiated -----------------------------------
+ * The exchange of the expert-parallel layer by direct stores into peer memory (no host sync,
+ * no collective library in the data path).  No reference counterpart: the reference has no
+ * expert parallelism; these replace the two all-to-alls of the layer above.  Every rank holds a
+ * region of the same layout mapped into all peers (e.g. torch symmetric memory): flags (world
+ * uint32), cnt [world][E] int32, receive rows [r_cap][H] f16, return rows [n_cap][H] f16.
+ * peer_* are device arrays of `world` pointers to those regions on each rank (index = rank).
+ * E = El * world, world <= 8, E <= 256.  epoch: one more than the previous barrier's, the same
+ * on every rank (each call below that takes one is a barrier).  err: KNX_DEV_TIMEOUT when a
+ * barrier waited 2 s.
+ *   knx_ep_p2p_counts    counts[E] of this rank's pairs (knx_moe_align) to every peer; barrier;
+ *                        writes the plan (knx_ep_p2p_plan_ints ints).  plan[E .. E + El] are
+ *                        the offsets of this rank's local experts in its receive rows.
+ *   knx_ep_p2p_dispatch  pair rows of xp [T][H] in align order (sorted_pair, offsets) into the
+ *                        owners' receive rows, at the slots the grouped GEMMs read (n_cap >=
+ *                        T*topk: slots beyond offsets[E] are skipped).
+ *   knx_ep_p2p_barrier   a barrier.
+ *   knx_ep_p2p_return    result rows out3 [r_cap][H] (local, expert-major) into the sources'
+ *                        return rows at their align slots (for knx_moe_combine there). */
+KNX_API size_t knx_ep_p2p_plan_ints(int E, int El, int world);
+KNX_API int knx_ep_p2p_counts(const int32_t* counts, int E, int El, int rank, int world,
+                              int32_t* const* peer_cnt, uint32_t* const* peer_flags,
+                              uint32_t epoch, int32_t* plan, int32_t* err, void* stream);
+KNX_API int knx_ep_p2p_dispatch(const void* xp, int64_t H, int topk, const int32_t* sorted_pair,
+                                const int32_t* offsets, int E, int El, const int32_t* plan,
+                                void* const* peer_rows, int64_t n_cap, void* stream);
+KNX_API int knx_ep_p2p_barrier(uint32_t* const* peer_flags, int rank, int world, uint32_t epoch,
+                               int32_t* err, void* stream);
+KNX_API int knx_ep_p2p_return(const void* out3, int64_t H, int El, int world, int E,
+                              const int32_t* plan, void* const* peer_ret, int64_t r_cap,
+                              void* stream);
+
 /* ---- dense W4A16 linear -------------------------------------------------------------------
  * Replaces w4a16_linear (w4a16.py:96-108):  Y[M,N] = X[M,K] . dequant(q,s,z)^T, f16 out.
  * X: f16 [M,K] row-major; q u8 [N,K/2]; s,z f16 [N,K/gs].  K % 64 == 0, gs % 32 == 0, gs | K,

@@ -49,6 +49,11 @@ _SIGS = {
     "knx_rmsnorm": (_i32, [_vp, _vp, _i32, _vp, _vp, _i64, _i64, _f32, _i32, _i32, _vp]),
     "knx_router_workspace_size": (_sz, [_i64, _i32]),
     "knx_router_topk": (_i32, [_vp, _vp, _vp, _i64, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "knx_ep_p2p_plan_ints": (_sz, [_i32, _i32, _i32]),
+    "knx_ep_p2p_counts": (_i32, [_vp, _i32, _i32, _i32, _i32, _vp, _vp, _c.c_uint32, _vp, _vp, _vp]),
+    "knx_ep_p2p_dispatch": (_i32, [_vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _i64, _vp]),
+    "knx_ep_p2p_barrier": (_i32, [_vp, _i32, _i32, _c.c_uint32, _vp, _vp]),
+    "knx_ep_p2p_return": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
     "knx_rmsnorm_router_topk": (_i32, [_vp, _vp, _f32, _i32, _vp, _vp, _i64, _i64, _i32, _i32,
                                        _vp, _vp, _vp, _vp, _vp, _vp]),
     "knx_moe_align": (_i32, [_vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,

@@ -68,6 +68,23 @@ class CudaOps:
                                      stream_of(dev)), "knx_moe_w4_grouped")
         return out3
 
+    def grouped_rows(self, xrows, offsets, weights, tokens_per_expert, flags):
+        """grouped() for rows already in slot order (row = slot); xrows: [R_cap, H]."""
+        dev = require_device(xrows)
+        gu_q, gu_s, gu_z, dn_q, dn_s, dn_z = weights
+        R, H = xrows.shape
+        El, twoI, _ = gu_q.shape
+        I = twoI // 2
+        out3 = torch.empty(R, H, dtype=torch.float16, device=xrows.device)
+        lib = load()
+        ws = workspace(dev, lib.knx_moe_w4_grouped_workspace_size(R, H, I, El), "ep_grouped")
+        check(lib.knx_moe_w4_grouped(ptr(xrows), None, R, ptr(offsets), ptr(gu_q), ptr(gu_s),
+                                     ptr(gu_z), ptr(dn_q), ptr(dn_s), ptr(dn_z), H, I, El,
+                                     H // gu_s.shape[-1], I // dn_s.shape[-1], flags,
+                                     int(tokens_per_expert), ptr(ws), ws.numel(), ptr(out3), None,
+                                     stream_of(dev)), "knx_moe_w4_grouped")
+        return out3
+
     def combine(self, out3, inv, w, T, out_dtype):
         dev = require_device(out3)
         H = out3.shape[1]
@@ -153,3 +170,107 @@ def shard_experts(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, rank, world):
     El = E // world
     sl = slice(rank * El, (rank + 1) * El)
     return tuple(t[sl].contiguous() for t in (gu_q, gu_s, gu_z, dn_q, dn_s, dn_z))
+
+
+class _P2PExchange:
+    """One symmetric region per rank (torch symmetric memory, mapped into every peer) for the
+    device-initiated exchange: flags | counts [world][E] | receive rows [r_cap][H] | return rows
+    [n_cap][H].  Shared by every layer with the same group and sizes (layers run one after the
+    other on the stream, and the barriers order each layer's use of the region after the last)."""
+
+    _cache = {}
+
+    @classmethod
+    def get(cls, group, E, n_cap, H, device):
+        key = (id(group), E, n_cap, H, str(device))
+        ex = cls._cache.get(key)
+        if ex is None:
+            ex = cls._cache[key] = cls(group, E, n_cap, H, device)
+        return ex
+
+    def __init__(self, group, E, n_cap, H, device):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.E, self.El, self.n_cap, self.H = E, E // self.world, n_cap, H
+        self.r_cap = n_cap * self.world  # every pair of every rank could go to one owner
+        al = lambda b: (b + 255) & ~255
+        self.off_flags = 0
+        self.off_cnt = al(64 * 4)
+        self.off_rows = al(self.off_cnt + self.world * E * 4)
+        self.off_ret = al(self.off_rows + self.r_cap * H * 2)
+        total = al(self.off_ret + n_cap * H * 2)
+        self.buf = symm_mem.empty(total, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        grp = group if group is not None else dist.group.WORLD
+        if hasattr(symm_mem, "enable_symm_mem_for_group") and not symm_mem.is_symm_mem_enabled_for_group(grp.group_name):
+            symm_mem.enable_symm_mem_for_group(grp.group_name)
+        self.hdl = symm_mem.rendezvous(self.buf, grp)
+        bases = [int(b) for b in self.hdl.buffer_ptrs]
+        i64 = dict(dtype=torch.int64, device=device)
+        self.peer_flags = torch.tensor([b + self.off_flags for b in bases], **i64)
+        self.peer_cnt = torch.tensor([b + self.off_cnt for b in bases], **i64)
+        self.peer_rows = torch.tensor([b + self.off_rows for b in bases], **i64)
+        self.peer_ret = torch.tensor([b + self.off_ret for b in bases], **i64)
+        self.rows = self.buf[self.off_rows:self.off_rows + self.r_cap * H * 2].view(torch.float16).view(self.r_cap, H)
+        self.ret = self.buf[self.off_ret:self.off_ret + n_cap * H * 2].view(torch.float16).view(n_cap, H)
+        self.plan = torch.empty(load().knx_ep_p2p_plan_ints(E, self.El, self.world), dtype=torch.int32,
+                                device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        self.epoch = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's flags are zero before anyone signals
+
+    def next_epoch(self):
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        return self.epoch
+
+
+class P2PExpertParallelMoE(ExpertParallelMoE):
+    """ExpertParallelMoE with the exchange done by the device over NVLink: the pairs' rows are
+    stored straight into the owning ranks' memory and the results straight back (three
+    device-side barriers per layer), so no step of the layer waits for the host.  Needs every
+    rank on one node with peer access, and the same token count T <= max_tokens on every rank.
+    The output is bit-identical to ExpertParallelMoE and to the single-GPU layer."""
+
+    def __init__(self, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=None, engine=None,
+                 int_zeros=None, max_tokens=256, topk=8):
+        super().__init__(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=group, ops=CudaOps(),
+                         engine=engine, int_zeros=int_zeros)
+        H = gu_q.shape[2] * 2
+        self.ex = _P2PExchange.get(group, E_total, max_tokens * topk, H, gu_q.device)
+
+    @torch.no_grad()
+    def forward(self, x, topk_ids, topk_w, out_dtype=torch.float16, tokens_per_expert=None):
+        """x: this rank's activation rows [T, H] (f16, MoE K-interleave); topk_ids/topk_w:
+        [T, k].  tokens_per_expert: the job-wide pairs per expert (engine choice); default
+        T * k * world / E (every rank holds T tokens)."""
+        ex, lib = self.ex, load()
+        T, H = x.shape
+        tk = topk_ids.shape[1]
+        if T * tk > ex.n_cap:
+            raise ValueError(f"{T} tokens x top-{tk} exceed the exchange capacity {ex.n_cap}")
+        if tokens_per_expert is None:
+            tokens_per_expert = T * tk * self.N // self.E
+        dev = require_device(x)
+        st = stream_of(dev)
+        counts, offsets, sorted_pair, inv = self.ops.align(topk_ids, self.E)
+        counts = counts.to(torch.int32)
+        E, El, world, rank = self.E, self.El, self.N, self.rank
+        check(lib.knx_ep_p2p_counts(ptr(counts), E, El, rank, world, ptr(ex.peer_cnt),
+                                    ptr(ex.peer_flags), ex.next_epoch(), ptr(ex.plan), ptr(ex.err),
+                                    st), "knx_ep_p2p_counts")
+        check(lib.knx_ep_p2p_dispatch(ptr(x.contiguous()), H, tk, ptr(sorted_pair), ptr(offsets), E,
+                                      El, ptr(ex.plan), ptr(ex.peer_rows), T * tk, st),
+              "knx_ep_p2p_dispatch")
+        check(lib.knx_ep_p2p_barrier(ptr(ex.peer_flags), rank, world, ex.next_epoch(),
+                                     ptr(ex.err), st), "knx_ep_p2p_barrier")
+        recv_off = ex.plan[E:E + El + 1]
+        out3 = self.ops.grouped_rows(ex.rows, recv_off, self.weights, tokens_per_expert, self.flags)
+        check(lib.knx_ep_p2p_return(ptr(out3), H, El, world, E, ptr(ex.plan), ptr(ex.peer_ret),
+                                    ex.r_cap, st), "knx_ep_p2p_return")
+        check(lib.knx_ep_p2p_barrier(ptr(ex.peer_flags), rank, world, ex.next_epoch(),
+                                     ptr(ex.err), st), "knx_ep_p2p_barrier")
+        return self.ops.combine(ex.ret[:T * tk], inv, topk_w.contiguous(), T, out_dtype)
+
+    __call__ = forward

@@ -105,3 +105,59 @@ def test_ep_two_gpus_bitwise_equal_single_gpu(cuda):
         mp.spawn(_worker, args=(world, _free_port(), d), nprocs=world, join=True)
         got = torch.cat([torch.load(os.path.join(d, f"y{r}.pt")) for r in range(world)])
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+def _worker_p2p(rank, world, port, out_dir):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    import datetime
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        import ep_moe
+        W, hidden, xp, ids, w = _case(128, 2816, 704, 256 * world, 8, 41, dev)
+        local = ep_moe.shard_experts(W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"],
+                                     W["dn_z"], rank, world)
+        sl = slice(rank * 256, (rank + 1) * 256)
+        layer = ep_moe.P2PExpertParallelMoE(*local, E_total=128)
+        # three layers in a row through the same exchange region (epochs, reuse of the rows)
+        ys = [layer(xp[sl].contiguous(), ids[sl].contiguous(), w[sl].contiguous(),
+                    out_dtype=torch.float16).clone() for _ in range(3)]
+        torch.cuda.synchronize()
+        err = int(layer.ex.err.item())
+        same = all(torch.equal(ys[0].view(torch.int16), y.view(torch.int16)) for y in ys[1:])
+        torch.save({"y": ys[0].cpu(), "err": err, "same": same}, os.path.join(out_dir, f"p{rank}.pt"))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_p2p(world):
+    import torch.multiprocessing as mp
+    import fused_moe_w4_v2
+    W, hidden, xp, ids, w = _case(128, 2816, 704, 256 * world, 8, 41, torch.device("cuda", 0))
+    want = fused_moe_w4_v2.moe_forward(hidden, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"],
+                                       W["dn_s"], W["dn_z"], ids, w, hidden_perm=xp,
+                                       engine="auto").cpu()
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_worker_p2p, args=(world, _free_port(), d), nprocs=world, join=True)
+        res = [torch.load(os.path.join(d, f"p{r}.pt")) for r in range(world)]
+    for r in res:
+        assert r["err"] == 0 and r["same"]
+    got = torch.cat([r["y"] for r in res])
+    assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+def test_ep_p2p_one_rank_bitwise_equal_single_gpu(cuda):
+    """The NVLink exchange at one rank (stores into its own region) equals the single-GPU layer."""
+    _run_p2p(1)
+
+
+def test_ep_p2p_two_gpus_bitwise_equal_single_gpu(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    _run_p2p(2)
