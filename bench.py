@@ -191,7 +191,7 @@ class EpLayer:
         for i in range(NSETS):
             Wf = workloads.moe_weights(E, H, I, seed=100 + i, device=dev)
             local = ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"], Wf["gu_z"], Wf["dn_q"],
-                                         Wf["dn_s"], Wf["dn_z"], rank, world)
+                                         Wf["dn_s"], Wf["dn_z"], rank, world, interleaved=True)
             del Wf
             # the exchange runs on the device over NVLink (no host sync per layer)
             self.layers.append(ep_moe.P2PExpertParallelMoE(*local, E_total=E, int_zeros=False,
@@ -326,7 +326,7 @@ def time_prefill(dev, steps, rank, world):
         layer = ep_moe.P2PExpertParallelMoE(*ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"],
                                                                     Wf["gu_z"], Wf["dn_q"],
                                                                     Wf["dn_s"], Wf["dn_z"], rank,
-                                                                    world),
+                                                                    world, interleaved=True),
                                             E_total=E, int_zeros=False, max_tokens=Tr, topk=TOPK)
         del Wf
     tpe = PREFILL_TOKENS * TOPK // E

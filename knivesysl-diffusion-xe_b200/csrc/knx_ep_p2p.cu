@@ -1,7 +1,9 @@
 // knx_ep_p2p.cu — expert-parallel dispatch and return by direct stores into the peers' memory
 // over NVLink, with no host synchronisation and no collective library in the data path.
 //
-// Each rank owns one symmetric region (the same layout on every rank, mapped into every
+// Experts are sharded round-robin: rank r owns the global experts e = el * world + r, local
+// index el (a skewed router, e.g. one biased towards low expert ids, then loads every rank
+// alike).  Each rank owns one symmetric region (the same layout on every rank, mapped into every
 // peer's address space): barrier flags, the [world][E] matrix of per-expert pair counts, the
 // receive rows and the return rows.  One layer:
 //   knx_ep_p2p_counts    this rank's counts into every peer's matrix row `rank`; barrier; then
@@ -85,7 +87,7 @@ __global__ void __launch_bounds__(256)
                       int32_t* const* __restrict__ peer_cnt, uint32_t* const* __restrict__ peer_flags,
                       uint32_t epoch, int32_t* __restrict__ plan, int32_t* __restrict__ err) {
   pdl_wait_trigger();
-  __shared__ int tot[P2P_MAX_E];
+  __shared__ int tot_own[P2P_MAX_E];  // pairs per expert from all ranks, owner-major [r][el]
   __shared__ int own_off[P2P_MAX_E + P2P_MAX_WORLD];   // per owner: scan of tot over its experts
   __shared__ int srcpre[P2P_MAX_WORLD][P2P_MAX_E + 1];  // per source: scan of its counts
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -98,13 +100,13 @@ __global__ void __launch_bounds__(256)
   for (int e = tid; e < E; e += blockDim.x) {
     int a = 0;
     for (int s = 0; s < world; ++s) a += cnt[s * E + e];
-    tot[e] = a;
+    tot_own[(e % world) * El + e / world] = a;
   }
   __syncthreads();
   if (warp < world) {
     warp_excl_scan(cnt + warp * E, E, srcpre[warp], lane);
     // owner `warp`: offsets of its local experts in its receive rows
-    warp_excl_scan(tot + warp * El, El, own_off + warp * (El + 1), lane);
+    warp_excl_scan(tot_own + warp * El, El, own_off + warp * (El + 1), lane);
   }
   __syncthreads();
   int32_t* dest_base = plan;
@@ -112,14 +114,14 @@ __global__ void __launch_bounds__(256)
   int32_t* seg_start = recv_off + El + 1;
   int32_t* src_base = seg_start + El * world + 1;
   for (int e = tid; e < E; e += blockDim.x) {
-    const int r = e / El, el = e - r * El;
+    const int r = e % world, el = e / world;
     int a = own_off[r * (El + 1) + el];
     for (int s = 0; s < rank; ++s) a += cnt[s * E + e];
     dest_base[e] = a;  // first slot of this rank's pairs of expert e in owner r's rows
   }
   for (int el = tid; el <= El; el += blockDim.x) recv_off[el] = own_off[rank * (El + 1) + el];
   for (int i = tid; i < El * world; i += blockDim.x) {
-    const int el = i / world, s = i - el * world, e = rank * El + el;
+    const int el = i / world, s = i - el * world, e = el * world + rank;
     int a = own_off[rank * (El + 1) + el];
     for (int s2 = 0; s2 < s; ++s2) a += cnt[s2 * E + e];
     seg_start[i] = a;            // first local row from source s for local expert el
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(256)
     const int mid = (lo + hi + 1) >> 1;
     if (offsets[mid] <= j) lo = mid; else hi = mid - 1;
   }
-  const int e = lo, r = e / El;
+  const int e = lo, r = e % (E / El);  // owner: round-robin sharding
   const int64_t dst = plan[e] + (j - offsets[e]);
   const uint4* s = xp + static_cast<int64_t>(sorted_pair[j] / topk) * vpr;
   uint4* d = peer_rows[r] + dst * vpr;

@@ -164,11 +164,13 @@ class ExpertParallelMoE:
     __call__ = forward
 
 
-def shard_experts(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, rank, world):
-    """This rank's contiguous expert slice of full pack_experts buffers."""
+def shard_experts(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, rank, world, interleaved=False):
+    """This rank's experts of full pack_experts buffers: the contiguous slice
+    [rank * E / world, (rank + 1) * E / world) (ExpertParallelMoE), or with interleaved=True the
+    experts rank, rank + world, ... (P2PExpertParallelMoE)."""
     E = gu_q.shape[0]
     El = E // world
-    sl = slice(rank * El, (rank + 1) * El)
+    sl = slice(rank, E, world) if interleaved else slice(rank * El, (rank + 1) * El)
     return tuple(t[sl].contiguous() for t in (gu_q, gu_s, gu_z, dn_q, dn_s, dn_z))
 
 
@@ -229,7 +231,8 @@ class _P2PExchange:
 class P2PExpertParallelMoE(ExpertParallelMoE):
     """ExpertParallelMoE with the exchange done by the device over NVLink: the pairs' rows are
     stored straight into the owning ranks' memory and the results straight back (three
-    device-side barriers per layer), so no step of the layer waits for the host.  Needs every
+    device-side barriers per layer), so no step of the layer waits for the host.  The local
+    experts are rank, rank + world, ... (shard_experts(..., interleaved=True)).  Needs every
     rank on one node with peer access, and the same token count T <= max_tokens on every rank.
     The output is bit-identical to ExpertParallelMoE and to the single-GPU layer."""
 

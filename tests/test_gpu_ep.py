@@ -121,7 +121,7 @@ def _worker_p2p(rank, world, port, out_dir):
         import ep_moe
         W, hidden, xp, ids, w = _case(128, 2816, 704, 256 * world, 8, 41, dev)
         local = ep_moe.shard_experts(W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"],
-                                     W["dn_z"], rank, world)
+                                     W["dn_z"], rank, world, interleaved=True)
         sl = slice(rank * 256, (rank + 1) * 256)
         layer = ep_moe.P2PExpertParallelMoE(*local, E_total=128)
         # three layers in a row through the same exchange region (epochs, reuse of the rows)
