@@ -212,8 +212,8 @@ class EpLayer:
                                       tokens_per_expert=self.tpe), ids
 
 
-EP_LAUNCHES_PER_LAYER = 9  # RMSNorm + router, align, gather, layout, task list, gate_up, down,
-                           # gather, combine (plus three NCCL all-to-alls)
+EP_LAUNCHES_PER_LAYER = 11  # RMSNorm + router, align, counts exchange + plan, dispatch, barrier,
+                            # task list, gate_up, down, return, barrier, combine (NVLink exchange)
 
 
 def time_layer_ep(dev, steps, warmup, rank, world):
