@@ -153,30 +153,74 @@ def time_layer(dev, steps, warmup, dist):
     return ms, {k: v / max(ncalls, 1) for k, v in stages.items()}, counts, clocks
 
 
+def pipelined_e2e(dev, step_fn, host_src, steps, warmup, sync=None):
+    """End to end as a serving loop runs it: every step copies its input host->device from
+    pinned memory, runs step_fn(i, dev_input) -> output, and copies the output device->host.
+    The copies run on a second stream with two buffers each way, so step i+1's upload and step
+    i's download overlap the neighbouring steps' compute.  The timed region covers every copy of
+    every step.  -> (ms, h2d bytes per step, d2h bytes per step)."""
+    comp = torch.cuda.current_stream(dev)
+    copy = torch.cuda.Stream(dev)
+    host_in = [host_src.clone().pin_memory() for _ in range(2)]
+    dev_in = [torch.empty(host_src.shape, dtype=host_src.dtype, device=dev) for _ in range(2)]
+    host_out = [None, None]
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    in_free = [torch.cuda.Event() for _ in range(2)]
+    out_ready = [torch.cuda.Event() for _ in range(2)]
+    out_bytes = [0]
+
+    def upload(i):
+        b = i % 2
+        with torch.cuda.stream(copy):
+            copy.wait_event(in_free[b])  # the step that read this buffer two steps ago is done
+            dev_in[b].copy_(host_in[b], non_blocking=True)
+            in_ready[b].record(copy)
+
+    def run(i):
+        b = i % 2
+        comp.wait_event(in_ready[b])
+        y = step_fn(i, dev_in[b])
+        in_free[b].record(comp)
+        out_ready[b].record(comp)
+        if host_out[b] is None:
+            host_out[b] = torch.empty(y.shape, dtype=y.dtype).pin_memory()
+        out_bytes[0] = y.numel() * y.element_size()
+        with torch.cuda.stream(copy):
+            copy.wait_event(out_ready[b])
+            y.record_stream(copy)
+            host_out[b].copy_(y, non_blocking=True)
+
+    def loop(i0, n):
+        upload(i0)
+        for i in range(i0, i0 + n):
+            if i + 1 < i0 + n:
+                upload(i + 1)
+            run(i)
+        comp.wait_stream(copy)
+
+    loop(0, warmup)
+    torch.cuda.synchronize(dev)
+    if sync is not None:
+        sync()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(comp)
+    loop(warmup, steps)
+    ev1.record(comp)
+    torch.cuda.synchronize(dev)
+    return ev0.elapsed_time(ev1), host_src.numel() * host_src.element_size(), out_bytes[0]
+
+
 def time_layer_e2e(dev, steps, warmup):
     """Through the public API with host buffers: H2D of the canvas hidden states from pinned
-    memory, the layer, D2H of the layer output, every step."""
+    memory, the layer, D2H of the layer output, every step (copies overlapped on a second
+    stream, see pipelined_e2e)."""
     sets, inp = build_layer(dev)
-    host_in = inp["hidden"].cpu().pin_memory()
-    host_out = torch.empty(T, H, dtype=torch.float16).pin_memory()
     xp = torch.empty(T, H, dtype=torch.float16, device=dev)
-    dev_in = torch.empty_like(inp["hidden"])
 
-    def step(i):
-        dev_in.copy_(host_in, non_blocking=True)
-        inp2 = dict(inp, hidden=dev_in)
-        y, _ = layer_step(sets[i % NSETS], inp2, None, xp)
-        host_out.copy_(y, non_blocking=True)
-    for i in range(warmup):
-        step(i)
-    torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for i in range(steps):
-        step(i)
-    ev1.record()
-    torch.cuda.synchronize(dev)
-    return ev0.elapsed_time(ev1), host_in.numel() * 2, host_out.numel() * 2
+    def step(i, x):
+        y, _ = layer_step(sets[i % NSETS], dict(inp, hidden=x), None, xp)
+        return y
+    return pipelined_e2e(dev, step, inp["hidden"].cpu(), steps, warmup)
 
 
 class EpLayer:
@@ -241,26 +285,15 @@ def time_layer_ep(dev, steps, warmup, rank, world):
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item())
     # end to end: the canvas from pinned host memory, the layer output back, every step
-    host_in = ep.inp["hidden"].cpu().pin_memory()
-    host_out = torch.empty(T, H, dtype=torch.float16).pin_memory()
-    dev_in = torch.empty_like(ep.inp["hidden"])
-    for i in range(warmup):
-        dev_in.copy_(host_in, non_blocking=True)
-        y, _ = ep.step(i, dev_in)
-        host_out.copy_(y, non_blocking=True)
-    torch.cuda.synchronize(dev)
-    torch.distributed.barrier()
-    ev0.record()
-    for i in range(steps):
-        dev_in.copy_(host_in, non_blocking=True)
-        y, _ = ep.step(i, dev_in)
-        host_out.copy_(y, non_blocking=True)
-    ev1.record()
-    torch.cuda.synchronize(dev)
-    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    def step(i, x):
+        y, _ = ep.step(i, x)
+        return y
+    e2e_ms, h2d, d2h = pipelined_e2e(dev, step, ep.inp["hidden"].cpu(), steps, warmup,
+                                     sync=torch.distributed.barrier)
+    t = torch.tensor([e2e_ms], device=dev)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     e2e_ms = float(t.item())
-    return ms, counts, clocks, e2e_ms, host_in.numel() * 2, host_out.numel() * 2
+    return ms, counts, clocks, e2e_ms, h2d, d2h
 
 
 def time_stack(dev, steps=48):

@@ -29,19 +29,22 @@ def route_topk(x, router_weight, top_k, bias=None, want_logits=True):
 
 
 KNX_E_UNSUPPORTED = -5
+FUSED_MAX_TOKENS = 512
 
 
 def rmsnorm_route_topk(x, norm_weight, eps, router_weight, top_k, bias=None, xperm=None,
                        round_bf16=True, want_logits=True):
     """fused_rmsnorm(x, norm_weight, eps, round_bf16, xperm) then route_topk on its output, as one
-    launch where the shapes allow (f16 x and weights, E in {64, 128}, H % 256 == 0, H <= 3840);
-    otherwise as the two calls.  Same bits either way.  -> (y, ids, weights, logits)."""
+    launch where the shapes allow (f16 x and weights, E in {64, 128}, H % 256 == 0, H <= 3840)
+    and the batch is a canvas (T <= FUSED_MAX_TOKENS: one cluster of 8 CTAs per 32 tokens, and
+    only ~15 such clusters are resident at once on a B200); otherwise as the two calls.  Same
+    bits either way.  -> (y, ids, weights, logits)."""
     import fused_rmsnorm
     dev = require_device(x)
     T, H = x.shape
     E = router_weight.shape[0]
-    if (x.dtype == torch.float16 and norm_weight is not None and norm_weight.dtype == torch.float16
-            and router_weight.dtype == torch.float16):
+    if (T <= FUSED_MAX_TOKENS and x.dtype == torch.float16 and norm_weight is not None
+            and norm_weight.dtype == torch.float16 and router_weight.dtype == torch.float16):
         xc = x.contiguous()
         nw = norm_weight.contiguous()
         wr = router_weight.contiguous()
