@@ -114,6 +114,11 @@ KNX_DEVINL uint4 lds128(uint32_t addr) {
                : "r"(addr));
   return r;
 }
+KNX_DEVINL void sts128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};\n" ::"r"(addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
 
 // lop3 with immediate truth table: (a & b) | c  -> 0xEA
 KNX_DEVINL uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {

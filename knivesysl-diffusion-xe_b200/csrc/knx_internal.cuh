@@ -5,6 +5,7 @@
 namespace knx {
 
 constexpr int64_t ALIGN_MAX_PAIRS = 32768;  // single-CTA counting sort limit (pairs)
+constexpr int MAX_TASK_TOKENS = 128;        // largest task size the task-list builders accept
 constexpr int ALIGN_MAX_EXPERTS = 256;
 
 bool align_supported(int64_t N, int E);
@@ -24,8 +25,8 @@ int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t
 int launch_tasks_from_offsets(const int32_t* offsets, int E, int m, int4* tasks, int32_t* ntasks,
                               int32_t* counters, cudaStream_t s);
 
-// tcgen05 grouped W4A16 GEMMs (knx_moe_tc.cu)
-constexpr int TC_TASK_TOKENS = 64;  // tokens per task on the tcgen05 path
+// tcgen05 grouped W4A16 GEMMs (knx_moe_tcp.cu): MMA M = the tokens of one task
+constexpr int TC_TASK_TOKENS = 128;  // tokens per task on the tcgen05 path
 bool tc_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated);
 int launch_tc_gateup(const __half* xp, const int32_t* sorted_pair, int topk, const int32_t* offsets,
                      const int4* tasks, const int32_t* ntasks, int* counter, const uint8_t* gu_q,

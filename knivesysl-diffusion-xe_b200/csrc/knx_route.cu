@@ -220,7 +220,8 @@ __global__ void __launch_bounds__(AL_THREADS)
   int* scan_buf = spblk + E + 1;                       // [100]
   int* size_hist = scan_buf + 100;                     // [m_max+1]
   int* scnt = size_hist + m_max + 1;                   // [E] pairs per expert
-  int* rhist = scnt + E;                               // [8][65] remainder counts per warp
+  int* rhist = scnt + E;                               // [8][m_max+1] remainder counts per warp
+  const int RH = m_max + 1;
 
   for (int i = tid; i < 32 * E; i += AL_THREADS) whist[i] = 0;
   for (int i = tid; i <= m_max; i += AL_THREADS) size_hist[i] = 0;
@@ -349,30 +350,37 @@ __global__ void __launch_bounds__(AL_THREADS)
 
   // task list: sizes descending; size_hist[s] becomes the number of tasks with size > s
   if (tasks) {
-    for (int i = tid; i < 8 * 65; i += AL_THREADS) rhist[i] = 0;
+    for (int i = tid; i < 8 * RH; i += AL_THREADS) rhist[i] = 0;
     __syncthreads();  // placement above still reads whist; rhist zeroed
     // rank of this expert's remainder task among the experts with the same remainder, in expert
     // order: lanes of one warp by __match_any_sync, earlier warps through rhist
     const int r = (e_me < E && rem > 0) ? rem : -1;
     const unsigned peers = __match_any_sync(0xffffffffu, r);
     const int rank_w = __popc(peers & lt_mask);
-    if (r > 0 && lane == __ffs(peers) - 1) rhist[warp * 65 + r] = __popc(peers);
+    if (r > 0 && lane == __ffs(peers) - 1) rhist[warp * RH + r] = __popc(peers);
     __syncthreads();
     if (warp == 0) {
-      // reverse exclusive scan over sizes s = m_max .. 1 (position i = m_max - s), two per lane
-      const int i0 = 2 * lane, i1 = i0 + 1;
-      const int v0 = i0 < m_max ? size_hist[m_max - i0] : 0;
-      const int v1 = i1 < m_max ? size_hist[m_max - i1] : 0;
-      const int a = v0 + v1;
+      // reverse exclusive scan over sizes s = m_max .. 1 (position i = m_max - s), four per lane
+      int v[4], a = 0;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = 4 * lane + j;
+        v[j] = i < m_max ? size_hist[m_max - i] : 0;
+        a += v[j];
+      }
       int incl = a;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int n = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += n;
       }
-      const int base = incl - a;
-      if (i0 < m_max) size_hist[m_max - i0] = base;
-      if (i1 < m_max) size_hist[m_max - i1] = base + v0;
+      int base = incl - a;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int i = 4 * lane + j;
+        if (i < m_max) size_hist[m_max - i] = base;
+        base += v[j];
+      }
       if (lane == 31) *ntasks = incl;
     }
     __syncthreads();
@@ -381,7 +389,7 @@ __global__ void __launch_bounds__(AL_THREADS)
         tasks[size_hist[m_max] + fpre + j] = make_int4(e_me, j * m_max, m_max, 0);
       if (rem > 0) {
         int before_same = rank_w;
-        for (int w2 = 0; w2 < warp; ++w2) before_same += rhist[w2 * 65 + rem];
+        for (int w2 = 0; w2 < warp; ++w2) before_same += rhist[w2 * RH + rem];
         tasks[size_hist[rem] + before_same] = make_int4(e_me, nfull * m_max, rem, 0);
       }
     }
@@ -397,9 +405,16 @@ __global__ void tasks_from_offsets_kernel(const int32_t* __restrict__ offsets, i
   pdl_wait_trigger();
   __shared__ int full_pre[257];
   __shared__ int rem_of[256];
-  __shared__ int rem_start[65];
+  __shared__ int rem_cnt[MAX_TASK_TOKENS + 1];
+  __shared__ int rem_start[MAX_TASK_TOKENS + 1];
   const int tid = threadIdx.x;
-  if (tid < E) rem_of[tid] = (offsets[tid + 1] - offsets[tid]) % m;
+  for (int r = tid; r <= m; r += blockDim.x) rem_cnt[r] = 0;
+  __syncthreads();
+  if (tid < E) {
+    const int rem = (offsets[tid + 1] - offsets[tid]) % m;
+    rem_of[tid] = rem;
+    if (rem > 0) atomicAdd(&rem_cnt[rem], 1);
+  }
   __syncthreads();
   if (tid == 0) {
     int acc = 0;
@@ -410,7 +425,7 @@ __global__ void tasks_from_offsets_kernel(const int32_t* __restrict__ offsets, i
     full_pre[E] = acc;
     for (int r = m - 1; r >= 1; --r) {
       rem_start[r] = acc;
-      for (int e = 0; e < E; ++e) acc += rem_of[e] == r;
+      acc += rem_cnt[r];
     }
     *ntasks = acc;
     counters[0] = 0;
@@ -575,7 +590,7 @@ constexpr int RT_KSPLIT_PUBLIC = RT_KSPLIT;
 size_t align_smem_bytes(int N, int E, int m_max) {
   const int npad = (N + 7) & ~7;
   return static_cast<size_t>(npad) * 4 +
-         static_cast<size_t>(32 * E + 2 * (E + 1) + 100 + m_max + 1 + E + 8 * 65) * 4;
+         static_cast<size_t>(32 * E + 2 * (E + 1) + 100 + m_max + 1 + E + 8 * (m_max + 1)) * 4;
 }
 
 bool align_supported(int64_t N, int E) {
@@ -588,7 +603,7 @@ int launch_align(const void* ids, int ids_dtype, int T, int topk, int E, int blo
                  int32_t* ntasks, int32_t* work_counters, int n_work_counters, int32_t* err,
                  cudaStream_t stream) {
   const int N = T * topk;
-  if (tasks && (m_max < 1 || m_max > 64)) return KNX_E_UNSUPPORTED;  // task sizes: one warp scan
+  if (tasks && (m_max < 1 || m_max > MAX_TASK_TOKENS)) return KNX_E_UNSUPPORTED;  // one warp scan
   const size_t smem = align_smem_bytes(N, E, m_max);
   static bool attr_set[64] = {};
   int dev = 0;
@@ -643,7 +658,7 @@ int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t
 
 int launch_tasks_from_offsets(const int32_t* offsets, int E, int m, int4* tasks, int32_t* ntasks,
                               int32_t* counters, cudaStream_t s) {
-  if (E > 256 || m > 64) return KNX_E_UNSUPPORTED;
+  if (E > 256 || m < 1 || m > MAX_TASK_TOKENS) return KNX_E_UNSUPPORTED;
   (void)launch_pdl(tasks_from_offsets_kernel, 1, 256, 0, s, offsets, E, m, tasks, ntasks, counters);
   return launch_status();
 }

@@ -1,6 +1,6 @@
 // knx_sm100.cuh — Blackwell (sm_100a) building blocks: mbarriers with bounded waits, TMA tensor
 // loads, 1-D bulk copies, tensor-memory (TMEM) allocation / loads / stores, tcgen05.mma with the A
-// operand in TMEM, UMMA shared-memory and instruction descriptors.
+// operand in TMEM or shared memory, UMMA shared-memory and instruction descriptors.
 //
 // Descriptor formats (PTX ISA "Matrix Descriptors" / "Instruction descriptor" for tcgen05.mma):
 //   shared-memory descriptor (64 bit): [0,14) start address >> 4, [16,30) leading byte offset >> 4,
@@ -167,6 +167,15 @@ KNX_DEVINL void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, ui
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f16, one CTA.
+KNX_DEVINL void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // Arrive on `bar` once every tcgen05.mma previously issued by this thread has completed.
