@@ -37,10 +37,10 @@ NSETS = 4
 # The dominant kernel per GEMM engine, and its DRAM bytes per launch (dram__bytes_read.sum +
 # dram__bytes_write.sum) from one ncu capture of the configs[1] layer, summarised under profiles/;
 # None where no capture of the current kernel exists.
-GEMM1_KERNEL = {"tc": "tc_gemm_kernel<1,0> (gate_up + GELU)",
+GEMM1_KERNEL = {"tc": "tcp_gemm_kernel<1,0> (gate_up + GELU)",
                 "ws": "hw_gemm_kernel<1,0,4> (gate_up + GELU)",
                 "mma": "gateup_gelu_kernel"}
-GEMM1_NCU_TRAFFIC = {"tc": 276.584960e6 + 6.810624e6, "ws": 288.256512e6 + 5.845248e6}
+GEMM1_NCU_TRAFFIC = {"tc": None, "ws": 288.256512e6 + 5.845248e6}
 
 
 def peaks():

@@ -9,17 +9,18 @@
 // M128 x N256 x K16 shape.  One persistent CTA per SM, warp-specialised:
 //
 //   warp 20      scheduler + weight producer: pulls (task, slice) work items from the counter,
-//                publishes them in a 2-slot item ring, then streams the slice's packed nibbles
-//                with 2-D TMA loads (32 B x 64 rows boxes, no swizzle) into a 6-stage ring, 64 k
-//                per stage.
-//   warp 21      activation producer: gathers the task's token rows (K-interleaved f16) with
+//                publishes them in a 2-slot item ring, bulk-copies the item's scale / zero rows
+//                into the item's shared-memory slot, then streams the slice's packed nibbles with
+//                2-D TMA loads (32 B x 64 rows boxes, no swizzle) into a 4-stage ring, 64 k per
+//                stage.
+//   warps 21-22  activation producers: gather the task's token rows (K-interleaved f16) with
 //                cp.async straight into the UMMA 128-byte-swizzle K-major layout (8 lanes per
-//                128-byte row), 4-stage ring.
+//                128-byte row, 64 rows per warp; one warp's instruction stream was the limit),
+//                4-stage ring.
 //   warps 0-15   dequant: thread = (weight row, half of the stage's 64 k).  Nibbles -> f16 pairs
 //                in registers (dequant8), stored into the B operand ring in the 128-byte-swizzle
-//                K-major layout, 3 stages.  Scale / zero of the thread's row are read from global
-//                memory two groups ahead.
-//   warp 22      MMA issuer (one thread): tcgen05.mma kind::f16, A and B from shared memory through
+//                K-major layout, 2 stages.  Scale / zero come from the item's slot.
+//   warp 23      MMA issuer (one thread): tcgen05.mma kind::f16, A and B from shared memory through
 //                descriptors, D (fp32, 128 token lanes x N columns) in TMEM, double-buffered across
 //                work items (2 x 256 columns); tcgen05.commit releases the stages and D.
 //   warps 16-19  epilogue: thread = token (TMEM lane).  tcgen05.ld of D; gated: gate column c and
@@ -28,8 +29,8 @@
 //
 // Work item (task, slice): gated slices hold gate rows [128 s, 128 s + h) and the matching up rows
 // (h = min(128, I - 128 s), N = 2 h); plain slices hold rows [256 s, 256 s + N), N <= 256.  Token
-// rows past the task's count are not loaded: their A rows hold stale data, their D rows are never
-// stored, and rows of an MMA are independent.  Every barrier wait is bounded (2 s); on a timeout the
+// rows past the task's count load token 0's row again: their D rows are never stored, and rows of
+// an MMA are independent.  Every barrier wait is bounded (2 s); on a timeout the
 // kernel records KNX_DEV_TIMEOUT in the error word, all roles leave their loops, and the CTA
 // releases its tensor memory before returning.
 #include "knx_common.cuh"
@@ -46,9 +47,10 @@ constexpr int NROWS = 256;                // weight rows per work item (MMA N <=
 constexpr int BK = 64;                    // k per stage
 constexpr int WROW = BK / 2;              // 32 bytes of nibbles per weight row per stage
 constexpr int BOX_ROWS = 64;              // rows per TMA box
-constexpr int SW = 6;                     // packed weight stages
-constexpr int SB = 3;                     // dequantised weight stages (MMA B operand)
+constexpr int SW = 4;                     // packed weight stages
+constexpr int SB = 2;                     // dequantised weight stages (MMA B operand)
 constexpr int SA = 4;                     // activation stages (MMA A operand)
+constexpr int SZ_MAX_NG = 30;             // scale groups per weight row on this path
 constexpr int IR = 2;                     // work-item ring slots
 constexpr int W_STAGE = NROWS * WROW;     // 8 KB
 constexpr int B_STAGE = NROWS * 128;      // 32 KB: 256 rows x 64 f16
@@ -58,10 +60,12 @@ constexpr int TMEM_COLS = 2 * D_COLS;
 constexpr int DQ_WARPS = 16;
 constexpr int EPI_WARPS = 4;
 constexpr int WARP_EPI0 = DQ_WARPS;       // warps 16-19 (lane quadrant = warp % 4)
-constexpr int WARP_WPROD = DQ_WARPS + EPI_WARPS, WARP_APROD = WARP_WPROD + 1, WARP_MMA = WARP_WPROD + 2;
+constexpr int A_WARPS = 2;                // activation producer warps
+constexpr int WARP_WPROD = DQ_WARPS + EPI_WARPS, WARP_APROD0 = WARP_WPROD + 1;
+constexpr int WARP_MMA = WARP_APROD0 + A_WARPS;
 constexpr int NUM_WARPS = WARP_MMA + 1;
 constexpr int NTHREADS = NUM_WARPS * 32;
-constexpr int ITEM_CONSUMERS = DQ_WARPS + EPI_WARPS + 2;  // dequant, epilogue, act producer, MMA
+constexpr int ITEM_CONSUMERS = DQ_WARPS + EPI_WARPS + A_WARPS + 1;  // + the MMA warp
 static_assert(DQ_WARPS * 32 == 2 * NROWS, "dequant threads = 2 per weight row");
 static_assert(TOKM == 128, "MMA M");
 
@@ -76,6 +80,7 @@ struct Ctrl {
   uint64_t a_full[SA], a_empty[SA];
   uint64_t d_full[2], d_empty[2];
   uint64_t i_full[IR], i_empty[IR];
+  uint64_t sz_full[IR];  // the item's scale / zero rows have landed (dequant warps)
   uint64_t fin;  // MMA drain before tensor memory is released
   Item items[IR];
   uint32_t tmem_base;
@@ -105,10 +110,14 @@ struct Params {
 };
 
 // smem layout (from a 1024-aligned base): activation ring, dequantised weight ring, packed ring
+// and the scale / zero slots of the item ring: [s of the item's rows][z of the item's rows], f16,
+// rows in B-operand order (gated: gate rows, then up rows)
 constexpr int OFF_A = 0;
 constexpr int OFF_B = OFF_A + SA * A_STAGE;
 constexpr int OFF_W = OFF_B + SB * B_STAGE;
-constexpr size_t SMEM_BYTES = 1024 + OFF_W + SW * W_STAGE;
+constexpr int OFF_SZ = OFF_W + SW * W_STAGE;
+KNX_HOST_DEVINL int sz_slot_bytes(int ng) { return 2 * NROWS * ng * 2; }
+inline size_t smem_bytes(int ng) { return 1024 + OFF_SZ + static_cast<size_t>(IR) * sz_slot_bytes(ng); }
 
 KNX_DEVINL float gelu_tanh(float x) {
   const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
@@ -116,11 +125,11 @@ KNX_DEVINL float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + th);
 }
 
+// f16x2 of two floats, low half = a
 KNX_DEVINL void cp_async16_s(uint32_t saddr, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(saddr), "l"(gmem) : "memory");
 }
 
-// f16x2 of two floats, low half = a
 KNX_DEVINL uint32_t pack_h2(float a, float b) { return h2_as_u32(__floats2half2_rn(a, b)); }
 
 template <bool GATED, bool ZINT>
@@ -133,16 +142,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t a_ring = smem_u32(base + OFF_A);
   const uint32_t b_ring = smem_u32(base + OFF_B);
   uint8_t* w_ring = base + OFF_W;
+  uint8_t* sz_ring = base + OFF_SZ;
+  const int szb = sz_slot_bytes(p.ng);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nst = p.K / BK;
 
   if (tid == 0) {
     for (int s = 0; s < SW; ++s) { mbar_init(&ctrl.w_full[s], 1); mbar_init(&ctrl.w_empty[s], DQ_WARPS); }
     for (int s = 0; s < SB; ++s) { mbar_init(&ctrl.b_full[s], DQ_WARPS); mbar_init(&ctrl.b_empty[s], 1); }
-    for (int s = 0; s < SA; ++s) { mbar_init(&ctrl.a_full[s], 32); mbar_init(&ctrl.a_empty[s], 1); }
+    for (int s = 0; s < SA; ++s) { mbar_init(&ctrl.a_full[s], 32 * A_WARPS); mbar_init(&ctrl.a_empty[s], 1); }
     for (int d = 0; d < 2; ++d) { mbar_init(&ctrl.d_full[d], 1); mbar_init(&ctrl.d_empty[d], EPI_WARPS); }
     for (int i = 0; i < IR; ++i) {
       mbar_init(&ctrl.i_full[i], 1);
+      mbar_init(&ctrl.sz_full[i], 1);
       mbar_init(&ctrl.i_empty[i], ITEM_CONSUMERS);
     }
     mbar_init(&ctrl.fin, 1);
@@ -202,9 +214,29 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         ctrl.items[slot] = it;
         mbar_arrive(&ctrl.i_full[slot]);
         if (!it.valid) break;
-        // packed weights: one stage = 64 k of the slice's rows, in boxes of 64 rows
         const int64_t erow = static_cast<int64_t>(it.e) * p.rows_per_expert;
         const int half = it.nrows >> 1;
+        // scale / zero rows of the item -> its slot (1-D bulk copies; rows are whole 64-row
+        // boxes, so every offset and size is a multiple of 128 bytes)
+        {
+          uint8_t* szs = sz_ring + slot * szb;
+          const uint32_t zoff = static_cast<uint32_t>(it.nrows) * p.ng * 2;
+          mbar_arrive_expect_tx(&ctrl.sz_full[slot], 2 * zoff);
+          if (GATED) {
+            const int64_t g0 = (erow + it.slice * (NROWS / 2)) * p.ng;
+            const int64_t u0 = g0 + static_cast<int64_t>(p.I) * p.ng;
+            const uint32_t b = static_cast<uint32_t>(half) * p.ng * 2;
+            bulk_load(szs, p.ws + g0, b, &ctrl.sz_full[slot]);
+            bulk_load(szs + b, p.ws + u0, b, &ctrl.sz_full[slot]);
+            bulk_load(szs + zoff, p.wz + g0, b, &ctrl.sz_full[slot]);
+            bulk_load(szs + zoff + b, p.wz + u0, b, &ctrl.sz_full[slot]);
+          } else {
+            const int64_t r0 = (erow + it.slice * NROWS) * p.ng;
+            bulk_load(szs, p.ws + r0, zoff, &ctrl.sz_full[slot]);
+            bulk_load(szs + zoff, p.wz + r0, zoff, &ctrl.sz_full[slot]);
+          }
+        }
+        // packed weights: one stage = 64 k of the slice's rows, in boxes of 64 rows
         for (int st = 0; st < nst; ++st, ++wst) {
           const int s = wst % SW;
           if (!wait(&ctrl.w_empty[s], ((wst / SW) & 1) ^ 1)) break;
@@ -227,12 +259,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
     __syncwarp();
-  } else if (warp == WARP_APROD) {
+  } else if (warp >= WARP_APROD0 && warp < WARP_APROD0 + A_WARPS) {
     // ---------------------------------------------------------------- activation gather
-    // lane l copies 16-byte chunk (l % 8) of rows 4 i + l / 8, i = 0..31, straight into the
-    // swizzled K-major layout: row t, chunk j -> (t / 8) * 1024 + (t % 8) * 128 + ((j ^ t % 8) * 16)
+    // A_WARPS warps split the 128 token rows; lane l of warp a copies 16-byte chunk (l % 8) of
+    // rows 4 i + l / 8 for the warp's row groups i, straight into the swizzled K-major layout:
+    // row t, chunk j -> (t / 8) * 1024 + (t % 8) * 128 + ((j ^ t % 8) * 16).  The lane's source
+    // pointers are set once per item and advance by one stage each stage; rows past the task's
+    // count copy token 0's row (their D rows are never stored).
+    constexpr int AI = TOKM / 4 / A_WARPS;  // row groups (of four rows) per warp
+    constexpr int AJ = TOKM / 32 / A_WARPS; // activation rows held per lane
+    static_assert(AJ >= 1 && AI == 8 * AJ, "producer row mapping");
+    const int aw = warp - WARP_APROD0;
     uint32_t ast = 0;
     const int rsub = lane >> 3, ch = lane & 7;
+    // shared-memory offset of this lane's chunk of row group i (same for every stage)
+    uint32_t doff[AI];
+#pragma unroll
+    for (int i = 0; i < AI; ++i) {
+      const int t = 4 * (aw * AI + i) + rsub;
+      doff[i] = (t >> 3) * 1024 + (t & 7) * 128 + ((ch ^ (t & 7)) << 4);
+    }
     for (int n = 0;; ++n) {
       const int slot = n % IR;
       if (!wait(&ctrl.i_full[slot], (n / IR) & 1, 64)) break;
@@ -242,13 +288,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (lane == 0) mbar_arrive(&ctrl.i_empty[slot]);
         break;
       }
-      // activation row of tokens lane + 32 j (-1: past the task's count)
-      int arow[4];
+      // activation row of tokens 32 (aw * AJ + j) + lane
+      int arow[AJ];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int t = lane + 32 * j;
-        arow[j] = t < it.cnt ? (p.sorted_pair ? p.sorted_pair[it.slot0 + t] / p.topk : it.slot0 + t)
-                             : -1;
+      for (int j = 0; j < AJ; ++j) {
+        const int t = 32 * (aw * AJ + j) + lane;
+        const int tt = t < it.cnt ? t : 0;
+        arow[j] = p.sorted_pair ? p.sorted_pair[it.slot0 + tt] / p.topk : it.slot0 + tt;
+      }
+      const __half* src[AI];
+#pragma unroll
+      for (int i = 0; i < AI; ++i) {
+        const int t = 4 * (aw * AI + i) + rsub;
+        const int r = __shfl_sync(0xffffffffu, arow[i >> 3], t & 31);
+        src[i] = p.act + static_cast<int64_t>(r) * p.act_stride + ch * 8;
       }
       bool ok = true;
       for (int st = 0; st < nst; ++st, ++ast) {
@@ -258,14 +311,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           break;
         }
         const uint32_t dst = a_ring + s * A_STAGE;
-        const __half* src = p.act + st * BK + ch * 8;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int t = 4 * i + rsub;
-          const int r = __shfl_sync(0xffffffffu, arow[i >> 3], t & 31);
-          if (r >= 0)
-            cp_async16_s(dst + (t >> 3) * 1024 + (t & 7) * 128 + ((ch ^ (t & 7)) << 4),
-                         src + static_cast<int64_t>(r) * p.act_stride);
+        for (int i = 0; i < AI; ++i) {
+          cp_async16_s(dst + doff[i], src[i]);
+          src[i] += BK;
         }
         cp_async_mbar_arrive_noinc(&ctrl.a_full[s]);
       }
@@ -289,23 +338,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         break;
       }
       const bool row_ok = row < it.nrows;
-      int grow;  // row of the expert
-      if (GATED) {
-        const int half = it.nrows >> 1;
-        grow = it.slice * (NROWS / 2) + (row < half ? row : p.I + row - half);
-      } else {
-        grow = it.slice * NROWS + row;
-      }
-      const int64_t sz0 = (static_cast<int64_t>(it.e) * p.rows_per_expert + (row_ok ? grow : 0)) * p.ng;
-      const __half* srow = p.ws + sz0;
-      const __half* zrow = p.wz + sz0;
-      // scale / zero of groups g (cur) and g + 1 (nxt), loaded two groups ahead
-      __half s_cur = __ushort_as_half(0), z_cur = __ushort_as_half(0);
-      __half s_nxt = __ushort_as_half(0), z_nxt = __ushort_as_half(0);
-      if (row_ok) {
-        s_cur = srow[0]; z_cur = zrow[0];
-        if (p.ng > 1) { s_nxt = srow[1]; z_nxt = zrow[1]; }
-      }
+      // this row's scale / zero in the item's slot (rows in B order)
+      const uint32_t srow = smem_u32(sz_ring + slot * szb) + row * p.ng * 2;
+      const uint32_t zrow = srow + it.nrows * p.ng * 2;
+      if (!wait(&ctrl.sz_full[slot], (n / IR) & 1, 64)) break;
       __half2 s2 = __half2half2(__ushort_as_half(0)), s16 = s2, cc = s2, c16 = s2;
       const uint32_t wrow = smem_u32(w_ring) + row * WROW + kh * 16;
       const uint32_t brow = b_ring + (row >> 3) * 1024 + (row & 7) * 128;
@@ -321,11 +357,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         uint4 u = make_uint4(0u, 0u, 0u, 0u);
         if (row_ok) {
           if (gleft == 0) {  // first stage of a scale group
-            const uint2 c = make_sz<ZINT>(s_cur, z_cur);
+            const uint2 c = make_sz<ZINT>(lds16h(srow + 2 * g), lds16h(zrow + 2 * g));
             s2 = __low2half2(u32_as_h2(c.x)); cc = __high2half2(u32_as_h2(c.x));
             s16 = __low2half2(u32_as_h2(c.y)); c16 = __high2half2(u32_as_h2(c.y));
-            s_cur = s_nxt; z_cur = z_nxt;
-            if (g + 2 < p.ng) { s_nxt = srow[g + 2]; z_nxt = zrow[g + 2]; }
             ++g;
             gleft = gstages;
           }
@@ -527,13 +561,16 @@ bool encode_weight_map(CUtensorMap* map, const uint8_t* q, int64_t total_rows, i
 template <bool GATED, bool ZINT>
 int launch_tcp(const tcp::Params& p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
                int64_t work_bound, cudaStream_t s) {
+  // the scale / zero bulk copies need 16-byte aligned bases
+  if ((reinterpret_cast<uintptr_t>(p.ws) & 15) || (reinterpret_cast<uintptr_t>(p.wz) & 15))
+    return KNX_E_ALIGN;
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
     if (cudaFuncSetAttribute(tcp::tcp_gemm_kernel<GATED, ZINT>,
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(tcp::SMEM_BYTES)) != cudaSuccess)
+                             static_cast<int>(tcp::smem_bytes(tcp::SZ_MAX_NG))) != cudaSuccess)
       return KNX_E_DEVICE;
     attr[dev & 63] = true;
   }
@@ -541,16 +578,19 @@ int launch_tcp(const tcp::Params& p, const uint8_t* wq, int64_t total_rows, int6
   if (!encode_weight_map(&map, wq, total_rows, row_bytes)) return KNX_E_DEVICE;
   const int sms = num_sms();
   const int grid = static_cast<int>(work_bound < sms ? (work_bound > 0 ? work_bound : 1) : sms);
-  (void)launch_pdl(tcp::tcp_gemm_kernel<GATED, ZINT>, grid, tcp::NTHREADS, tcp::SMEM_BYTES, s, map, p);
+  (void)launch_pdl(tcp::tcp_gemm_kernel<GATED, ZINT>, grid, tcp::NTHREADS, tcp::smem_bytes(p.ng), s,
+                   map, p);
   return launch_status();
 }
 
 }  // namespace
 
-// K a multiple of the stage, scale groups whole stages, weight rows whole TMA boxes; the row
+// K a multiple of the stage, scale groups whole stages and at most SZ_MAX_NG of them (the item's
+// scale / zero rows sit in shared memory), weight rows whole TMA boxes; the row
 // indices of the tensor map (expert * rows + row) stay below 2^31.
 bool tc_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated) {
-  if (K % tcp::BK != 0 || gs % tcp::BK != 0 || ng < 1 || static_cast<int64_t>(ng) * gs != K)
+  if (K % tcp::BK != 0 || gs % tcp::BK != 0 || ng < 1 || ng > tcp::SZ_MAX_NG ||
+      static_cast<int64_t>(ng) * gs != K)
     return false;
   if (gated) return (rows_per_expert / 2) % tcp::BOX_ROWS == 0 && rows_per_expert % 2 == 0;
   return rows_per_expert % tcp::BOX_ROWS == 0;
