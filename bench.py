@@ -394,7 +394,7 @@ def time_prefill(dev, steps, rank, world):
             "tokens": PREFILL_TOKENS, "n_gpus": world,
             "per_gpu_hbm_gbs": layer_bytes / world / (ms * 1e-3) / 1e9,
             "max_tokens_per_expert": int(counts.max()),
-            "engine": "tc" if tpe > 64 else "ws"}
+            "engine": "tc" if tpe > 36 else "ws"}
 
 
 def time_sampler(dev, reps=1):
@@ -568,8 +568,8 @@ def main():
     # the kernel roofline is the single-GPU layer's (per-stage events exist only there)
     achieved = gemm1_bytes / (gemm1_ms * 1e-3) / 1e9 if gemm1_ms else None
     engine = os.environ.get("KNX_ENGINE", "auto")
-    if engine == "auto":  # the library's rule: ws up to 64 pairs per expert, tcgen05 above
-        engine = "ws" if T * TOPK // E <= 64 else "tc"
+    if engine == "auto":  # the library's rule: ws up to 36 pairs per expert, tcgen05 above
+        engine = "ws" if T * TOPK // E <= 36 else "tc"
     line = {
         "metric": METRIC, "value": value, "unit": "us", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False,

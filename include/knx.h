@@ -57,11 +57,11 @@ extern "C" {
 
 /* weight-format / engine flags */
 #define KNX_W4_INT_ZEROS 0x1 /* all zero-points are integers in [0, 15] */
-/* GEMM engine (at most one; none = automatic: the warp-specialised mma.sync kernels up to 64
+/* GEMM engine (at most one; none = automatic: the warp-specialised mma.sync kernels up to 36
  * (token, slot) pairs per expert on average, tcgen05 above that) */
 #define KNX_W4_WARP_MMA 0x2  /* the plain mma.sync kernels (A/B runs) */
 #define KNX_W4_WARP_WS 0x8   /* the warp-specialised mma.sync kernels (TMA-fed, 16 math warps) */
-#define KNX_W4_TCGEN05 0x10  /* the tcgen05 kernels (A in tensor memory, TMA-fed) */
+#define KNX_W4_TCGEN05 0x10  /* the tcgen05 kernels (128 tokens x 256 weight rows per MMA) */
 
 KNX_API int knx_version(void);
 /* 1 when the current device is a compute-capability 10.0 part (the only target). */

@@ -503,13 +503,15 @@ struct MoeWs {
 inline size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
 // The GEMM engine a call runs: an explicit flag, else the warp-specialised mma.sync kernels for
-// small per-expert token counts (where a tcgen05 instruction's ~108 ns cost does not pay off)
-// and tcgen05 for large ones.
+// small per-expert token counts and tcgen05 for large ones.  The switch point is the measured
+// crossover of the two on B200 (MoE call with Zipf routing, H 2816, I 704): ws 297 / tc 317 us at
+// 32 pairs per expert, ws 399 / tc 332 us at 48.
+constexpr int64_t WS_MAX_TOKENS_PER_EXPERT = 36;
 int engine_choice(int flags, int64_t tokens_per_expert) {
   if (flags & KNX_W4_WARP_MMA) return KNX_W4_WARP_MMA;
   if (flags & KNX_W4_WARP_WS) return KNX_W4_WARP_WS;
   if (flags & KNX_W4_TCGEN05) return KNX_W4_TCGEN05;
-  return tokens_per_expert <= 64 ? KNX_W4_WARP_WS : KNX_W4_TCGEN05;
+  return tokens_per_expert <= WS_MAX_TOKENS_PER_EXPERT ? KNX_W4_WARP_WS : KNX_W4_TCGEN05;
 }
 
 MoeWs carve_moe_ws(uint8_t* base, int64_t T, int64_t H, int64_t I, int E, int topk) {

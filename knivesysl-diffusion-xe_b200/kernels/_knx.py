@@ -32,7 +32,7 @@ _ENGINES = {"auto": 0, "tc": KNX_W4_TCGEN05, "mma": KNX_W4_WARP_MMA, "ws": KNX_W
 
 def engine_flags(engine=None):
     """Engine selection flags for the W4A16 GEMMs: "auto" (the default: the warp-specialised
-    mma.sync kernels up to 64 tokens per expert, tcgen05 above), "ws", "tc" (tcgen05) or "mma"
+    mma.sync kernels up to 36 tokens per expert, tcgen05 above), "ws", "tc" (tcgen05) or "mma"
     (the plain mma.sync kernels); `engine` or the KNX_ENGINE environment variable chooses."""
     engine = engine or os.environ.get("KNX_ENGINE", "auto")
     if engine not in _ENGINES:
