@@ -51,6 +51,17 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def tensor_peak():
+    """Dense f16/bf16 tensor peak (TFLOP/s) for a kernel timed inside a multi-millisecond step:
+    the sustained cuBLAS figure of MEASURED_PEAKS.json, else the recipe's fallback."""
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        if "bf16_tflops_sustained" in d:
+            return float(d["bf16_tflops_sustained"]), "measured sustained"
+    return 1400.0, "fallback sustained"
+
+
 # --------------------------------------------------------------------------------- clocks
 class Clocks:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
@@ -390,8 +401,13 @@ def time_prefill(dev, steps, rank, world):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item()) / steps
     layer_bytes = workloads.moe_layer_bytes(counts.cpu().numpy(), T=PREFILL_TOKENS)
+    # tensor-bound at ~1150 pairs per expert: the expert GEMMs' FLOPs per GPU over the step time
+    tpeak, tkind = tensor_peak()
+    tflops = workloads.moe_layer_flops(PREFILL_TOKENS * TOPK) / world / (ms * 1e-3) / 1e12
     return {"tokens_per_s": PREFILL_TOKENS / (ms * 1e-3), "ms_per_step": ms, "steps": steps,
             "tokens": PREFILL_TOKENS, "n_gpus": world,
+            "per_gpu_tflops": tflops, "tensor_frac": tflops / tpeak, "tensor_peak_tflops": tpeak,
+            "tensor_peak_kind": tkind,
             "per_gpu_hbm_gbs": layer_bytes / world / (ms * 1e-3) / 1e9,
             "max_tokens_per_expert": int(counts.max()),
             "engine": "tc" if tpe > 36 else "ws"}
