@@ -25,7 +25,8 @@
 //                work items (2 x 256 columns); tcgen05.commit releases the stages and D.
 //   warps 16-19  epilogue: thread = token (TMEM lane).  tcgen05.ld of D; gated: gate column c and
 //                up column c + N/2 sit in the same lane, so tanh-GELU(gate) * up needs no exchange;
-//                plain: f16 cast.  Each thread stores its own token's output row.
+//                plain: f16 cast.  Each warp stages 32 tokens x 64 columns in shared memory and
+//                stores them as whole 128-byte row pieces.
 //
 // Work item (task, slice): gated slices hold gate rows [128 s, 128 s + h) and the matching up rows
 // (h = min(128, I - 128 s), N = 2 h); plain slices hold rows [256 s, 256 s + N), N <= 256.  Token
@@ -50,7 +51,8 @@ constexpr int BOX_ROWS = 64;              // rows per TMA box
 constexpr int SW = 4;                     // packed weight stages
 constexpr int SB = 2;                     // dequantised weight stages (MMA B operand)
 constexpr int SA = 4;                     // activation stages (MMA A operand)
-constexpr int SZ_MAX_NG = 30;             // scale groups per weight row on this path
+constexpr int SZ_MAX_NG = 24;             // scale groups per weight row on this path
+constexpr int EPI_WARP_BYTES = 32 * 128;  // epilogue staging tile per warp: 32 tokens x 64 f16
 constexpr int IR = 2;                     // work-item ring slots
 constexpr int W_STAGE = NROWS * WROW;     // 8 KB
 constexpr int B_STAGE = NROWS * 128;      // 32 KB: 256 rows x 64 f16
@@ -117,7 +119,10 @@ constexpr int OFF_B = OFF_A + SA * A_STAGE;
 constexpr int OFF_W = OFF_B + SB * B_STAGE;
 constexpr int OFF_SZ = OFF_W + SW * W_STAGE;
 KNX_HOST_DEVINL int sz_slot_bytes(int ng) { return 2 * NROWS * ng * 2; }
-inline size_t smem_bytes(int ng) { return 1024 + OFF_SZ + static_cast<size_t>(IR) * sz_slot_bytes(ng); }
+// ... followed by the epilogue warps' staging tiles
+inline size_t smem_bytes(int ng) {
+  return 1024 + OFF_SZ + static_cast<size_t>(IR) * sz_slot_bytes(ng) + EPI_WARPS * EPI_WARP_BYTES;
+}
 
 KNX_DEVINL float gelu_tanh(float x) {
   const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
@@ -433,8 +438,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp >= WARP_EPI0 && warp < WARP_EPI0 + EPI_WARPS) {
     // ---------------------------------------------------------------- epilogue
     const int q = warp & 3;
-    const int tok = 32 * q + lane;
     const uint32_t lane_addr = (32u * q) << 16;
+    const uint32_t stg = smem_u32(sz_ring + IR * szb) + q * EPI_WARP_BYTES;  // this warp's tile
     uint32_t dc = 0;
     for (int n = 0;; ++n) {
       const int slot = n % IR;
@@ -449,54 +454,54 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (!wait(&ctrl.d_full[db], (dc >> 1) & 1, 128)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem + lane_addr + db * D_COLS;
-      const bool live = tok < it.cnt;
-      __half* orow = p.out + static_cast<int64_t>(it.slot0 + (live ? tok : 0)) * p.out_stride;
-      if (GATED) {
-        // gate column c, up column c + h; out2 channel 128 s + c, written in the K-interleaved
-        // order the down GEMM reads: within each 8-group [c0, c4, c1, c5, c2, c6, c3, c7]
-        const int half = it.nrows >> 1;
-        __half* o = orow + it.slice * (NROWS / 2);
+      // Output columns in blocks of 64: each thread (token) packs its 64 f16 into the warp's
+      // 4 KB staging tile (row = token, 128-byte rows, 16-byte chunks XOR-swizzled by row), then
+      // the warp stores the tile row-wise, four rows of 128 bytes per instruction.
+      const int ncols = GATED ? (it.nrows >> 1) : it.nrows;
+      const int colbase = GATED ? it.slice * (NROWS / 2) : it.slice * NROWS;
+      const uint32_t srow = stg + lane * 128;
 #pragma unroll 1
-        for (int c = 0; c < half; c += 16) {
-          uint32_t gv[16], uv[16];
-          tmem_ld16(d_tmem + c, gv);
-          tmem_ld16(d_tmem + half + c, uv);
-          tmem_wait_ld();
-          float r[16];
+      for (int cb = 0; cb < ncols; cb += 64) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            r[i] = gelu_tanh(__uint_as_float(gv[i])) * __uint_as_float(uv[i]);
-          if (live) {
-            uint4 v0, v1;
-            v0.x = pack_h2(r[0], r[4]);  v0.y = pack_h2(r[1], r[5]);
-            v0.z = pack_h2(r[2], r[6]);  v0.w = pack_h2(r[3], r[7]);
-            v1.x = pack_h2(r[8], r[12]); v1.y = pack_h2(r[9], r[13]);
-            v1.z = pack_h2(r[10], r[14]); v1.w = pack_h2(r[11], r[15]);
-            *reinterpret_cast<uint4*>(o + c) = v0;
-            *reinterpret_cast<uint4*>(o + c + 8) = v1;
+        for (int sub = 0; sub < 4; ++sub) {
+          const int c = cb + 16 * sub;
+          uint32_t w[8];
+          if (GATED) {
+            // gate column c, up column c + h; out2 channel 128 s + c, written in the
+            // K-interleaved order the down GEMM reads: in each 8-group [c0, c4, c1, c5, c2, c6, c3, c7]
+            uint32_t gv[16], uv[16];
+            tmem_ld16(d_tmem + c, gv);
+            tmem_ld16(d_tmem + ncols + c, uv);
+            tmem_wait_ld();
+            float r[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              r[i] = gelu_tanh(__uint_as_float(gv[i])) * __uint_as_float(uv[i]);
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) w[4 * h + i] = pack_h2(r[8 * h + i], r[8 * h + i + 4]);
+          } else {
+            uint32_t v[16];
+            tmem_ld16(d_tmem + c, v);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) w[i] = pack_h2(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
           }
+          sts128(srow + (((2 * sub) ^ (lane & 7)) << 4), w[0], w[1], w[2], w[3]);
+          sts128(srow + (((2 * sub + 1) ^ (lane & 7)) << 4), w[4], w[5], w[6], w[7]);
         }
-      } else {
-        __half* o = orow + it.slice * NROWS;
-#pragma unroll 1
-        for (int c = 0; c < it.nrows; c += 16) {
-          uint32_t v[16];
-          tmem_ld16(d_tmem + c, v);
-          tmem_wait_ld();
-          if (live) {
-            uint4 v0, v1;
-            v0.x = pack_h2(__uint_as_float(v[0]), __uint_as_float(v[1]));
-            v0.y = pack_h2(__uint_as_float(v[2]), __uint_as_float(v[3]));
-            v0.z = pack_h2(__uint_as_float(v[4]), __uint_as_float(v[5]));
-            v0.w = pack_h2(__uint_as_float(v[6]), __uint_as_float(v[7]));
-            v1.x = pack_h2(__uint_as_float(v[8]), __uint_as_float(v[9]));
-            v1.y = pack_h2(__uint_as_float(v[10]), __uint_as_float(v[11]));
-            v1.z = pack_h2(__uint_as_float(v[12]), __uint_as_float(v[13]));
-            v1.w = pack_h2(__uint_as_float(v[14]), __uint_as_float(v[15]));
-            *reinterpret_cast<uint4*>(o + c) = v0;
-            *reinterpret_cast<uint4*>(o + c + 8) = v1;
-          }
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int rr = 4 * i + (lane >> 3), cc = lane & 7;
+          const uint4 v = lds128(stg + rr * 128 + ((cc ^ (rr & 7)) << 4));
+          const int t = 32 * q + rr;
+          if (t < it.cnt)
+            *reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(it.slot0 + t) * p.out_stride +
+                                      colbase + cb + 8 * cc) = v;
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
