@@ -68,7 +68,9 @@ constexpr int WARP_MMA = WARP_APROD0 + A_WARPS;
 constexpr int NUM_WARPS = WARP_MMA + 1;
 constexpr int NTHREADS = NUM_WARPS * 32;
 constexpr int ITEM_CONSUMERS = DQ_WARPS + EPI_WARPS + A_WARPS + 1;  // + the MMA warp
-static_assert(DQ_WARPS * 32 == 2 * NROWS, "dequant threads = 2 per weight row");
+constexpr int DQ_TPR = DQ_WARPS * 32 / NROWS;  // dequant threads per weight row
+constexpr int DQ_WORDS = BK / 8 / DQ_TPR;       // 32-bit nibble words per thread per stage
+static_assert(DQ_TPR * NROWS == DQ_WARPS * 32 && (DQ_TPR == 1 || DQ_TPR == 2), "dequant threads");
 static_assert(TOKM == 128, "MMA M");
 
 struct Item {
@@ -329,7 +331,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp < DQ_WARPS) {
     // ---------------------------------------------------------------- dequant -> B ring
-    const int row = tid >> 1, kh = tid & 1;  // weight row of the item, half (32 k) of the stage
+    const int row = tid / DQ_TPR, kh = tid % DQ_TPR;  // weight row of the item, part of the stage's k
     const int sw = row & 7;
     const int gstages = p.gs / BK;           // stages per scale group
     uint32_t wst = 0, bst = 0;
@@ -348,7 +350,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const uint32_t zrow = srow + it.nrows * p.ng * 2;
       if (!wait(&ctrl.sz_full[slot], (n / IR) & 1, 64)) break;
       __half2 s2 = __half2half2(__ushort_as_half(0)), s16 = s2, cc = s2, c16 = s2;
-      const uint32_t wrow = smem_u32(w_ring) + row * WROW + kh * 16;
+      const uint32_t wrow = smem_u32(w_ring) + row * WROW + kh * (WROW / DQ_TPR);
       const uint32_t brow = b_ring + (row >> 3) * 1024 + (row & 7) * 128;
       bool ok = true;
       int g = 0, gleft = 0;
@@ -359,7 +361,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           ok = false;
           break;
         }
-        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        uint4 u[DQ_WORDS / 4];
+#pragma unroll
+        for (int j = 0; j < DQ_WORDS / 4; ++j) u[j] = make_uint4(0u, 0u, 0u, 0u);
         if (row_ok) {
           if (gleft == 0) {  // first stage of a scale group
             const uint2 c = make_sz<ZINT>(lds16h(srow + 2 * g), lds16h(zrow + 2 * g));
@@ -369,18 +373,23 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             gleft = gstages;
           }
           --gleft;
-          u = lds128(wrow + ws_ * W_STAGE);
+#pragma unroll
+          for (int j = 0; j < DQ_WORDS / 4; ++j) u[j] = lds128(wrow + ws_ * W_STAGE + 16 * j);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctrl.w_empty[ws_]);  // packed stage consumed
         if (row_ok) {
           const uint32_t dst = brow + bs * B_STAGE;
-          const uint32_t uu[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint32_t w4[4];
-            dequant8<ZINT>(uu[i], s2, s16, cc, c16, w4);
-            sts128(dst + ((((kh << 2) | i) ^ sw) << 4), w4[0], w4[1], w4[2], w4[3]);
+          for (int j = 0; j < DQ_WORDS / 4; ++j) {
+            const uint32_t uu[4] = {u[j].x, u[j].y, u[j].z, u[j].w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t w4[4];
+              dequant8<ZINT>(uu[i], s2, s16, cc, c16, w4);
+              const int chunk = kh * DQ_WORDS + 4 * j + i;  // 16-byte chunk (8 k) of the row
+              sts128(dst + ((chunk ^ sw) << 4), w4[0], w4[1], w4[2], w4[3]);
+            }
           }
         }
         fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
