@@ -1,9 +1,9 @@
 """Generate the golden fixtures in tests/golden/ from the REFERENCE's own code.
 
-Run in a container that has the reference checkout (read-only) at REF (default
-/root/reference) — it is never needed at test time:
+Run where a checkout of the reference repository is available (read-only), passing its path
+(or setting KNX_REFERENCE) — it is never needed at test time:
 
-    python tests/golden/make_golden.py [REF]
+    python tests/golden/make_golden.py REF
 
 The reference's Triton kernels are executed by Triton's CPU interpreter (TRITON_INTERPRET=1),
 its pure-torch functions (quantize_w4, dequant_w4, moe_align) run as they are, and its
@@ -20,7 +20,9 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("KNX_REFERENCE", "")
+if not REF or not os.path.isdir(os.path.join(REF, "kernels")):
+    sys.exit("usage: make_golden.py REFERENCE_CHECKOUT  (or set KNX_REFERENCE)")
 OUT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REF, "kernels"))
 
