@@ -384,19 +384,24 @@ def time_prefill(dev, steps, rank, world):
         return fused_moe_w4_v2.moe_forward(yn, Wf["gu_q"], Wf["gu_s"], Wf["gu_z"], Wf["dn_q"],
                                            Wf["dn_s"], Wf["dn_z"], ids, w, hidden_perm=xp,
                                            int_zeros=False), ids
-    _, ids = step()
+    for _ in range(3):
+        _, ids = step()
     counts = torch.bincount(ids.flatten().long(), minlength=E)
     if world > 1:
         torch.distributed.all_reduce(counts)
         torch.distributed.barrier()
     torch.cuda.synchronize(dev)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(steps):
+    # per-step events (their median shows whether one step stalled) inside the bracketing pair
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    clk = Clocks(dev.index if dev.index is not None else 0) if rank == 0 else None
+    evs[0].record()
+    for i in range(steps):
         step()
-    ev1.record()
+        evs[i + 1].record()
     torch.cuda.synchronize(dev)
-    t = torch.tensor([ev0.elapsed_time(ev1)], device=dev)
+    clocks = clk.stop() if clk is not None else None
+    per_step = sorted(evs[i].elapsed_time(evs[i + 1]) for i in range(steps))
+    t = torch.tensor([evs[0].elapsed_time(evs[-1])], device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     ms = float(t.item()) / steps
@@ -405,6 +410,8 @@ def time_prefill(dev, steps, rank, world):
     tpeak, tkind = tensor_peak()
     tflops = workloads.moe_layer_flops(PREFILL_TOKENS * TOPK) / world / (ms * 1e-3) / 1e12
     return {"tokens_per_s": PREFILL_TOKENS / (ms * 1e-3), "ms_per_step": ms, "steps": steps,
+            "ms_median_step_rank0": per_step[len(per_step) // 2], "ms_max_step_rank0": per_step[-1],
+            "clocks": clocks,
             "tokens": PREFILL_TOKENS, "n_gpus": world,
             "per_gpu_tflops": tflops, "tensor_frac": tflops / tpeak, "tensor_peak_tflops": tpeak,
             "tensor_peak_kind": tkind,
@@ -540,7 +547,7 @@ def main():
                           "kernel_us": kern_ms * 1000.0}), flush=True)
         return
     if args.only == "prefill":
-        print(json.dumps({"only": "prefill", **time_prefill(dev, max(2, args.steps // 4), 0, 1)}),
+        print(json.dumps({"only": "prefill", **time_prefill(dev, max(10, 2 * args.steps), 0, 1)}),
               flush=True)
         return
     if args.only == "stack":
@@ -567,7 +574,7 @@ def main():
     if not dist:
         e2e_ms, h2d, d2h = time_layer_e2e(dev, args.steps, args.warmup)
     samp_step_ms, samp_kern_ms = time_sampler(dev)
-    cfg4 = None if args.no_extra else time_prefill(dev, max(2, args.steps // 4), rank, world)
+    cfg4 = None if args.no_extra else time_prefill(dev, max(10, 2 * args.steps), rank, world)
     cfg3 = None if (args.no_extra or dist) else time_stack(dev)
     if dist:
         torch.distributed.barrier()
