@@ -466,6 +466,34 @@ def time_sampler(dev, reps=1):
 
 
 # --------------------------------------------------------------------------------- CPU arms
+def time_selfcond(dev, reps=20, T=0.6):
+    """The denoising step's self-conditioning copy (bf16 of the processed logits): the sampler
+    pass with the copy written by the pass itself, against the pass alone and against torch's
+    separate cast of the fp32 logits (the reference step's .to(bfloat16), fast_sampler.py:109)."""
+    import fused_sampler_ops
+    import workloads
+    x = workloads.sampler_logits(256, V_SAMPLER, seed=0, device=dev).view(1, 256, V_SAMPLER)
+    prev = torch.zeros(x.shape, dtype=torch.bfloat16, device=dev)
+    fin = torch.zeros(1, dtype=torch.bool, device=dev)
+
+    def t(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        return e0.elapsed_time(e1) * 1000.0 / reps
+    base = t(lambda: fused_sampler_ops.sample_step(x, 1234, T))
+    fused = t(lambda: fused_sampler_ops.sample_step_selfcond(x, 1234, T, prev, fin))
+    cast = t(lambda: x.to(torch.bfloat16))
+    return {"temperature": T, "sample_step_us": base, "sample_step_with_copy_us": fused,
+            "separate_cast_us": cast, "copy_bytes": x.numel() * 2}
+
+
 def cpu_layer_sample(nthreads, expert_stride=16):
     """The reference algorithm on the host (oracle restatement of the reference torch path:
     per-expert F.linear on dequant_w4 weights + tanh-GELU + fixed-order combine), on a bounded
@@ -575,6 +603,7 @@ def main():
         e2e_ms, h2d, d2h = time_layer_e2e(dev, args.steps, args.warmup)
     samp_step_ms, samp_kern_ms = time_sampler(dev)
     cfg4 = None if args.no_extra else time_prefill(dev, max(10, 2 * args.steps), rank, world)
+    selfcond = None if (args.no_extra or rank != 0) else time_selfcond(dev)
     cfg3 = None if (args.no_extra or dist) else time_stack(dev)
     if dist:
         torch.distributed.barrier()
@@ -627,6 +656,7 @@ def main():
         "cpu_baseline": cpu,
         "configs3_stack": cfg3,
         "configs4_prefill": cfg4,
+        "sampler_selfcond": selfcond,
     }
     print(json.dumps(line), flush=True)
 

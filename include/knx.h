@@ -250,6 +250,23 @@ KNX_API int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, floa
                       int64_t seed, float* entropy, int64_t* samp, int64_t* amax,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* knx_sampler_fused plus the denoising step's self-conditioning copy in the same pass over the
+ * logits.  Replaces the end of the reference step (fast_sampler.py:103-109):
+ *   processed = where(finished[:, None, None], self_conditioning_logits, processed)
+ *   self_conditioning_logits = processed.to(bfloat16)
+ * i.e. sc_out[r, :] = (finished && finished[r / canvas_len]) ? sc_prev[r, :] : bf16(x[r, :] / T),
+ * with x / T the IEEE quotient the sampler uses and round-to-nearest-even (NaN -> 0x7FC0).
+ * sc_out, sc_prev: bf16 [rows, V] (sc_prev may be sc_out itself); finished: one byte per canvas
+ * of canvas_len rows (NULL: no canvas has finished; then sc_prev may be NULL).
+ * entropy/samp/amax are bit-identical to knx_sampler_fused's.  With V % 4 == 0 and 8-byte aligned
+ * bf16 buffers the copy is written by the sampling pass itself; otherwise one elementwise launch
+ * follows it. */
+KNX_API int knx_sampler_fused_sc(const float* logits, int64_t rows, int64_t V, float temperature,
+                                 int64_t seed, float* entropy, int64_t* samp, int64_t* amax,
+                                 void* sc_out, const void* sc_prev, const uint8_t* finished,
+                                 int64_t canvas_len, void* workspace, size_t workspace_bytes,
+                                 void* stream);
+
 /* knx_sampler_fused without a workspace argument, for callers that cannot allocate device memory
  * when they sample (FFI hosts without a CUDA allocator, serving loops whose device memory is
  * frozen after warm-up).  No counterpart in the reference: its sampler allocates its outputs and

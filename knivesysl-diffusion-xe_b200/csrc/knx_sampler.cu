@@ -376,11 +376,24 @@ KNX_DEVINL int warp_min_i(int v) {
   return v;
 }
 
+// bf16 bits of v rounded to nearest even; NaN -> 0x7FC0 (torch's float -> bfloat16 conversion)
+KNX_DEVINL uint32_t bf16_bits(float v) {
+  return v != v ? 0x7FC0u : static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
+}
+KNX_DEVINL uint32_t bf16x2_bits(float lo, float hi) { return bf16_bits(lo) | (bf16_bits(hi) << 16); }
+
+// Self-conditioning copy (SC): besides the sampling results the pass writes
+//   sc_out[r, :] = finished[r / canvas_len] ? sc_prev[r, :] : bf16(x[r, :] / T)
+// (x / T the same IEEE quotient the sampler uses), i.e. the reference step's
+// where(finished, previous self-conditioning logits, processed logits).to(bfloat16).
+template <bool SC>
 __global__ void __launch_bounds__(SX_THREADS, 1)
     sampler_stream_kernel(const float* __restrict__ logits, int64_t rows, int V, float temp,
                           float rtemp, int do_div, int64_t seed, int seed_is32, int want_gumbel,
                           int nchunks, Part* __restrict__ parts, uint32_t* __restrict__ row_bound,
-                          int* __restrict__ err) {
+                          int* __restrict__ err, __nv_bfloat16* __restrict__ sc_out,
+                          const __nv_bfloat16* __restrict__ sc_prev,
+                          const uint8_t* __restrict__ finished, int canvas_len) {
   pdl_wait_trigger();
   using namespace sm100;
   extern __shared__ uint8_t sx_raw[];
@@ -489,6 +502,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
       uint32_t k0 = 0, k1 = 0;
       row_key(seed, seed_is32, row, k0, k1);
       if (warp == 0 && lane == 0) *reinterpret_cast<volatile long long*>(&c.cur_row) = row;
+      bool sc_keep = false;  // SC: the row's canvas has finished, copy its previous logits
+      if constexpr (SC) sc_keep = finished != nullptr && finished[row / canvas_len] != 0;
       // entropy state: m (warp-uniform running max), per lane sp = sum of 2^d2 over the lane's
       // elements except the one element that carries the implicit 1, t2 = sum d2 * 2^d2
       float m = -INFINITY, m2 = -INFINITY, sp = 0.f, t2 = 0.f;
@@ -573,6 +588,23 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
             } else {
 #pragma unroll
               for (int i = 0; i < 16; ++i) q[i] = isfinite(q[i]) ? div_rn_by(q[i], temp, rtemp) : q[i] * rtemp;
+            }
+          }
+          if constexpr (SC) {
+            const int64_t rb = row * static_cast<int64_t>(V) + c0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int cl = base + 128 * j + 4 * lane;
+              if (cl < scols) {
+                uint2 o;
+                if (sc_keep) {
+                  o = *reinterpret_cast<const uint2*>(sc_prev + rb + cl);
+                } else {
+                  o.x = bf16x2_bits(q[4 * j], q[4 * j + 1]);
+                  o.y = bf16x2_bits(q[4 * j + 2], q[4 * j + 3]);
+                }
+                __stcs(reinterpret_cast<uint2*>(sc_out + rb + cl), o);
+              }
             }
           }
           float tm = q[0];
@@ -827,10 +859,33 @@ extern "C" size_t knx_sampler_workspace_size(int64_t rows, int64_t V) {
   return knx::sampler_ws_layout(rows, V, nullptr, nullptr, nullptr, nullptr, nullptr);
 }
 
-extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, float temperature,
-                                 int64_t seed, float* entropy, int64_t* samp, int64_t* amax,
-                                 void* workspace, size_t workspace_bytes, void* stream) {
-  using namespace knx;
+namespace knx {
+namespace {
+
+// Self-conditioning copy for the shapes and alignments the stream kernel does not take (same rule
+// and the same quotient: IEEE x / T).
+__global__ void sc_cast_kernel(const float* __restrict__ x, int64_t rows, int64_t V, float temp,
+                               int do_div, __nv_bfloat16* __restrict__ out,
+                               const __nv_bfloat16* __restrict__ prev,
+                               const uint8_t* __restrict__ finished, int64_t canvas_len) {
+  pdl_wait_trigger();
+  const int64_t n = rows * V;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = i / V;
+    if (finished != nullptr && finished[r / canvas_len] != 0) {
+      out[i] = prev[i];
+    } else {
+      const float q = do_div ? __fdiv_rn(x[i], temp) : x[i];
+      out[i] = __ushort_as_bfloat16(static_cast<unsigned short>(bf16_bits(q)));
+    }
+  }
+}
+
+int sampler_run(const float* logits, int64_t rows, int64_t V, float temperature, int64_t seed,
+                float* entropy, int64_t* samp, int64_t* amax, void* workspace,
+                size_t workspace_bytes, cudaStream_t s, __nv_bfloat16* sc_out,
+                const __nv_bfloat16* sc_prev, const uint8_t* finished, int64_t canvas_len) {
   if (rows < 0 || V <= 0 || V > 0x7fffffffLL || rows > (1LL << 31)) return KNX_E_INVALID;
   if (!(temperature > 0.f) || !isfinite(temperature)) return KNX_E_INVALID;
   if (!aligned(logits, 4)) return KNX_E_ALIGN;
@@ -840,7 +895,6 @@ extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, f
   const size_t need = sampler_ws_layout(rows, V, &nch, &ccols, &o_ticket, &o_bound, &o_counter);
   if (workspace == nullptr || workspace_bytes < need) return KNX_E_WORKSPACE;
   if (!aligned(workspace, 256)) return KNX_E_ALIGN;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   // row tickets, per-row Gumbel bounds and the work counter start from zero every call
   if (cudaMemsetAsync(ws + o_ticket, 0, o_counter + 256 - o_ticket, s) != cudaSuccess)
@@ -857,16 +911,21 @@ extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, f
   uint32_t* ticket = reinterpret_cast<uint32_t*>(ws + o_ticket);
   uint32_t* bound = reinterpret_cast<uint32_t*>(ws + o_bound);
   int* counter = reinterpret_cast<int*>(ws + o_counter);
+  // the stream kernel writes the self-conditioning copy itself when both buffers allow 8-byte
+  // stores; otherwise sc_cast_kernel does it after the sampler
+  const bool sc_in_pass = sc_out != nullptr && aligned(sc_out, 8) &&
+                          (sc_prev == nullptr || aligned(sc_prev, 8)) && vec && (ccols % 4) == 0;
   if (vec && (ccols % 4) == 0) {
     // streaming kernel: one persistent CTA per SM, static item assignment
-    static bool attr[64] = {};
+    static bool attr[2][64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!attr[dev & 63]) {
-      if (cudaFuncSetAttribute(sampler_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    auto kern = sc_in_pass ? sampler_stream_kernel<true> : sampler_stream_kernel<false>;
+    if (!attr[sc_in_pass][dev & 63]) {
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                static_cast<int>(SX_SMEM)) != cudaSuccess)
         return KNX_E_DEVICE;
-      attr[dev & 63] = true;
+      attr[sc_in_pass][dev & 63] = true;
     }
     // quarter-row items (the workspace holds rows * nch >= rows * nch_s partials)
     const int nch_s = static_cast<int>((V + SX_CHUNK - 1) / SX_CHUNK);
@@ -874,9 +933,10 @@ extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, f
     const int64_t sms = num_sms();
     const int sgrid = static_cast<int>(sitems < sms ? sitems : sms);
     int* dev_err = counter + 1;  // workspace word next to the counter, zeroed above
-    (void)launch_pdl(sampler_stream_kernel, sgrid, SX_THREADS, SX_SMEM, s, logits, rows,
-                     static_cast<int>(V), temperature, rtemp, do_div, seed, seed_is32, want_g,
-                     nch_s, parts, bound, dev_err);
+    (void)launch_pdl(kern, sgrid, SX_THREADS, SX_SMEM, s, logits, rows, static_cast<int>(V),
+                     temperature, rtemp, do_div, seed, seed_is32, want_g, nch_s, parts, bound,
+                     dev_err, sc_in_pass ? sc_out : nullptr, sc_in_pass ? sc_prev : nullptr,
+                     sc_in_pass ? finished : nullptr, static_cast<int>(canvas_len));
     if (cudaGetLastError() != cudaSuccess) return KNX_E_LAUNCH;
     (void)launch_pdl(row_merge_kernel, static_cast<unsigned>((rows + 127) / 128), 128, 0, s, parts,
                      rows, nch_s, entropy, samp, amax);
@@ -889,7 +949,45 @@ extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, f
                      static_cast<int>(V), temperature, rtemp, do_div, seed, seed_is32, want_g, nch,
                      ccols, parts, ticket, bound, counter, entropy, samp, amax);
   }
+  if (sc_out != nullptr && !sc_in_pass) {
+    if (cudaGetLastError() != cudaSuccess) return KNX_E_LAUNCH;
+    const int64_t n = rows * V;
+    const int64_t blocks = (n + 255) / 256;
+    const int64_t cap = static_cast<int64_t>(num_sms()) * 16;
+    (void)launch_pdl(sc_cast_kernel, static_cast<unsigned>(blocks < cap ? blocks : cap), 256, 0, s,
+                     logits, rows, V, temperature, do_div, sc_out, sc_prev, finished, canvas_len);
+  }
   return launch_status();
+}
+
+}  // namespace
+}  // namespace knx
+
+extern "C" int knx_sampler_fused(const float* logits, int64_t rows, int64_t V, float temperature,
+                                 int64_t seed, float* entropy, int64_t* samp, int64_t* amax,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  return knx::sampler_run(logits, rows, V, temperature, seed, entropy, samp, amax, workspace,
+                          workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, nullptr,
+                          nullptr, 1);
+}
+
+extern "C" int knx_sampler_fused_sc(const float* logits, int64_t rows, int64_t V,
+                                    float temperature, int64_t seed, float* entropy,
+                                    int64_t* samp, int64_t* amax, void* sc_out,
+                                    const void* sc_prev, const uint8_t* finished,
+                                    int64_t canvas_len, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  using namespace knx;
+  if (sc_out == nullptr || !aligned(sc_out, 2)) return sc_out == nullptr ? KNX_E_INVALID : KNX_E_ALIGN;
+  if (finished != nullptr) {
+    if (sc_prev == nullptr || canvas_len < 1 || rows % canvas_len != 0) return KNX_E_INVALID;
+    if (!aligned(sc_prev, 2)) return KNX_E_ALIGN;
+  }
+  if (canvas_len > 0x7fffffffLL) return KNX_E_INVALID;
+  return sampler_run(logits, rows, V, temperature, seed, entropy, samp, amax, workspace,
+                     workspace_bytes, static_cast<cudaStream_t>(stream),
+                     static_cast<__nv_bfloat16*>(sc_out), static_cast<const __nv_bfloat16*>(sc_prev),
+                     finished, canvas_len > 0 ? canvas_len : 1);
 }
 
 extern "C" int knx_accept_stop(const float* entropy, const int64_t* cur, const int64_t* proposal,

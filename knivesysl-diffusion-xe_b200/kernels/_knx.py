@@ -71,6 +71,8 @@ _SIGS = {
     "knx_sampler_workspace_size": (_sz, [_i64, _i64]),
     "knx_sampler_fused": (_i32, [_vp, _i64, _i64, _f32, _i64, _vp, _vp, _vp, _vp, _sz, _vp]),
     "knx_sampler_fused_static": (_i32, [_vp, _i64, _i64, _f32, _i64, _vp, _vp, _vp, _vp]),
+    "knx_sampler_fused_sc": (_i32, [_vp, _i64, _i64, _f32, _i64, _vp, _vp, _vp, _vp, _vp, _vp,
+                                    _i64, _vp, _sz, _vp]),
     "knx_accept_stop": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp, _vp, _vp, _i32, _f32,
                                _vp, _vp]),
     "knx_gather_rows": (_i32, [_vp, _i64, _i64, _vp, _i32, _i64, _vp, _vp]),

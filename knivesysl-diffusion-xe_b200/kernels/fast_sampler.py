@@ -83,8 +83,10 @@ def _denoising_step_parity(self, decoder_forward, current_canvas, argmax_canvas,
                            past_key_values, finished_denoising, cur_step, sampler,
                            logits_processor, diffusion_stopping_criteria, **model_kwargs):
     """The stock step except its sampling block, which is one fused pass (entropy + Gumbel-max +
-    argmax); the seed mixing is the reference's (fast_sampler.py:92)."""
-    from fused_sampler_ops import sample_step
+    argmax); the seed mixing is the reference's (fast_sampler.py:92).  With bf16 embeddings the
+    same pass also writes the next self-conditioning logits, where(finished, previous, processed)
+    in bf16, instead of the step's final where + cast over the logits (fast_sampler.py:103-109)."""
+    from fused_sampler_ops import sample_step, sample_step_selfcond
     step_int = int(cur_step)
     cur_step = torch.tensor(cur_step, device=current_canvas.device, dtype=torch.int32)
     torch.compiler.cudagraph_mark_step_begin()
@@ -96,7 +98,17 @@ def _denoising_step_parity(self, decoder_forward, current_canvas, argmax_canvas,
     processed_logits = logits_processor(input_ids, decoder_outputs.logits, cur_step=cur_step)
     batch_size, canvas_length = current_canvas.shape
     seed = (int(torch.randint(0, 2**31 - 1, (1,)).item()) ^ (step_int * 0x9E3779B1)) & 0x7FFFFFFF
-    ent, samp, amax = sample_step(processed_logits, seed)
+    emb_dtype = self.model.decoder.embed_tokens.weight.dtype
+    fuse_sc = (emb_dtype == torch.bfloat16 and torch.is_tensor(self_conditioning_logits)
+               and self_conditioning_logits.dtype == torch.bfloat16
+               and self_conditioning_logits.shape == processed_logits.shape)
+    if fuse_sc:
+        # finished flags as they are before this step's stopping test, like the reference's where
+        fin = finished_denoising if diffusion_stopping_criteria is not None else None
+        ent, samp, amax, sc_next = sample_step_selfcond(processed_logits, seed, 1.0,
+                                                        self_conditioning_logits, fin)
+    else:
+        ent, samp, amax = sample_step(processed_logits, seed)
     _STATE["key"] = (processed_logits.data_ptr(), processed_logits._version)
     _STATE["entropy"] = ent.view(batch_size, canvas_length)
     denoiser_canvas = samp.view(batch_size, canvas_length)
@@ -113,8 +125,7 @@ def _denoising_step_parity(self, decoder_forward, current_canvas, argmax_canvas,
             processed_logits = torch.where(finished_denoising[:, None, None],
                                            self_conditioning_logits, processed_logits)
         finished_denoising |= diffusion_stopping_criteria(new_argmax_canvas, processed_logits)
-    emb_dtype = self.model.decoder.embed_tokens.weight.dtype
-    self_conditioning_logits = processed_logits.to(emb_dtype)
+    self_conditioning_logits = sc_next if fuse_sc else processed_logits.to(emb_dtype)
     return new_current_canvas, new_argmax_canvas, self_conditioning_logits, finished_denoising
 
 
