@@ -58,3 +58,33 @@ def test_selfcond_rejects_bad_arguments(cuda):
     with pytest.raises(ValueError):  # rows are not whole canvases
         fused_sampler_ops.sample_step_selfcond(x, 1, 1.0, torch.zeros_like(x, dtype=torch.bfloat16),
                                                torch.zeros(3, dtype=torch.bool, device=cuda))
+
+
+def test_denoising_step_glue_writes_selfcond_from_the_pass(cuda):
+    """fast_sampler._denoising_step_parity with stand-ins for the transformers objects (decoder,
+    temperature processor, sampler, stopping test): with bf16 embeddings the returned
+    self-conditioning logits are the reference step's where(finished, previous, processed) cast
+    to bf16, and finished canvases keep their argmax."""
+    from types import SimpleNamespace as NS
+
+    import fast_sampler
+    B, L, V, T = 2, 16, 4096, 0.6
+    g = torch.Generator().manual_seed(7)
+    raw = (torch.randn(B, L, V, generator=g) * 3.0).to(cuda)
+    prev = torch.randn(B, L, V, generator=g).bfloat16().to(cuda)
+    finished = torch.tensor([False, True], device=cuda)
+    owner = NS(model=NS(decoder=NS(embed_tokens=NS(weight=torch.zeros(1, dtype=torch.bfloat16)))))
+    sampler = NS(accept_canvas=lambda cur, den, logits, step: den,
+                 renoise_canvas=lambda acc, step: acc)
+    stop = lambda argmax_canvas, logits: torch.zeros(B, dtype=torch.bool, device=cuda)  # noqa: E731
+    canvas = torch.zeros(B, L, dtype=torch.int64, device=cuda)
+    old_argmax = torch.full((B, L), 7, dtype=torch.int64, device=cuda)
+    _, new_argmax, sc, fin = fast_sampler._denoising_step_parity(
+        owner, lambda **kw: NS(logits=raw), canvas, old_argmax, None, None, prev, None, None,
+        finished.clone(), 3, sampler, lambda ids, logits, cur_step: logits / T, stop)
+    want = torch.where(finished[:, None, None], prev, raw / T).to(torch.bfloat16)
+    assert sc.dtype == torch.bfloat16
+    assert torch.equal(sc.view(torch.int16), want.view(torch.int16))
+    assert torch.equal(new_argmax[1], old_argmax[1])
+    assert torch.equal(new_argmax[0], (raw[0] / T).argmax(-1))
+    assert torch.equal(fin, finished)
