@@ -116,7 +116,18 @@ def _denoising_step_parity(self, decoder_forward, current_canvas, argmax_canvas,
     accepted = sampler.accept_canvas(current_canvas, denoiser_canvas, processed_logits, cur_step)
     accepted = accepted.clone()
     new_current_canvas = sampler.renoise_canvas(accepted, cur_step).clone()
-    if diffusion_stopping_criteria is not None:
+    if diffusion_stopping_criteria is not None and fuse_sc:
+        # No host test of finished.any() (a device sync every step): the two canvas selects run
+        # unconditionally (B x L elements), the self-conditioning copy already holds the where,
+        # and the stopping test reads the processed logits as sampled, so its entropy comes from
+        # the pass's cache.  Its result is OR-ed into `finished`, so what it computes for canvases
+        # that have finished already cannot change the outcome.
+        new_argmax_canvas = torch.where(finished_denoising[:, None], argmax_canvas,
+                                        new_argmax_canvas)
+        new_current_canvas = torch.where(finished_denoising[:, None], current_canvas,
+                                         new_current_canvas)
+        finished_denoising |= diffusion_stopping_criteria(new_argmax_canvas, processed_logits)
+    elif diffusion_stopping_criteria is not None:
         if finished_denoising.any():
             new_argmax_canvas = torch.where(finished_denoising[:, None], argmax_canvas,
                                             new_argmax_canvas)

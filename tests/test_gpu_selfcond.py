@@ -76,15 +76,19 @@ def test_denoising_step_glue_writes_selfcond_from_the_pass(cuda):
     owner = NS(model=NS(decoder=NS(embed_tokens=NS(weight=torch.zeros(1, dtype=torch.bfloat16)))))
     sampler = NS(accept_canvas=lambda cur, den, logits, step: den,
                  renoise_canvas=lambda acc, step: acc)
-    stop = lambda argmax_canvas, logits: torch.zeros(B, dtype=torch.bool, device=cuda)  # noqa: E731
+    def stop(argmax_canvas, logits):  # confident canvases: mean entropy below a threshold
+        return torch.distributions.Categorical(logits=logits.float()).entropy().mean(-1) < 2.0
     canvas = torch.zeros(B, L, dtype=torch.int64, device=cuda)
     old_argmax = torch.full((B, L), 7, dtype=torch.int64, device=cuda)
     _, new_argmax, sc, fin = fast_sampler._denoising_step_parity(
         owner, lambda **kw: NS(logits=raw), canvas, old_argmax, None, None, prev, None, None,
         finished.clone(), 3, sampler, lambda ids, logits, cur_step: logits / T, stop)
-    want = torch.where(finished[:, None, None], prev, raw / T).to(torch.bfloat16)
+    # the stock step: where over the logits, stopping test on them, cast
+    proc = torch.where(finished[:, None, None], prev, raw / T)
+    want = proc.to(torch.bfloat16)
+    fin_want = finished | stop(None, proc)
     assert sc.dtype == torch.bfloat16
     assert torch.equal(sc.view(torch.int16), want.view(torch.int16))
     assert torch.equal(new_argmax[1], old_argmax[1])
     assert torch.equal(new_argmax[0], (raw[0] / T).argmax(-1))
-    assert torch.equal(fin, finished)
+    assert torch.equal(fin, fin_want)
