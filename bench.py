@@ -620,8 +620,8 @@ def main():
     # the kernel roofline is the single-GPU layer's (per-stage events exist only there)
     achieved = gemm1_bytes / (gemm1_ms * 1e-3) / 1e9 if gemm1_ms else None
     engine = os.environ.get("KNX_ENGINE", "auto")
-    if engine == "auto":  # the library's rule: ws up to 36 pairs per expert, tcgen05 above
-        engine = "ws" if T * TOPK // E <= 36 else "tc"
+    if engine == "auto":  # the library's rule on job-wide pairs per expert: ws up to 36, else tc
+        engine = "ws" if T * TOPK * world // E <= 36 else "tc"
     line = {
         "metric": METRIC, "value": value, "unit": "us", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": False,
@@ -630,11 +630,13 @@ def main():
                                "T=256 H=2816 I=704 E=128 top-8, gate_up gs128 / down gs64",
                    "l2": f"{NSETS} rotating weight sets ({NSETS} x 416 MB) > 126 MB L2",
                    "parallelism": (f"expert-parallel x{world} (128/{world} experts per GPU, "
-                                   f"one 256-token canvas per GPU, NCCL all-to-all)"
+                                   f"one 256-token canvas per GPU, device-initiated NVLink "
+                                   f"exchange through symmetric memory)"
                                    if world > 1 else "single GPU"),
                    "touched_experts": touched,
                    "max_tokens_per_expert": int(counts.max())},
         "layer_hbm_gbs": bytes_layer / (ms_step * 1e-3) / 1e9,
+        # each step streams every touched expert once, split over the ranks: per-GPU fraction
         "layer_hbm_frac": bytes_layer / (ms_step * 1e-3) / 1e9 / (peak * world),
         "layer_bytes": bytes_layer,
         "stages_us": {k: v * 1000.0 for k, v in stages.items()},
@@ -642,7 +644,10 @@ def main():
                      "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None,
                      "peak_kind": peak_kind, "traffic": GEMM1_NCU_TRAFFIC.get(engine),
-                     "algorithmic_bytes": gemm1_bytes},
+                     "algorithmic_bytes": gemm1_bytes,
+                     **({} if achieved else {"note": "per-kernel events are taken on the "
+                                                     "single-GPU layer only; layer_hbm_frac is "
+                                                     "the per-GPU fraction of this run"})},
         "sampler_step_us": samp_step_ms * 1000.0,
         "sampler_roofline": {"kernel": "sampler_stream_kernel + row_merge_kernel", "bound": "hbm",
                              "achieved": 256 * V_SAMPLER * 4 / (samp_kern_ms * 1e-3) / 1e9,
