@@ -72,6 +72,7 @@ constexpr int DQ_TPR = DQ_WARPS * 32 / NROWS;  // dequant threads per weight row
 constexpr int DQ_WORDS = BK / 8 / DQ_TPR;       // 32-bit nibble words per thread per stage
 static_assert(DQ_TPR * NROWS == DQ_WARPS * 32 && (DQ_TPR == 1 || DQ_TPR == 2), "dequant threads");
 static_assert(TOKM == 128, "MMA M");
+static_assert(WARP_EPI0 % 4 == 0, "epilogue warp e reads TMEM lane quadrant e % 4");
 
 struct Item {
   int valid, e, cnt, slice;
@@ -125,6 +126,10 @@ KNX_HOST_DEVINL int sz_slot_bytes(int ng) { return 2 * NROWS * ng * 2; }
 inline size_t smem_bytes(int ng) {
   return 1024 + OFF_SZ + static_cast<size_t>(IR) * sz_slot_bytes(ng) + EPI_WARPS * EPI_WARP_BYTES;
 }
+// the largest configuration plus the static control block fits one CTA's 227 KB
+static_assert(1024 + OFF_SZ + IR * 2 * NROWS * SZ_MAX_NG * 2 + EPI_WARPS * EPI_WARP_BYTES + 2048 <=
+                  227 * 1024,
+              "shared memory");
 
 KNX_DEVINL float gelu_tanh(float x) {
   const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
