@@ -42,6 +42,27 @@ __device__ __forceinline__ uint32_t philox_w0(uint32_t c0, uint32_t k0, uint32_t
   return c0;
 }
 
+// philox_w0 for two counters under one key: the same rounds, with the key schedule shared.
+__device__ __forceinline__ void philox_w0_x2(uint32_t a0, uint32_t b0, uint32_t k0, uint32_t k1,
+                                             uint32_t& wa, uint32_t& wb) {
+  uint32_t a1 = 0u, a2 = 0u, a3 = 0u, b1 = 0u, b2 = 0u, b3 = 0u;
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t ha0 = __umulhi(PHILOX_M0, a0), la0 = PHILOX_M0 * a0;
+    const uint32_t ha2 = __umulhi(PHILOX_M1, a2), la2 = PHILOX_M1 * a2;
+    const uint32_t hb0 = __umulhi(PHILOX_M0, b0), lb0 = PHILOX_M0 * b0;
+    const uint32_t hb2 = __umulhi(PHILOX_M1, b2), lb2 = PHILOX_M1 * b2;
+    const uint32_t na0 = ha2 ^ a1 ^ k0, na2 = ha0 ^ a3 ^ k1;
+    const uint32_t nb0 = hb2 ^ b1 ^ k0, nb2 = hb0 ^ b3 ^ k1;
+    a0 = na0; a1 = la2; a2 = na2; a3 = la0;
+    b0 = nb0; b1 = lb2; b2 = nb2; b3 = lb0;
+    k0 += PHILOX_W0;
+    k1 += PHILOX_W1;
+  }
+  wa = a0;
+  wb = b0;
+}
+
 // Triton's uint_to_uniform_float for 32-bit words: reinterpret as int32, fold negatives with
 // -x-1, convert to fp32 (round to nearest) and scale by the largest float below 2^-31.
 __device__ __forceinline__ float uint_to_uniform(uint32_t w) {

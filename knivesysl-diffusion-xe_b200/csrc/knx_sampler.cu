@@ -532,7 +532,19 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
             const int i = i0 + 32 * r + lane;
             qv[r] = i < nbuf ? __uint_as_float(lds32(wq + 4 * i)) : -INFINITY;
             colv[r] = i < nbuf ? static_cast<int>(lds32(wcol + 4 * i)) : 0;
-            wv[r] = qv[r] < thr_now ? 0u : philox_w0(static_cast<uint32_t>(colv[r]), k0, k1);
+          }
+          if constexpr (SX_CHAINS == 2) {
+            if (nbuf - i0 > 32) {  // both chains hold candidates: one pass, key schedule once
+              philox_w0_x2(static_cast<uint32_t>(colv[0]), static_cast<uint32_t>(colv[1]), k0,
+                           k1, wv[0], wv[1]);
+            } else {
+              wv[0] = qv[0] < thr_now ? 0u : philox_w0(static_cast<uint32_t>(colv[0]), k0, k1);
+              wv[1] = 0u;
+            }
+          } else {
+#pragma unroll
+            for (int r = 0; r < SX_CHAINS; ++r)
+              wv[r] = qv[r] < thr_now ? 0u : philox_w0(static_cast<uint32_t>(colv[r]), k0, k1);
           }
 #pragma unroll
           for (int r = 0; r < SX_CHAINS; ++r) {
