@@ -60,3 +60,20 @@ def test_sampler_and_accept_reject_bad_arguments():
     assert lib.knx_sampler_fused(None, 4, 100, 1.0, 1, None, None, None, None, 0, None) == -3
     assert lib.knx_accept_stop(None, None, None, 1, 2048, 0.1, None, None, None, None, 0, 0.0,
                                None, None) == -1
+
+
+def test_sampler_selfcond_rejects_bad_arguments_on_host():
+    """knx_sampler_fused_sc checks its self-conditioning arguments before touching the device
+    (the addresses below are never dereferenced)."""
+    lib = _knx.load()
+    f = lib.knx_sampler_fused_sc
+    sc, prev, fin = 4096, 8192, 12288
+    # no output buffer
+    assert f(None, 4, 100, 1.0, 1, None, None, None, None, None, None, 1, None, 0, None) == -1
+    # finished flags without the previous logits, or rows that are not whole canvases
+    assert f(None, 4, 100, 1.0, 1, None, None, None, sc, None, fin, 2, None, 0, None) == -1
+    assert f(None, 4, 100, 1.0, 1, None, None, None, sc, prev, fin, 3, None, 0, None) == -1
+    # bf16 buffers must be 2-byte aligned
+    assert f(None, 4, 100, 1.0, 1, None, None, None, sc + 1, None, None, 1, None, 0, None) == -2
+    # valid arguments reach the workspace check, which fails without touching the device
+    assert f(None, 4, 100, 1.0, 1, None, None, None, sc, prev, fin, 2, None, 0, None) == -3
