@@ -215,7 +215,10 @@ def test_w4a16_linear_vs_reference_golden(cuda, tag):
 
 @pytest.mark.parametrize("engine", ["tc", "ws", "mma"])
 @pytest.mark.parametrize("N,K,M", [(2816, 2816, 256), (1408, 2816, 64), (2816, 704, 64),
-                                   (4096, 2816, 256), (200, 256, 3), (1408, 2816, 130)])
+                                   (4096, 2816, 256), (200, 256, 3), (1408, 2816, 130),
+                                   # 24 scale groups: the tcgen05 engine's largest shared-memory
+                                   # configuration; 25: past it (another engine takes the shape)
+                                   (512, 3072, 256), (192, 3200, 129)])
 def test_w4a16_linear_killtest_shapes(cuda, N, K, M, engine):
     import w4a16
     gs = 128 if K % 128 == 0 else 64
