@@ -24,8 +24,46 @@ extern "C" const char* knx_status_string(int status) {
   }
 }
 
-// ---- stage profiling ------------------------------------------------------------------------
+// ---- per-device launch set-up -----------------------------------------------------------------
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <vector>
+
+namespace knx {
+namespace {
+std::mutex g_setup_mu;
+}
+
+int num_sms() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  static std::map<int, int> cache;
+  std::lock_guard<std::mutex> lk(g_setup_mu);
+  auto it = cache.find(dev);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  cache[dev] = n > 0 ? n : 148;
+  return cache[dev];
+}
+
+int set_max_dyn_smem(const void* func, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KNX_E_DEVICE;
+  static std::map<std::tuple<const void*, int>, int> done;  // (kernel, device) -> bytes set
+  std::lock_guard<std::mutex> lk(g_setup_mu);
+  const auto key = std::make_tuple(func, dev);
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return KNX_OK;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess)
+    return KNX_E_DEVICE;
+  done[key] = bytes;
+  return KNX_OK;
+}
+}  // namespace knx
+
+// ---- stage profiling ------------------------------------------------------------------------
 
 namespace knx {
 namespace prof {

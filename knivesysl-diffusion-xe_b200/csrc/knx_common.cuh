@@ -19,6 +19,8 @@ namespace knx {
 
 // Number of SMs on the current device (cached per device id; B200 = 148).
 int num_sms();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device); thread-safe.
+int set_max_dyn_smem(const void* func, int bytes);
 
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

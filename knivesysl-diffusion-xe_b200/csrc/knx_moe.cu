@@ -21,18 +21,6 @@
 
 namespace knx {
 
-int num_sms() {
-  static int cache[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (cache[dev & 63] == 0) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cache[dev & 63] = n > 0 ? n : 148;
-  }
-  return cache[dev & 63];
-}
-
 namespace {
 
 constexpr int THREADS = 256;
@@ -540,24 +528,12 @@ MoeWs carve_moe_ws(uint8_t* base, int64_t T, int64_t H, int64_t I, int E, int to
 }
 
 bool set_smem_attrs() {
-  static bool done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!done[dev & 63]) {
-    const int m1 = static_cast<int>(g1_smem(SZ_MAX_GROUPS));
-    const int m2 = static_cast<int>(g2_smem(SZ_MAX_GROUPS));
-    if (cudaFuncSetAttribute(gateup_gelu_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             m1) != cudaSuccess ||
-        cudaFuncSetAttribute(gateup_gelu_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             m1) != cudaSuccess ||
-        cudaFuncSetAttribute(rows_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             m2) != cudaSuccess ||
-        cudaFuncSetAttribute(rows_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             m2) != cudaSuccess)
-      return false;
-    done[dev & 63] = true;
-  }
-  return true;
+  const int m1 = static_cast<int>(g1_smem(SZ_MAX_GROUPS));
+  const int m2 = static_cast<int>(g2_smem(SZ_MAX_GROUPS));
+  return set_max_dyn_smem(reinterpret_cast<const void*>(gateup_gelu_kernel<true>), m1) == KNX_OK &&
+         set_max_dyn_smem(reinterpret_cast<const void*>(gateup_gelu_kernel<false>), m1) == KNX_OK &&
+         set_max_dyn_smem(reinterpret_cast<const void*>(rows_gemm_kernel<true>), m2) == KNX_OK &&
+         set_max_dyn_smem(reinterpret_cast<const void*>(rows_gemm_kernel<false>), m2) == KNX_OK;
 }
 
 }  // namespace
@@ -598,12 +574,12 @@ int run_moe_gemms(const GemmArgs& a, int eng, int pc, cudaStream_t s) {
   }
   if (eng == KNX_W4_WARP_WS) {
     st = launch_hw_gateup(a.xp, a.sorted_pair, a.topk, a.offsets, a.tasks, a.ntasks, a.counters,
-                          a.gu_q, a.gu_s, a.gu_z, a.E, H, I, ng1, a.gs_gu, a.zint, a.out2,
+                          a.gu_q, a.gu_s, a.gu_z, a.E, H, I, ng1, a.gs_gu, a.dq, a.out2,
                           max_tasks, a.err, s);
     if (st != KNX_OK) return st;
     prof::mark(pc, 2, s);
     return launch_hw_rows(a.out2, I, I, a.offsets, a.tasks, a.ntasks, 0, a.counters + 1, a.dn_q,
-                          a.dn_s, a.dn_z, a.E, H, ng2, a.gs_dn, a.zint, a.out3, H, max_tasks,
+                          a.dn_s, a.dn_z, a.E, H, ng2, a.gs_dn, a.dq, a.out3, H, max_tasks,
                           a.err, s);
   }
   if (!set_smem_attrs()) return KNX_E_DEVICE;
@@ -720,6 +696,7 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
   ga.gu_q = gu_q; ga.gu_s = static_cast<const __half*>(gu_s); ga.gu_z = static_cast<const __half*>(gu_z);
   ga.dn_q = dn_q; ga.dn_s = static_cast<const __half*>(dn_s); ga.dn_z = static_cast<const __half*>(dn_z);
   ga.E = E; ga.H = H; ga.I = I; ga.gs_gu = gs_gu; ga.gs_dn = gs_dn; ga.zint = zint;
+  ga.dq = dequant_mode(flags);
   ga.out2 = w.out2; ga.out3 = w.out3; ga.pairs = T * topk; ga.err = err;
   st = run_moe_gemms(ga, eng, pc, s);
   if (st != KNX_OK) return st;
@@ -762,8 +739,9 @@ extern "C" int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, 
     if (cudaMemsetAsync(counter, 0, sizeof(int), st) != cudaSuccess) return KNX_E_LAUNCH;
     return launch_hw_rows(xp, K, static_cast<int>(K), nullptr, nullptr, nullptr,
                           static_cast<int>(M), counter, q, static_cast<const __half*>(s),
-                          static_cast<const __half*>(z), 1, static_cast<int>(N), ng, gs, zint,
-                          static_cast<__half*>(Y), N, (M + HW_TASK_TOKENS - 1) / HW_TASK_TOKENS,
+                          static_cast<const __half*>(z), 1, static_cast<int>(N), ng, gs,
+                          dequant_mode(flags), static_cast<__half*>(Y), N,
+                          (M + HW_TASK_TOKENS - 1) / HW_TASK_TOKENS,
                           nullptr, st);
   }
   if (eng != KNX_W4_WARP_MMA && tc_supported(K, gs, ng, N, false)) {

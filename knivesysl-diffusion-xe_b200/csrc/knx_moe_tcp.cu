@@ -583,16 +583,9 @@ int launch_tcp(const tcp::Params& p, const uint8_t* wq, int64_t total_rows, int6
   // the scale / zero bulk copies need 16-byte aligned bases
   if ((reinterpret_cast<uintptr_t>(p.ws) & 15) || (reinterpret_cast<uintptr_t>(p.wz) & 15))
     return KNX_E_ALIGN;
-  static bool attr[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
-    if (cudaFuncSetAttribute(tcp::tcp_gemm_kernel<GATED, ZINT>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(tcp::smem_bytes(tcp::SZ_MAX_NG))) != cudaSuccess)
-      return KNX_E_DEVICE;
-    attr[dev & 63] = true;
-  }
+  if (set_max_dyn_smem(reinterpret_cast<const void*>(tcp::tcp_gemm_kernel<GATED, ZINT>),
+                       static_cast<int>(tcp::smem_bytes(tcp::SZ_MAX_NG))) != KNX_OK)
+    return KNX_E_DEVICE;
   CUtensorMap map;
   if (!encode_weight_map(&map, wq, total_rows, row_bytes)) return KNX_E_DEVICE;
   const int sms = num_sms();

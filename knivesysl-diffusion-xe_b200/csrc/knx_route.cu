@@ -605,13 +605,8 @@ int launch_align(const void* ids, int ids_dtype, int T, int topk, int E, int blo
   const int N = T * topk;
   if (tasks && (m_max < 1 || m_max > MAX_TASK_TOKENS)) return KNX_E_UNSUPPORTED;  // one warp scan
   const size_t smem = align_smem_bytes(N, E, m_max);
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    cudaFuncSetAttribute(align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    attr_set[dev & 63] = true;
-  }
+  if (set_max_dyn_smem(reinterpret_cast<const void*>(align_kernel), 200 * 1024) != KNX_OK)
+    return KNX_E_DEVICE;
   (void)launch_pdl(align_kernel, 1, AL_THREADS, smem, stream, ids, ids_dtype, T, topk, E, block_m,
                    m_max, counts, offsets, sorted_pair, inv, sorted_rows, expert_ids, padded_inv,
                    tasks, ntasks, work_counters, n_work_counters, err);
@@ -688,15 +683,9 @@ extern "C" int knx_router_topk(const void* x, const void* wr, const float* bias,
   const dim3 g1(static_cast<unsigned>((T + RT_TOK - 1) / RT_TOK), E / RT_EXP, RT_KSPLIT);
   const int nchunk = static_cast<int>(H / RT_KSPLIT / RT_BK);
   const size_t smem = static_cast<size_t>(nchunk < RT_RING ? nchunk : RT_RING) * RT_CHUNK_BYTES;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    if (cudaFuncSetAttribute(router_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             RT_RING * RT_CHUNK_BYTES) != cudaSuccess)
-      return KNX_E_DEVICE;
-    attr_set[dev & 63] = true;
-  }
+  if (set_max_dyn_smem(reinterpret_cast<const void*>(router_logits_kernel),
+                       RT_RING * RT_CHUNK_BYTES) != KNX_OK)
+    return KNX_E_DEVICE;
   (void)launch_pdl(router_logits_kernel, g1, 128, smem, s, static_cast<const __half*>(x),
                    static_cast<const __half*>(wr), static_cast<int>(T), static_cast<int>(H), E,
                    part);

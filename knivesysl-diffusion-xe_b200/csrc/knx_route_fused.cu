@@ -198,15 +198,9 @@ extern "C" int knx_rmsnorm_router_topk(const void* x, const void* norm_w, float 
     return KNX_E_ALIGN;
   if (T == 0) return KNX_OK;
   const int nchunk = static_cast<int>(H / RF_KSPLIT / RF_BK);
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    if (cudaFuncSetAttribute(route_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(rf_smem_bytes(RF_MAX_CHUNKS))) != cudaSuccess)
-      return KNX_E_DEVICE;
-    attr_set[dev & 63] = true;
-  }
+  if (set_max_dyn_smem(reinterpret_cast<const void*>(route_fused_kernel),
+                       static_cast<int>(rf_smem_bytes(RF_MAX_CHUNKS))) != KNX_OK)
+    return KNX_E_DEVICE;
   const int neb = E / RF_EXP;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((T + RF_TOK - 1) / RF_TOK), neb, RF_KSPLIT);

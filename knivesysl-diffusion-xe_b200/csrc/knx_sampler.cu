@@ -929,16 +929,9 @@ int sampler_run(const float* logits, int64_t rows, int64_t V, float temperature,
                           (sc_prev == nullptr || aligned(sc_prev, 8)) && vec && (ccols % 4) == 0;
   if (vec && (ccols % 4) == 0) {
     // streaming kernel: one persistent CTA per SM, static item assignment
-    static bool attr[2][64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
     auto kern = sc_in_pass ? sampler_stream_kernel<true> : sampler_stream_kernel<false>;
-    if (!attr[sc_in_pass][dev & 63]) {
-      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(SX_SMEM)) != cudaSuccess)
-        return KNX_E_DEVICE;
-      attr[sc_in_pass][dev & 63] = true;
-    }
+    if (set_max_dyn_smem(reinterpret_cast<const void*>(kern), static_cast<int>(SX_SMEM)) != KNX_OK)
+      return KNX_E_DEVICE;
     // quarter-row items (the workspace holds rows * nch >= rows * nch_s partials)
     const int nch_s = static_cast<int>((V + SX_CHUNK - 1) / SX_CHUNK);
     const int64_t sitems = rows * nch_s;

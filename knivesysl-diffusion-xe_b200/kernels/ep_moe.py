@@ -103,7 +103,7 @@ class ExpertParallelMoE:
     (contiguous slices of the full [E_total, ...] tensors)."""
 
     def __init__(self, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=None, ops=None,
-                 engine=None, int_zeros=None):
+                 engine=None, int_zeros=None, exact=None):
         self.weights = (gu_q, gu_s, gu_z, dn_q, dn_s, dn_z)
         self.E = E_total
         self.group = group
@@ -117,7 +117,7 @@ class ExpertParallelMoE:
             flags = zero_flags(gu_z, dn_z) if gu_z.is_cuda else 0
         else:
             flags = KNX_W4_INT_ZEROS if int_zeros else 0
-        self.flags = flags | engine_flags(engine)
+        self.flags = flags | engine_flags(engine, exact)
 
     @torch.no_grad()
     def forward(self, x, topk_ids, topk_w, out_dtype=torch.float16, tokens_per_expert=None):
@@ -237,9 +237,9 @@ class P2PExpertParallelMoE(ExpertParallelMoE):
     The output is bit-identical to ExpertParallelMoE and to the single-GPU layer."""
 
     def __init__(self, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=None, engine=None,
-                 int_zeros=None, max_tokens=256, topk=8):
+                 int_zeros=None, max_tokens=256, topk=8, exact=None):
         super().__init__(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=group, ops=CudaOps(),
-                         engine=engine, int_zeros=int_zeros)
+                         engine=engine, int_zeros=int_zeros, exact=exact)
         H = gu_q.shape[2] * 2
         self.ex = _P2PExchange.get(group, E_total, max_tokens * topk, H, gu_q.device)
 

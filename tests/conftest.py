@@ -25,6 +25,15 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100 (B200) GPU and libknx.so")
 
 
+def pytest_terminal_summary(terminalreporter):
+    if not UNSCALED:
+        return
+    tr = terminalreporter
+    tr.section("fp16 comparisons: fraction outside the unscaled 2e-3 + 1e-2|ref| bound")
+    for what, n, frac, mx in UNSCALED:
+        tr.write_line(f"{frac * 100:8.4f}%  max|err| {mx:.3e}  n={n:<9d} {what}")
+
+
 def golden(name):
     return dict(np.load(GOLDEN / name))
 
@@ -36,6 +45,11 @@ def cuda():
     return torch.device("cuda:0")
 
 
+# (what, elements, fraction outside the unscaled bound, max |err|) of every fp16 comparison,
+# printed at the end of the session
+UNSCALED = []
+
+
 def assert_close_fp16(out, ref, rtol=1e-2, atol=2e-3, what=""):
     """The north-star fp16 tolerance, |out - ref| <= atol * max(1, rms(ref)) + rtol * |ref|.
 
@@ -43,12 +57,15 @@ def assert_close_fp16(out, ref, rtol=1e-2, atol=2e-3, what=""):
     configs' value distributions the MoE output RMS is ~8, where an f16 ulp is 4e-3-8e-3 and the
     reference's own Triton kernel differs from its torch path by up to 3.1e-2 on near-zero
     outputs (0.59% of elements exceed an unscaled 2e-3; 0 exceed the scaled bound).  For outputs
-    of RMS <= 1 this is exactly allclose(rtol=1e-2, atol=2e-3)."""
+    of RMS <= 1 this is exactly allclose(rtol=1e-2, atol=2e-3).  The fraction of elements outside
+    the unscaled bound (atol + rtol * |ref|) is recorded for every call and reported."""
     o = out.float().cpu()
     r = ref.float().cpu()
     err = (o - r).abs()
     scale = max(1.0, r.pow(2).mean().sqrt().item())
     bound = atol * scale + rtol * r.abs()
     bad = (err > bound).sum().item()
+    unscaled = (err > atol + rtol * r.abs()).float().mean().item() if err.numel() else 0.0
+    UNSCALED.append((what, err.numel(), unscaled, err.max().item() if err.numel() else 0.0))
     assert bad == 0, (f"{what}: {bad}/{err.numel()} elements outside atol={atol}*{scale:.2f} "
                       f"rtol={rtol}; max err {err.max().item():.3e}")

@@ -118,7 +118,7 @@ def test_moe_layer_vs_oracle(cuda, T, E, H, I, tk, skew, engine):
                                     Wd["dn_s"], Wd["dn_z"], ids.to(cuda), w.to(cuda), engine=engine)
     want = ref.moe_layer(hidden, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"], W["dn_z"],
                          ids, w)
-    assert_close_fp16(y, want, what=f"moe T={T} E={E}")
+    assert_close_fp16(y, want, what=f"moe {engine} T={T} E={E} H={H}")
 
 
 def test_moe_engines_agree_and_are_deterministic(cuda):
