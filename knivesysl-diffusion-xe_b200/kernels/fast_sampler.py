@@ -1,173 +1,220 @@
 """fast_sampler.py — DiffusionGemma denoising-step hooks on sm_100a (drop-in for the reference).
 
-install(parity=False) / uninstall() / stats() patch transformers' DiffusionGemma generation
-classes exactly where the reference does (fast_sampler.py:113-143):
-  * EntropyBoundSampler.accept_canvas  -> _accept_canvas  (fast_sampler.py:32-42)
-  * StableAndConfidentStoppingCriteria.__call__ -> _stop_call (fast_sampler.py:45-65)
-  * with parity=True also DiffusionGemmaGenerationMixin._denoising_step -> _denoising_step_parity
-    (fast_sampler.py:68-110), whose sampling block is ONE streaming pass over the processed logits
-    that yields entropy, Gumbel-max sample and argmax together (the reference needs two passes).
-The "bitexact" tier (parity=False) keeps the stock torch entropy chain and only removes the
-duplicate computation through the (data_ptr, _version) cache, like the reference.  The parity
-tier computes entropies, samples and the acceptance mask with the sm_100a kernels.
+Public surface (the reference's, fast_sampler.py:113-143): install(parity=False), uninstall(),
+stats().  install() replaces three methods of transformers' DiffusionGemma generation classes:
+
+  EntropyBoundSampler.accept_canvas             entropy-bound acceptance (fast_sampler.py:32-42)
+  StableAndConfidentStoppingCriteria.__call__   stable-and-confident stop (fast_sampler.py:45-65)
+  DiffusionGemmaGenerationMixin._denoising_step only with parity=True (fast_sampler.py:68-110)
+
+Two tiers, as in the reference:
+  * bit-exact (parity=False): torch's own entropy chain; the stopping test reuses the entropy the
+    acceptance step computed for the same logits tensor instead of recomputing it;
+  * parity (parity=True): the step's sampling is ONE streaming pass over the processed logits
+    (entropy, Gumbel-max sample and argmax together; optionally the bf16 self-conditioning copy),
+    and acceptance runs on the sm_100a kernel.  The Gumbel stream differs from torch's
+    multinomial, hence "parity", not bit-exact, with the stock generation.
+
+The entropy reuse is keyed by the logits tensor's (data_ptr, _version): a tensor that was
+replaced or written in place since misses the cache and is recomputed.
 """
 import torch
 
-_STATE = {}
-_ORIG = {}
-_PARITY = {"on": False}
+
+class _EntropyCache:
+    """The entropy most recently computed (or produced by the sampling pass) for one logits
+    tensor, with hit / miss counters for stats()."""
+
+    def __init__(self):
+        self.reset()
+
+    def reset(self):
+        self.key = None
+        self.value = None
+        self.hits = 0
+        self.misses = 0
+
+    @staticmethod
+    def _key(logits):
+        return (logits.data_ptr(), logits._version)
+
+    def put(self, logits, entropy):
+        self.key = self._key(logits)
+        self.value = entropy
+
+    def get(self, logits):
+        """The cached entropy of `logits` or None, counting the outcome."""
+        if self.key is not None and self.key == self._key(logits):
+            self.hits += 1
+            return self.value
+        self.misses += 1
+        return None
 
 
-def _G():
-    from transformers.models.diffusion_gemma import generation_diffusion_gemma as G
-    return G
+_CACHE = _EntropyCache()
+_TIER = {"parity": False}
+_SAVED = {}  # (class name, attribute) -> the original attribute, while installed
 
 
-def _entropy(logits):
-    if _PARITY["on"]:
+def _generation_module():
+    from transformers.models.diffusion_gemma import generation_diffusion_gemma
+    return generation_diffusion_gemma
+
+
+def _token_entropy(logits):
+    """Per-position entropy of softmax(logits): the fused one-pass kernel in the parity tier,
+    torch's Categorical chain (the stock computation) otherwise."""
+    if _TIER["parity"]:
         from fused_sampler_ops import fused_entropy
         return fused_entropy(logits)
     return torch.distributions.Categorical(logits=logits).entropy()
 
 
-def _cached_entropy(logits):
-    if _STATE.get("key") == (logits.data_ptr(), logits._version):
-        _STATE["hits"] = _STATE.get("hits", 0) + 1
-        return _STATE["entropy"]
-    _STATE["misses"] = _STATE.get("misses", 0) + 1
-    return None
+def _entropy_bound_mask(entropy, bound):
+    """Stock acceptance rule: positions sorted by entropy (ascending); a position is accepted
+    while the entropy accumulated before it stays within `bound`."""
+    h_sorted, order = torch.sort(entropy, dim=-1)
+    before = torch.cumsum(h_sorted, dim=-1) - h_sorted
+    return torch.zeros_like(entropy, dtype=torch.bool).scatter(-1, order, before <= bound)
 
 
 def _accept_canvas(self, current_canvas, denoiser_canvas, logits, cur_step):
-    token_entropy = _cached_entropy(logits) if _PARITY["on"] else None
-    if token_entropy is None:
-        token_entropy = _entropy(logits)
-    _STATE["key"] = (logits.data_ptr(), logits._version)
-    _STATE["entropy"] = token_entropy
-    if _PARITY["on"]:
+    entropy = _CACHE.get(logits) if _TIER["parity"] else None
+    if entropy is None:
+        entropy = _token_entropy(logits)
+    _CACHE.put(logits, entropy)
+    if _TIER["parity"]:
         from accept_ops import accept_canvas
-        mask, out = accept_canvas(token_entropy, current_canvas, denoiser_canvas, self.entropy_bound)
+        mask, accepted = accept_canvas(entropy, current_canvas, denoiser_canvas,
+                                       self.entropy_bound)
         self.accepted_token_mask = mask
-        return out
-    sorted_h, sorted_idx = torch.sort(token_entropy, dim=-1, descending=False)
-    cum = torch.cumsum(sorted_h, dim=-1)
-    sel = cum - sorted_h <= self.entropy_bound
-    self.accepted_token_mask = torch.scatter(input=torch.zeros_like(sel), dim=-1, index=sorted_idx,
-                                             src=sel)
+        return accepted
+    self.accepted_token_mask = _entropy_bound_mask(entropy, self.entropy_bound)
     return torch.where(self.accepted_token_mask, denoiser_canvas, current_canvas)
 
 
+def _stable_over_history(crit, argmax_canvas):
+    """True per canvas when the last `stability_threshold` argmax canvases all equal this one;
+    then this canvas enters the history (oldest dropped).  The history starts filled with -1."""
+    depth = crit.stability_threshold
+    if depth == 0:
+        return torch.ones(argmax_canvas.shape[0], dtype=torch.bool, device=argmax_canvas.device)
+    if crit.argmax_canvas_history is None:
+        crit.argmax_canvas_history = torch.full((depth, *argmax_canvas.shape), -1,
+                                                dtype=argmax_canvas.dtype,
+                                                device=argmax_canvas.device)
+    hist = crit.argmax_canvas_history
+    stable = torch.eq(hist, argmax_canvas.unsqueeze(0)).flatten(2).all(-1).all(0)
+    hist = hist.roll(-1, 0)
+    hist[depth - 1] = argmax_canvas
+    crit.argmax_canvas_history = hist
+    return stable
+
+
 def _stop_call(self, argmax_canvas, logits, **kwargs):
-    if self.stability_threshold == 0:
-        stable = torch.ones((logits.shape[0]), device=logits.device, dtype=torch.bool)
-    else:
-        if self.argmax_canvas_history is None:
-            self.argmax_canvas_history = torch.full(
-                (self.stability_threshold, argmax_canvas.shape[0], argmax_canvas.shape[1]), -1,
-                dtype=argmax_canvas.dtype, device=argmax_canvas.device)
-        stable = (self.argmax_canvas_history == argmax_canvas[None, :, :]).all(dim=-1).all(dim=0)
-        self.argmax_canvas_history = torch.roll(self.argmax_canvas_history, shifts=-1, dims=0)
-        self.argmax_canvas_history[-1] = argmax_canvas
-    if _STATE.get("key") == (logits.data_ptr(), logits._version):
-        token_entropy = _STATE["entropy"]
-        _STATE["hits"] = _STATE.get("hits", 0) + 1
-    else:
-        token_entropy = _entropy(logits)
-        _STATE["misses"] = _STATE.get("misses", 0) + 1
-    confident = torch.mean(token_entropy, dim=-1) < self.confidence_threshold
-    return stable & confident
+    stable = _stable_over_history(self, argmax_canvas)
+    entropy = _CACHE.get(logits)
+    if entropy is None:
+        entropy = _token_entropy(logits)
+    return stable & (entropy.mean(dim=-1) < self.confidence_threshold)
+
+
+def mixed_seed(base, step):
+    """Per-step Gumbel seed (fast_sampler.py:92): `base` (a draw from torch's CPU generator, so
+    seeded runs reproduce) XOR the step index times the golden-ratio constant, kept to 31 bits."""
+    return (int(base) ^ (int(step) * 0x9E3779B1)) & 0x7FFFFFFF
 
 
 def _denoising_step_parity(self, decoder_forward, current_canvas, argmax_canvas, input_ids,
                            decoder_position_ids, self_conditioning_logits, mask_mapping,
                            past_key_values, finished_denoising, cur_step, sampler,
                            logits_processor, diffusion_stopping_criteria, **model_kwargs):
-    """The stock step except its sampling block, which is one fused pass (entropy + Gumbel-max +
-    argmax); the seed mixing is the reference's (fast_sampler.py:92).  With bf16 embeddings the
-    same pass also writes the next self-conditioning logits, where(finished, previous, processed)
-    in bf16, instead of the step's final where + cast over the logits (fast_sampler.py:103-109)."""
+    """The stock step with its sampling block replaced by one fused pass (entropy + Gumbel-max +
+    argmax).  With bf16 embeddings the same pass also writes the next self-conditioning logits,
+    where(finished, previous, processed) in bf16, which the stock step builds with a where and a
+    cast over the logits at its end (fast_sampler.py:103-109)."""
     from fused_sampler_ops import sample_step, sample_step_selfcond
-    step_int = int(cur_step)
+    step_index = int(cur_step)
     cur_step = torch.tensor(cur_step, device=current_canvas.device, dtype=torch.int32)
     torch.compiler.cudagraph_mark_step_begin()
-    decoder_outputs = decoder_forward(decoder_input_ids=current_canvas,
-                                      self_conditioning_logits=self_conditioning_logits,
-                                      decoder_attention_mask=mask_mapping,
-                                      past_key_values=past_key_values,
-                                      decoder_position_ids=decoder_position_ids, **model_kwargs)
-    processed_logits = logits_processor(input_ids, decoder_outputs.logits, cur_step=cur_step)
-    batch_size, canvas_length = current_canvas.shape
-    seed = (int(torch.randint(0, 2**31 - 1, (1,)).item()) ^ (step_int * 0x9E3779B1)) & 0x7FFFFFFF
+    out = decoder_forward(decoder_input_ids=current_canvas,
+                          self_conditioning_logits=self_conditioning_logits,
+                          decoder_attention_mask=mask_mapping, past_key_values=past_key_values,
+                          decoder_position_ids=decoder_position_ids, **model_kwargs)
+    processed = logits_processor(input_ids, out.logits, cur_step=cur_step)
+    B, L = current_canvas.shape
+    seed = mixed_seed(torch.randint(0, 2**31 - 1, (1,)).item(), step_index)
     emb_dtype = self.model.decoder.embed_tokens.weight.dtype
-    fuse_sc = (emb_dtype == torch.bfloat16 and torch.is_tensor(self_conditioning_logits)
-               and self_conditioning_logits.dtype == torch.bfloat16
-               and self_conditioning_logits.shape == processed_logits.shape)
-    if fuse_sc:
-        # finished flags as they are before this step's stopping test, like the reference's where
+    copy_in_pass = (emb_dtype == torch.bfloat16 and torch.is_tensor(self_conditioning_logits)
+                    and self_conditioning_logits.dtype == torch.bfloat16
+                    and self_conditioning_logits.shape == processed.shape)
+    if copy_in_pass:
+        # the finished flags as they stand before this step's stopping test (the stock where)
         fin = finished_denoising if diffusion_stopping_criteria is not None else None
-        ent, samp, amax, sc_next = sample_step_selfcond(processed_logits, seed, 1.0,
-                                                        self_conditioning_logits, fin)
+        entropy, samp, amax, sc_next = sample_step_selfcond(processed, seed, 1.0,
+                                                            self_conditioning_logits, fin)
     else:
-        ent, samp, amax = sample_step(processed_logits, seed)
-    _STATE["key"] = (processed_logits.data_ptr(), processed_logits._version)
-    _STATE["entropy"] = ent.view(batch_size, canvas_length)
-    denoiser_canvas = samp.view(batch_size, canvas_length)
-    new_argmax_canvas = amax.view(batch_size, canvas_length)
-    accepted = sampler.accept_canvas(current_canvas, denoiser_canvas, processed_logits, cur_step)
-    accepted = accepted.clone()
-    new_current_canvas = sampler.renoise_canvas(accepted, cur_step).clone()
-    if diffusion_stopping_criteria is not None and fuse_sc:
-        # No host test of finished.any() (a device sync every step): the two canvas selects run
-        # unconditionally (B x L elements), the self-conditioning copy already holds the where,
-        # and the stopping test reads the processed logits as sampled, so its entropy comes from
-        # the pass's cache.  Its result is OR-ed into `finished`, so what it computes for canvases
-        # that have finished already cannot change the outcome.
-        new_argmax_canvas = torch.where(finished_denoising[:, None], argmax_canvas,
-                                        new_argmax_canvas)
-        new_current_canvas = torch.where(finished_denoising[:, None], current_canvas,
-                                         new_current_canvas)
-        finished_denoising |= diffusion_stopping_criteria(new_argmax_canvas, processed_logits)
-    elif diffusion_stopping_criteria is not None:
-        if finished_denoising.any():
-            new_argmax_canvas = torch.where(finished_denoising[:, None], argmax_canvas,
-                                            new_argmax_canvas)
-            new_current_canvas = torch.where(finished_denoising[:, None], current_canvas,
-                                             new_current_canvas)
-            processed_logits = torch.where(finished_denoising[:, None, None],
-                                           self_conditioning_logits, processed_logits)
-        finished_denoising |= diffusion_stopping_criteria(new_argmax_canvas, processed_logits)
-    self_conditioning_logits = sc_next if fuse_sc else processed_logits.to(emb_dtype)
-    return new_current_canvas, new_argmax_canvas, self_conditioning_logits, finished_denoising
+        entropy, samp, amax = sample_step(processed, seed)
+    _CACHE.put(processed, entropy.view(B, L))
+    proposal, new_argmax = samp.view(B, L), amax.view(B, L)
+    accepted = sampler.accept_canvas(current_canvas, proposal, processed, cur_step).clone()
+    new_canvas = sampler.renoise_canvas(accepted, cur_step).clone()
+    if diffusion_stopping_criteria is not None:
+        if copy_in_pass:
+            # No finished.any() on the host (a device sync per step): the two B x L selects run
+            # unconditionally, the copy above already holds the logits select, and the stopping
+            # test sees the logits as sampled (a cache hit).  Its verdict is OR-ed into
+            # `finished`, so what it says about canvases already finished changes nothing.
+            keep = finished_denoising[:, None]
+            new_argmax = torch.where(keep, argmax_canvas, new_argmax)
+            new_canvas = torch.where(keep, current_canvas, new_canvas)
+        elif finished_denoising.any():
+            keep = finished_denoising[:, None]
+            new_argmax = torch.where(keep, argmax_canvas, new_argmax)
+            new_canvas = torch.where(keep, current_canvas, new_canvas)
+            processed = torch.where(keep[..., None], self_conditioning_logits, processed)
+        finished_denoising |= diffusion_stopping_criteria(new_argmax, processed)
+    next_sc = sc_next if copy_in_pass else processed.to(emb_dtype)
+    return new_canvas, new_argmax, next_sc, finished_denoising
+
+
+# (class, attribute, replacement, parity tier only)
+_HOOKS = (("EntropyBoundSampler", "accept_canvas", _accept_canvas, False),
+          ("StableAndConfidentStoppingCriteria", "__call__", _stop_call, False),
+          ("DiffusionGemmaGenerationMixin", "_denoising_step", _denoising_step_parity, True))
 
 
 def install(parity=False):
-    if _ORIG:
-        if bool(parity) != _PARITY["on"]:
-            raise RuntimeError(f"fast_sampler already installed with parity={_PARITY['on']}; "
-                               f"call uninstall() before install(parity={bool(parity)})")
+    """Patch the generation classes.  Installing again with the same tier is a no-op; with the
+    other tier it raises RuntimeError (uninstall() first), so a tier is never changed silently."""
+    parity = bool(parity)
+    if _SAVED:
+        if parity != _TIER["parity"]:
+            raise RuntimeError(f"fast_sampler is installed with parity={_TIER['parity']}; "
+                               f"uninstall() it before install(parity={parity})")
         return
-    G = _G()
-    _PARITY["on"] = bool(parity)
-    _ORIG["accept"] = G.EntropyBoundSampler.accept_canvas
-    _ORIG["stop"] = G.StableAndConfidentStoppingCriteria.__call__
-    G.EntropyBoundSampler.accept_canvas = _accept_canvas
-    G.StableAndConfidentStoppingCriteria.__call__ = _stop_call
-    if parity:
-        _ORIG["step"] = G.DiffusionGemmaGenerationMixin._denoising_step
-        G.DiffusionGemmaGenerationMixin._denoising_step = _denoising_step_parity
-    _STATE.clear()
+    gen = _generation_module()
+    for cls_name, attr, fn, parity_only in _HOOKS:
+        if parity_only and not parity:
+            continue
+        cls = getattr(gen, cls_name)
+        _SAVED[(cls_name, attr)] = getattr(cls, attr)
+        setattr(cls, attr, fn)
+    _TIER["parity"] = parity
+    _CACHE.reset()
 
 
 def uninstall():
-    if not _ORIG:
+    """Restore every patched method (no-op when not installed)."""
+    if not _SAVED:
         return
-    G = _G()
-    G.EntropyBoundSampler.accept_canvas = _ORIG.pop("accept")
-    G.StableAndConfidentStoppingCriteria.__call__ = _ORIG.pop("stop")
-    if "step" in _ORIG:
-        G.DiffusionGemmaGenerationMixin._denoising_step = _ORIG.pop("step")
-    _PARITY["on"] = False
+    gen = _generation_module()
+    for (cls_name, attr), orig in list(_SAVED.items()):
+        setattr(getattr(gen, cls_name), attr, orig)
+    _SAVED.clear()
+    _TIER["parity"] = False
 
 
 def stats():
-    return {k: _STATE.get(k, 0) for k in ("hits", "misses")}
+    """Entropy reuse counters since install(): {"hits": n, "misses": m}."""
+    return {"hits": _CACHE.hits, "misses": _CACHE.misses}

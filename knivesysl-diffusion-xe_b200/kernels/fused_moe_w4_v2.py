@@ -30,24 +30,36 @@ _TANH_GELU_NAMES = ("gelu_pytorch_tanh", "gelu_new", "gelu_tanh", "quick_gelu_ta
 
 
 def hidden_device(exp):
-    for b in ("gu_s", "gu_q"):
-        t = getattr(exp, b, None)
-        if t is not None:
-            return t.device
-    return "cpu"
+    """Device of the module's packed buffers (scales first), CPU when it has none."""
+    t = next((getattr(exp, b) for b in ("gu_s", "gu_q") if getattr(exp, b, None) is not None),
+             None)
+    return t.device if t is not None else "cpu"
+
+
+def _act_name(fn):
+    return None if fn is None else (getattr(fn, "__name__", None) or type(fn).__name__)
+
+
+def _is_tanh_gelu(fn, device):
+    """By name (any name containing "gelu" passes, as in the reference), else by value on four
+    probe points against 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))."""
+    name = _act_name(fn)
+    if name in _TANH_GELU_NAMES or "gelu" in str(name).lower():
+        return True
+    if fn is None:
+        return False
+    x = torch.tensor([-1.0, 0.0, 0.5, 2.0], device=device)
+    want = 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x.pow(3))))
+    return bool(torch.allclose(fn(x).float(), want, atol=1e-3))
 
 
 def _check_act(exp):
-    """The gate_up epilogue is tanh-GELU; refuse a module whose act_fn is something else
-    (fused_moe_w4_v2.py:291-308)."""
+    """The gate_up epilogue computes tanh-GELU; a module whose act_fn is something else (or
+    missing) is refused once, with AssertionError (fused_moe_w4_v2.py:291-308)."""
     fn = getattr(exp, "act_fn", None)
-    name = (getattr(fn, "__name__", None) or type(fn).__name__) if fn is not None else None
-    ok = fn is None or name in _TANH_GELU_NAMES or "gelu" in str(name).lower()
-    if not ok:
-        x = torch.tensor([-1.0, 0.0, 0.5, 2.0], dtype=torch.float32, device=hidden_device(exp))
-        ref = 0.5 * x * (1.0 + torch.tanh(0.7978845608028654 * (x + 0.044715 * x ** 3)))
-        ok = torch.allclose(fn(x).float(), ref, atol=1e-3)
-    assert ok, (f"fused_moe_w4_v2 hardcodes tanh-GELU but this module's act_fn is {name!r}")
+    if not _is_tanh_gelu(fn, hidden_device(exp)):
+        raise AssertionError(f"fused_moe_w4_v2 computes tanh-GELU but this module's act_fn is "
+                             f"{_act_name(fn)!r}")
     exp._act_checked = True
     return True
 
@@ -74,8 +86,9 @@ def preshuffle_T_dn(qpacked, BK=64):
 
 
 def enable_ns_down(exp):
-    """No-op on sm_100a: the down GEMM streams the standard pack at full bandwidth, so the
-    preshuffled layout is not used (returns exp unchanged, dn_ns stays False)."""
+    """No-op on sm_100a, kept for API parity: the down GEMM reads the standard pack (its limit
+    is instruction issue, not the layout's access pattern), so the preshuffled layout is not
+    installed (returns exp unchanged, dn_ns stays False)."""
     exp.dn_ns = False
     return exp
 

@@ -125,3 +125,38 @@ def test_expert_parallel_matches_single_process(world):
         mp.spawn(_worker, args=(world, _free_port(), d), nprocs=world, join=True)
         got = torch.cat([torch.load(os.path.join(d, f"y{r}.pt")) for r in range(world)])
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
+
+
+def _straggler_worker(rank, world, port, out_dir):
+    """Rank 1 joins the process group but never enters the layer's collectives; rank 0 must get
+    an error from its first exchange once the group's timeout passes, not hang."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        time.sleep(12)            # longer than the timeout, then leave without a collective
+        return
+    import ep_moe
+    W, hidden, ids, w = _data()
+    local = ep_moe.shard_experts(W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"],
+                                 W["dn_z"], rank, world)
+    layer = ep_moe.ExpertParallelMoE(*local, E_total=E, ops=RefOps(), int_zeros=False)
+    t0 = time.monotonic()
+    outcome = "returned"
+    try:
+        layer(hidden[:T // 2], ids[:T // 2], w[:T // 2], out_dtype=torch.float16)
+    except Exception as exc:  # gloo reports the timeout as a RuntimeError subclass
+        outcome = type(exc).__name__
+    with open(os.path.join(out_dir, "rank0.txt"), "w") as f:
+        f.write(f"{outcome} {time.monotonic() - t0:.1f}")
+
+
+def test_rank_that_never_joins_is_reported_on_the_host():
+    with tempfile.TemporaryDirectory() as d:
+        mp.spawn(_straggler_worker, args=(2, _free_port(), d), nprocs=2, join=True)
+        outcome, secs = open(os.path.join(d, "rank0.txt")).read().split()
+    assert outcome != "returned"
+    assert float(secs) < 11.0      # ended by the 3 s group timeout, before the straggler left
