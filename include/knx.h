@@ -62,15 +62,6 @@ extern "C" {
 #define KNX_W4_WARP_MMA 0x2  /* the plain mma.sync kernels (A/B runs) */
 #define KNX_W4_WARP_WS 0x8   /* the warp-specialised mma.sync kernels (TMA-fed, 16 math warps) */
 #define KNX_W4_TCGEN05 0x10  /* the tcgen05 kernels (128 tokens x 256 weight rows per MMA) */
-/* Dequantisation arithmetic of the warp-specialised kernels.  By default (scale groups of 32 to
- * 128) they multiply the exact nibble values q in the MMA, scale each group's fp32 sum by s, and
- * subtract the zero-point term sum_g s_g z_g sum_{k in g} x_k once per output: the W4 arithmetic
- * without rounding any weight to f16 (9 instructions per 8 nibbles instead of 13-17), within the
- * fp16 tolerance of the exact forms, deterministic, but rounded differently from them.  That term
- * carries 16 s z and (group sums of x) / 16 as f16 pairs, so both must stay below 65504.  With
- * KNX_W4_EXACT_DEQUANT (and for larger groups) these kernels use the exact forms described at
- * knx_moe_w4, as the tcgen05 and plain mma.sync kernels always do. */
-#define KNX_W4_EXACT_DEQUANT 0x20
 
 KNX_API int knx_version(void);
 /* 1 when the current device is a compute-capability 10.0 part (the only target). */

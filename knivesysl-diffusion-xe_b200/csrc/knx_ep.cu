@@ -192,7 +192,6 @@ extern "C" int knx_moe_w4_grouped(const void* xrows, const int32_t* rows, int64_
   ga.gu_q = gu_q; ga.gu_s = static_cast<const __half*>(gu_s); ga.gu_z = static_cast<const __half*>(gu_z);
   ga.dn_q = dn_q; ga.dn_s = static_cast<const __half*>(dn_s); ga.dn_z = static_cast<const __half*>(dn_z);
   ga.E = E; ga.H = H; ga.I = I; ga.gs_gu = gs_gu; ga.gs_dn = gs_dn; ga.zint = zint;
-  ga.dq = dequant_mode(flags);
   ga.out2 = w.out2; ga.out3 = static_cast<__half*>(out3); ga.pairs = R; ga.err = err;
   return run_moe_gemms(ga, eng, -1, s);
 }

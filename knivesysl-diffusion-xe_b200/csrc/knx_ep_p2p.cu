@@ -21,7 +21,10 @@
 //
 // Barriers are epoch counters: a rank stores `epoch` into flag `rank` of every peer (release,
 // system scope) and waits until all its own flags have reached it (acquire).  Epochs only grow,
-// so no flag is ever reset.  Every wait gives up after 2 s and sets KNX_DEV_TIMEOUT.
+// so no flag is ever reset.  Every wait gives up after 2 s and sets KNX_DEV_TIMEOUT.  When the
+// counts barrier gives up, the count matrix may be partial, so the plan is written empty: no
+// expert slot (dest_base < 0: the dispatch stores nothing), no receive rows (the grouped GEMMs and
+// the return do nothing).  The layer's output is then invalid and the error word says so.
 #include "knx_common.cuh"
 #include "knx_internal.cuh"
 #include "knx_sm100.cuh"
@@ -93,9 +96,20 @@ __global__ void __launch_bounds__(256)
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int r = 0; r < world; ++r)
     for (int e = tid; e < E; e += blockDim.x) peer_cnt[r][rank * E + e] = counts[e];
+  __shared__ int met;
   __syncthreads();
-  if (tid == 0) p2p_barrier(peer_flags, rank, world, epoch, err);
+  if (tid == 0) met = p2p_barrier(peer_flags, rank, world, epoch, err) ? 1 : 0;
   __syncthreads();
+  int32_t* dest_base = plan;
+  int32_t* recv_off = dest_base + E;
+  int32_t* seg_start = recv_off + El + 1;
+  int32_t* src_base = seg_start + El * world + 1;
+  if (!met) {  // the empty plan (see the file comment)
+    for (int e = tid; e < E; e += blockDim.x) dest_base[e] = -1;
+    for (int i = tid; i <= El; i += blockDim.x) recv_off[i] = 0;
+    for (int i = tid; i <= El * world; i += blockDim.x) seg_start[i] = 0;
+    return;
+  }
   const int32_t* cnt = peer_cnt[rank];  // [world][E], complete after the barrier
   for (int e = tid; e < E; e += blockDim.x) {
     int a = 0;
@@ -109,10 +123,6 @@ __global__ void __launch_bounds__(256)
     warp_excl_scan(tot_own + warp * El, El, own_off + warp * (El + 1), lane);
   }
   __syncthreads();
-  int32_t* dest_base = plan;
-  int32_t* recv_off = dest_base + E;
-  int32_t* seg_start = recv_off + El + 1;
-  int32_t* src_base = seg_start + El * world + 1;
   for (int e = tid; e < E; e += blockDim.x) {
     const int r = e % world, el = e / world;
     int a = own_off[r * (El + 1) + el];
@@ -148,6 +158,7 @@ __global__ void __launch_bounds__(256)
     if (offsets[mid] <= j) lo = mid; else hi = mid - 1;
   }
   const int e = lo, r = e % (E / El);  // owner: round-robin sharding
+  if (plan[e] < 0) return;             // the counts barrier gave up: empty plan
   const int64_t dst = plan[e] + (j - offsets[e]);
   const uint4* s = xp + static_cast<int64_t>(sorted_pair[j] / topk) * vpr;
   uint4* d = peer_rows[r] + dst * vpr;

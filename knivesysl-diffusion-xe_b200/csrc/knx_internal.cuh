@@ -40,24 +40,16 @@ int launch_tc_rows(const __half* act, int64_t act_stride, int K, const int32_t* 
 
 // warp-specialised mma.sync grouped W4A16 GEMMs (knx_moe_hw.cu), 32 tokens per task
 constexpr int HW_TASK_TOKENS = 32;
-// dequantisation modes of those kernels: exact with fp16 zero-points (the reference kernel's
-// arithmetic), exact with integer zero-points (dequant_w4's), or integer (exact nibble values
-// in the MMA, fp32 scale per group, the zero-point term once per item; scale groups <= 128)
-constexpr int DQ_EXACT_F16 = 0, DQ_EXACT_ZINT = 1, DQ_INTEGER = 2;
-inline int dequant_mode(int flags) {
-  if (!(flags & KNX_W4_EXACT_DEQUANT)) return DQ_INTEGER;
-  return (flags & KNX_W4_INT_ZEROS) ? DQ_EXACT_ZINT : DQ_EXACT_F16;
-}
 constexpr int MIN_TASK_TOKENS = 16;  // smallest task size of any engine (sizes the task list)
 bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated);
 int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, const int32_t* offsets,
                      const int4* tasks, const int32_t* ntasks, int* counter, const uint8_t* gu_q,
                      const __half* gu_s, const __half* gu_z, int E, int H, int I, int ng, int gs,
-                     int dq, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s);
+                     bool zint, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s);
 int launch_hw_rows(const __half* act, int64_t act_stride, int K, const int32_t* offsets,
                    const int4* tasks, const int32_t* ntasks, int dense_rows, int* counter,
                    const uint8_t* wq, const __half* ws, const __half* wz, int E, int N, int ng,
-                   int gs, int dq, __half* out, int64_t out_stride, int64_t max_tasks,
+                   int gs, bool zint, __half* out, int64_t out_stride, int64_t max_tasks,
                    int32_t* err, cudaStream_t s);
 
 // The grouped expert GEMMs of one MoE layer over a task list (knx_moe.cu).
@@ -78,8 +70,7 @@ struct GemmArgs {
   int E;
   int64_t H, I;
   int gs_gu, gs_dn;
-  bool zint;  // integer zero-points (exact engines)
-  int dq;     // dequantisation mode of the warp-specialised engine (DQ_*)
+  bool zint;
   __half* out2;  // [pairs][I] f16 (K-interleaved)
   __half* out3;  // [pairs][H] f16
   int64_t pairs;

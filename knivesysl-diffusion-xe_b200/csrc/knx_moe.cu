@@ -574,12 +574,12 @@ int run_moe_gemms(const GemmArgs& a, int eng, int pc, cudaStream_t s) {
   }
   if (eng == KNX_W4_WARP_WS) {
     st = launch_hw_gateup(a.xp, a.sorted_pair, a.topk, a.offsets, a.tasks, a.ntasks, a.counters,
-                          a.gu_q, a.gu_s, a.gu_z, a.E, H, I, ng1, a.gs_gu, a.dq, a.out2,
+                          a.gu_q, a.gu_s, a.gu_z, a.E, H, I, ng1, a.gs_gu, a.zint, a.out2,
                           max_tasks, a.err, s);
     if (st != KNX_OK) return st;
     prof::mark(pc, 2, s);
     return launch_hw_rows(a.out2, I, I, a.offsets, a.tasks, a.ntasks, 0, a.counters + 1, a.dn_q,
-                          a.dn_s, a.dn_z, a.E, H, ng2, a.gs_dn, a.dq, a.out3, H, max_tasks,
+                          a.dn_s, a.dn_z, a.E, H, ng2, a.gs_dn, a.zint, a.out3, H, max_tasks,
                           a.err, s);
   }
   if (!set_smem_attrs()) return KNX_E_DEVICE;
@@ -696,7 +696,6 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
   ga.gu_q = gu_q; ga.gu_s = static_cast<const __half*>(gu_s); ga.gu_z = static_cast<const __half*>(gu_z);
   ga.dn_q = dn_q; ga.dn_s = static_cast<const __half*>(dn_s); ga.dn_z = static_cast<const __half*>(dn_z);
   ga.E = E; ga.H = H; ga.I = I; ga.gs_gu = gs_gu; ga.gs_dn = gs_dn; ga.zint = zint;
-  ga.dq = dequant_mode(flags);
   ga.out2 = w.out2; ga.out3 = w.out3; ga.pairs = T * topk; ga.err = err;
   st = run_moe_gemms(ga, eng, pc, s);
   if (st != KNX_OK) return st;
@@ -739,9 +738,8 @@ extern "C" int knx_w4a16_linear(const void* X, const uint8_t* q, const void* s, 
     if (cudaMemsetAsync(counter, 0, sizeof(int), st) != cudaSuccess) return KNX_E_LAUNCH;
     return launch_hw_rows(xp, K, static_cast<int>(K), nullptr, nullptr, nullptr,
                           static_cast<int>(M), counter, q, static_cast<const __half*>(s),
-                          static_cast<const __half*>(z), 1, static_cast<int>(N), ng, gs,
-                          dequant_mode(flags), static_cast<__half*>(Y), N,
-                          (M + HW_TASK_TOKENS - 1) / HW_TASK_TOKENS,
+                          static_cast<const __half*>(z), 1, static_cast<int>(N), ng, gs, zint,
+                          static_cast<__half*>(Y), N, (M + HW_TASK_TOKENS - 1) / HW_TASK_TOKENS,
                           nullptr, st);
   }
   if (eng != KNX_W4_WARP_MMA && tc_supported(K, gs, ng, N, false)) {

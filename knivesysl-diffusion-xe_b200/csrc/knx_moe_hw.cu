@@ -15,22 +15,11 @@
 //   * warps 0-15 (math): warp w owns one m16 row tile — gated: gate rows 8w..8w+7 on tile rows
 //     0-7 and the matching up rows on tile rows 8-15, so each lane ends with gate and up of one
 //     intermediate column; plain: rows 16w..16w+15 — over the full K.  Nibbles are dequantised in
-//     registers into A fragments and multiplied with the B fragments of the task's 1-4 n8 token
-//     tiles, so one dequantisation serves up to 32 tokens.  No split-K: every output is one
-//     warp's fixed-order sum (deterministic), and a token's sum does not depend on the other
-//     tokens of its task.  Two dequantisation modes:
-//       - exact (dequant8): A = (q - z) * s rounded to f16 once (integer zero-points,
-//         bit-identical to dequant_w4) or the reference kernel's RN16(RN16(q - z) * s);
-//         13-17 instructions per 8 nibbles;
-//       - integer (dequant8_q, the default for scale groups of 32-128): A = q exactly, 9
-//         instructions per 8 nibbles.  Each scale group accumulates into its own fp32
-//         registers, which are scaled into the output by one FFMA per element, and the
-//         zero-point term sum_g s_g z_g sum_{k in g} x_k is subtracted once per item (see
-//         zero_point_term).  Nothing is rounded to f16 before the accumulators: this is the W4
-//         arithmetic without the weight rounding of the other forms;
-//   * warp 18 (integer mode only): the per-token group sums of the activations, from the same
-//     activation ring, by MMAs with a ones matrix (16 tokens x 16 k per instruction), into a
-//     per-item table the math warps read after their last stage.
+//     registers into A fragments (dequant8: bit-identical to dequant_w4 for integer zero-points,
+//     the reference kernel's f16 arithmetic otherwise) and multiplied with the B fragments of
+//     the task's 1-4 n8 token tiles, so one dequantisation serves up to 32 tokens.  No split-K:
+//     every output is one warp's fixed-order sum (deterministic), and a token's sum does not
+//     depend on the other tokens of its task.
 //   * GELU(gate) * up (gated) or the plain result: each warp stages its own 8 (gated) or 16
 //     output columns per token in a private shared area and writes 16-byte chunks, so the math
 //     warps never wait for one another; the gated output is written in the K-interleave the
@@ -59,16 +48,10 @@ constexpr int W_STAGE = ROWS * WROW;     // 32 KB
 constexpr int AROW = BK * 2 + 64;        // 576 B per token row per stage
 constexpr int A_STAGE = TOK * AROW;      // 18 KB
 constexpr int MATH_WARPS = 16;
-constexpr int WARP_WPROD = MATH_WARPS, WARP_APROD = MATH_WARPS + 1, WARP_SUM = MATH_WARPS + 2;
-constexpr int num_warps(bool iq) { return MATH_WARPS + (iq ? 3 : 2); }
-constexpr int nthreads(bool iq) { return num_warps(iq) * 32; }
+constexpr int NUM_WARPS = MATH_WARPS + 2;
+constexpr int NTHREADS = NUM_WARPS * 32;
+constexpr int WARP_WPROD = MATH_WARPS, WARP_APROD = MATH_WARPS + 1;
 constexpr int SZ_MAX = 32;               // groups per row
-// integer mode: per-item table of each token's group sums, negated and divided by 16, as f16
-// hi and lo parts ([token][group], row stride 40 halves: the B-fragment loads of 8 tokens hit
-// distinct banks)
-constexpr int ASTR = 40;
-constexpr int ASUM_LO = TOK * ASTR * 2;  // byte offset of the lo table
-constexpr int ASUM_SLOT = 2 * ASUM_LO;   // 5 KB per item slot
 // per-warp output staging: 8 (gated) or 16 (plain) columns x 32 tokens of f16 per warp
 constexpr int ot_bytes(bool gated) { return MATH_WARPS * TOK * (gated ? 8 : 16) * 2; }
 constexpr size_t SMEM_LIMIT = 232448;    // 227 KB opt-in per block
@@ -98,7 +81,6 @@ struct Ctrl {
   uint64_t w_full[SW_MAX], w_empty[SW_MAX];
   uint64_t a_full[SA_MAX], a_empty[SA_MAX];
   uint64_t i_full[IR], i_empty[IR];
-  uint64_t s_full[IR];  // integer mode: the item's group-sum table is written
   Item items[IR];
   int abort;
 };
@@ -125,19 +107,19 @@ struct Params {
 };
 
 KNX_HOST_DEVINL size_t sz_slot_bytes(int ng) { return static_cast<size_t>(ROWS) * ng * 4; }
-inline size_t smem_bytes(bool gated, bool iq, int ng, int sw, int sa) {
+inline size_t smem_bytes(bool gated, int ng, int sw, int sa) {
   return 1024 + static_cast<size_t>(sw) * W_STAGE + static_cast<size_t>(sa) * A_STAGE +
-         ot_bytes(gated) + IR * sz_slot_bytes(ng) + (iq ? IR * ASUM_SLOT : 0);
+         ot_bytes(gated) + IR * sz_slot_bytes(ng);
 }
 // Ring depths that fit, in order of preference: at least 3 activation stages (their copies come
 // from L2 but each is gathered token by token), then the deepest weight ring (it streams from
 // HBM; 4 stages = 128 KB in flight).  Measured on the configs[1] gate_up: 3 + 3 beats 4 + 2.
-inline bool ring_depths(bool gated, bool iq, int ng, int& sw, int& sa) {
+inline bool ring_depths(bool gated, int ng, int& sw, int& sa) {
   static const int pref[][2] = {{4, 4}, {4, 3}, {3, 4}, {3, 3}, {4, 2}, {3, 2}, {2, 4}, {2, 3}, {2, 2}};
   for (const auto& c : pref) {
     sw = c[0];
     sa = c[1];
-    if (smem_bytes(gated, iq, ng, sw, sa) + STATIC_RESERVE <= SMEM_LIMIT) return true;
+    if (smem_bytes(gated, ng, sw, sa) + STATIC_RESERVE <= SMEM_LIMIT) return true;
   }
   sw = sa = 0;
   return false;
@@ -163,118 +145,6 @@ KNX_DEVINL void group_consts(__half s, __half z, __half2& s2, __half2& s16, __ha
   s16 = __half2half2(sh);
   c2 = __half2half2(c);
   c16 = __half2half2(ch);
-}
-
-// Integer mode: the 8 nibbles of one u32 as exact f16 values q in the four A-fragment registers
-// of dequant8 (same k order).  Magic-number halves h = 1024 + q (low nibble) give q = h - 1024;
-// h = 1024 + 16 q (high nibble) gives q = h / 16 - 64 in one fused multiply-add; both exact.
-KNX_DEVINL void dequant8_q(uint32_t u, uint32_t (&w)[4]) {
-  const uint32_t MAG = 0x64006400u;
-  const __half2 m1024 = __half2half2(__ushort_as_half(0xe400u));   // -1024
-  const __half2 r16 = __half2half2(__ushort_as_half(0x2c00u));     // 1/16
-  const __half2 m64 = __half2half2(__ushort_as_half(0xd400u));     // -64
-  const uint32_t p0 = lop3_and_or(u, 0x000F000Fu, MAG);
-  const uint32_t p1 = lop3_and_or(u, 0x00F000F0u, MAG);
-  const uint32_t u8 = u >> 8;
-  const uint32_t p2 = lop3_and_or(u8, 0x000F000Fu, MAG);
-  const uint32_t p3 = lop3_and_or(u8, 0x00F000F0u, MAG);
-  w[0] = h2_as_u32(__hadd2(u32_as_h2(p0), m1024));
-  w[1] = h2_as_u32(__hfma2(u32_as_h2(p1), r16, m64));
-  w[2] = h2_as_u32(__hadd2(u32_as_h2(p2), m1024));
-  w[3] = h2_as_u32(__hfma2(u32_as_h2(p3), r16, m64));
-}
-
-// D = A * B (no accumulator input): the first MMA of a scale group.
-KNX_DEVINL void mma_16816_first(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                uint32_t b0, uint32_t b1) {
-  const float z = 0.f;
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%10,%10,%10,%10};\n"
-      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(z));
-}
-
-// 16 s z of groups g0, g0 + 1 of one row as f16x2 hi + lo parts (hi = RN16(16 s z), lo =
-// RN16(16 s z - hi): the fma forms the exact difference); groups >= ng are zero.
-KNX_DEVINL void sz_split(uint32_t s_row, uint32_t z_row, int g0, int ng, uint32_t& hi,
-                         uint32_t& lo) {
-  const __half zero = __ushort_as_half(0);
-  const __half s0 = g0 < ng ? lds16h(s_row + 2 * g0) : zero;
-  const __half s1 = g0 + 1 < ng ? lds16h(s_row + 2 * g0 + 2) : zero;
-  const __half z0 = g0 < ng ? lds16h(z_row + 2 * g0) : zero;
-  const __half z1 = g0 + 1 < ng ? lds16h(z_row + 2 * g0 + 2) : zero;
-  const __half2 s2 = __hmul2(__halves2half2(s0, s1), __half2half2(__ushort_as_half(0x4c00u)));
-  const __half2 z2 = __halves2half2(z0, z1);
-  const __half2 h = __hmul2(s2, z2);
-  hi = h2_as_u32(h);
-  lo = h2_as_u32(__hfma2(s2, z2, __hneg2(h)));
-}
-
-// Integer mode, once per item: acc[t] += sum_g (16 s z)[row][g] * (-asum[token][g] / 16) over
-// the lane's rows (A operand: tile row g = row A, g + 8 = row B; k = the scale group) and token
-// tiles (B operand: the group-sum table), as hi*hi + hi*lo + lo*hi: the products agree with the
-// exact fp32 product of the two unsplit values to ~2^-22.  The scaling by 16 keeps both lo parts
-// normal f16 numbers at the benchmark's value ranges.
-// tab: shared address of the hi table entry of token g, group 2q (tile 0).
-template <int NTT>
-KNX_DEVINL void zero_point_term(uint32_t sA, uint32_t zA, uint32_t sB, uint32_t zB, int ng,
-                                int q, uint32_t tab, float (&acc)[NT][NACC][4]) {
-#pragma unroll 1
-  for (int c = 0; c < ng; c += 16) {
-    uint32_t ph[4], pl[4];
-    sz_split(sA, zA, c + 2 * q, ng, ph[0], pl[0]);
-    sz_split(sB, zB, c + 2 * q, ng, ph[1], pl[1]);
-    sz_split(sA, zA, c + 2 * q + 8, ng, ph[2], pl[2]);
-    sz_split(sB, zB, c + 2 * q + 8, ng, ph[3], pl[3]);
-#pragma unroll
-    for (int t = 0; t < NTT; ++t) {
-      const uint32_t o = tab + static_cast<uint32_t>(t * 8 * ASTR * 2 + c * 2);
-      const uint32_t bh0 = lds32(o), bh1 = lds32(o + 16);
-      const uint32_t bl0 = lds32(o + ASUM_LO), bl1 = lds32(o + ASUM_LO + 16);
-      mma_16816(acc[t][0], ph[0], ph[1], ph[2], ph[3], bh0, bh1);
-      mma_16816(acc[t][0], ph[0], ph[1], ph[2], ph[3], bl0, bl1);
-      mma_16816(acc[t][0], pl[0], pl[1], pl[2], pl[3], bh0, bh1);
-    }
-  }
-}
-
-// Integer mode: one stage (256 k) of one warp's m16 tile, GPJ k32 steps per scale group (1, 2
-// or 4: groups never straddle a stage).  Every group's products accumulate in fresh fp32
-// registers, then acc += s * group sum per element (s of the element's row).
-template <int NTT, int GPJ, bool TAIL, int BOFF>
-KNX_DEVINL void mma_stage_q(uint32_t wa, uint32_t ab, int jmax, int grp0, uint32_t sA,
-                            uint32_t sB, float (&acc)[NT][NACC][4]) {
-  static_assert(GPJ == 1 || GPJ == 2 || GPJ == 4, "integer mode: scale groups of 32-128");
-#pragma unroll 1
-  for (int j0 = 0; j0 < 8; j0 += GPJ) {
-    if (TAIL && j0 >= jmax) break;
-    const int grp = grp0 + j0 / GPJ;
-    const float fsA = __half2float(lds16h(sA + 2 * grp));
-    const float fsB = __half2float(lds16h(sB + 2 * grp));
-    float part[NTT][4];
-#pragma unroll
-    for (int jj = 0; jj < GPJ; ++jj) {
-      const uint32_t aj = wa ^ static_cast<uint32_t>((j0 + jj) << 4);
-      uint32_t fa[4], fb[4];
-      dequant8_q(lds32(aj), fa);
-      dequant8_q(lds32_at<BOFF>(aj), fb);
-#pragma unroll
-      for (int t = 0; t < NTT; ++t) {
-        const uint4 b = lds128(ab + t * 8 * AROW + (j0 + jj) * 64);
-        if (jj == 0) mma_16816_first(part[t], fa[0], fb[0], fa[1], fb[1], b.x, b.y);
-        else mma_16816(part[t], fa[0], fb[0], fa[1], fb[1], b.x, b.y);
-        mma_16816(part[t], fa[2], fb[2], fa[3], fb[3], b.z, b.w);
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < NTT; ++t) {
-      acc[t][0][0] = fmaf(fsA, part[t][0], acc[t][0][0]);
-      acc[t][0][1] = fmaf(fsA, part[t][1], acc[t][0][1]);
-      acc[t][0][2] = fmaf(fsB, part[t][2], acc[t][0][2]);
-      acc[t][0][3] = fmaf(fsB, part[t][3], acc[t][0][3]);
-    }
-  }
 }
 
 // One stage (256 k) of one warp's m16 tile: 8 k32 steps (jmax in the K tail), NTT n8 token
@@ -319,8 +189,8 @@ KNX_DEVINL void mma_stage(uint32_t wa, uint32_t ab, int jmax, int grp0,
   }
 }
 
-template <bool GATED, bool ZINT, bool IQ, int GPJ>
-__global__ void __launch_bounds__(nthreads(IQ), 1)
+template <bool GATED, bool ZINT, int GPJ>
+__global__ void __launch_bounds__(NTHREADS, 1)
     hw_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const Params p) {
   pdl_wait_trigger();
   extern __shared__ uint8_t dsm_raw[];
@@ -334,24 +204,15 @@ __global__ void __launch_bounds__(nthreads(IQ), 1)
   const uint32_t ot = smem_u32(a_ring + sa * A_STAGE);  // output tile (shared address)
   uint8_t* sz_ring = a_ring + sa * A_STAGE + ot_bytes(GATED);
   const size_t szr = sz_slot_bytes(p.ng);
-  uint8_t* asum_ring = sz_ring + IR * szr;  // integer mode only
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nst = (p.K + BK - 1) / BK;
 
-  if (IQ) {
-    // groups >= ng of the sum tables are never written and must read as zero
-    for (int i = tid; i < IR * ASUM_SLOT / 16; i += nthreads(IQ))
-      sts128(smem_u32(asum_ring) + 16u * i, 0u, 0u, 0u, 0u);
-  }
   if (tid == 0) {
-    // the group-sum warp (integer mode) consumes every activation stage and item like a math warp
-    const uint32_t a_cons = MATH_WARPS + (IQ ? 1 : 0);
     for (int s = 0; s < sw; ++s) { mbar_init(&ctrl.w_full[s], 1); mbar_init(&ctrl.w_empty[s], MATH_WARPS); }
-    for (int s = 0; s < sa; ++s) { mbar_init(&ctrl.a_full[s], 1); mbar_init(&ctrl.a_empty[s], a_cons); }
+    for (int s = 0; s < sa; ++s) { mbar_init(&ctrl.a_full[s], 1); mbar_init(&ctrl.a_empty[s], MATH_WARPS); }
     for (int i = 0; i < IR; ++i) {
       mbar_init(&ctrl.i_full[i], 1);
-      mbar_init(&ctrl.i_empty[i], a_cons + 1);
-      mbar_init(&ctrl.s_full[i], 32);
+      mbar_init(&ctrl.i_empty[i], MATH_WARPS + 1);
     }
     ctrl.abort = 0;
     fence_mbar_init();
@@ -497,80 +358,7 @@ __global__ void __launch_bounds__(nthreads(IQ), 1)
       for (uint32_t x = ast > static_cast<uint32_t>(sa) ? ast - sa : 0; x < ast; ++x)
         mbar_wait(&ctrl.a_full[x % sa], (x / sa) & 1);
     __syncwarp();
-  } else if (IQ && warp == WARP_SUM) {
-    // ---------------------------------------------------------------- activation group sums
-    // D[16 tokens x 8] += A[16 tokens x 16 k] * ones: every column of D holds the tokens' sums.
-    // Lane (g, q) feeds tokens g and g + 8 of a 16-token half with the 16 bytes it would load as
-    // a B fragment (4 + 4 k of each), so two MMAs cover a 32-k step.
-    const int g = lane >> 2, q = lane & 3;
-    const uint32_t ones = 0x3C003C00u;  // f16x2 (1, 1)
-    const int k32_per_group = p.gs >> 5;
-    uint32_t asl = 0, aph = 0;
-    for (int n = 0;; ++n) {
-      const int slot = n % IR;
-      const bool got = __all_sync(0xffffffffu, wait(&ctrl.i_full[slot], (n / IR) & 1, 64));
-      const Item it = ctrl.items[slot];
-      if (__any_sync(0xffffffffu, !got || !it.valid || *abort_flag)) {
-        __syncwarp();
-        if (lane == 0 && got) mbar_arrive(&ctrl.i_empty[slot]);
-        break;
-      }
-      const int nhalf = (it.cnt + 15) >> 4;  // 16-token halves of the task
-      // this lane stores part (q & 1: lo, else hi) of token g (q < 2) or g + 8 (q >= 2)
-      const uint32_t dst = smem_u32(asum_ring + slot * ASUM_SLOT) + ((q & 1) ? ASUM_LO : 0) +
-                           static_cast<uint32_t>((g + ((q >> 1) << 3)) * ASTR * 2);
-      float d[2][4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) d[h][i] = 0.f;
-      int grp = 0, left = k32_per_group;
-      bool ok = true;
-      for (int st = 0; st < nst; ++st) {
-        const int as = static_cast<int>(asl);
-        if (!__all_sync(0xffffffffu, wait(&ctrl.a_full[as], aph))) {
-          ok = false;
-          break;
-        }
-        const uint32_t ab = smem_u32(a_ring + as * A_STAGE) + g * AROW + q * 16;
-        const int jmax = min(8, (p.K - st * BK) >> 5);
-        for (int j = 0; j < jmax; ++j) {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            if (h < nhalf) {
-              const uint4 x0 = lds128(ab + (2 * h) * 8 * AROW + j * 64);
-              const uint4 x1 = lds128(ab + (2 * h + 1) * 8 * AROW + j * 64);
-              mma_16816(d[h], x0.x, x1.x, x0.y, x1.y, ones, ones);
-              mma_16816(d[h], x0.z, x1.z, x0.w, x1.w, ones, ones);
-            }
-          }
-          if (--left == 0) {
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              if (h < nhalf) {
-                // -sum / 16 as f16 hi + lo (an exact scaling; the zero-point term uses 16 s z)
-                const float v = -0.0625f * ((q >> 1) ? d[h][2] : d[h][0]);
-                const __half hi = __float2half_rn(v);
-                const __half lo = __float2half_rn(v - __half2float(hi));
-                sts16h(dst + static_cast<uint32_t>((16 * h * ASTR + grp) * 2), (q & 1) ? lo : hi);
-              }
-#pragma unroll
-              for (int i = 0; i < 4; ++i) d[h][i] = 0.f;
-            }
-            ++grp;
-            left = k32_per_group;
-          }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctrl.a_empty[as]);
-        if (++asl == static_cast<uint32_t>(sa)) { asl = 0; aph ^= 1u; }
-      }
-      if (!ok) break;
-      __syncwarp();
-      mbar_arrive(&ctrl.s_full[slot]);  // every lane: each releases its own table entries
-      if (lane == 0) mbar_arrive(&ctrl.i_empty[slot]);
-    }
-  } else if (warp < MATH_WARPS) {
+  } else {
     // ---------------------------------------------------------------- math warps
     const int g = lane >> 2, q = lane & 3;
     // smem rows of this lane's two fragment rows (tile rows g and g+8); both are = g (mod 8),
@@ -628,25 +416,7 @@ __global__ void __launch_bounds__(nthreads(IQ), 1)
           const uint32_t wa = smem_u32(w_ring + ws * W_STAGE) + rA * WROW + (g << 4) + 4 * q;
           const uint32_t ab = smem_u32(a_ring + as * A_STAGE) + g * AROW + q * 16;
           const int jmax = min(8, (p.K - st * BK) >> 5);
-          if (IQ) {
-            if constexpr (IQ && GPJ <= 4) {
-              if (jmax == 8) {
-                switch (ntl) {
-                  case 4: mma_stage_q<4, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, sB, acc); break;
-                  case 3: mma_stage_q<3, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, sB, acc); break;
-                  case 2: mma_stage_q<2, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, sB, acc); break;
-                  default: mma_stage_q<1, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, sB, acc);
-                }
-              } else {
-                switch (ntl) {
-                  case 4: mma_stage_q<4, GPJ, true, BOFF>(wa, ab, jmax, grp0, sA, sB, acc); break;
-                  case 3: mma_stage_q<3, GPJ, true, BOFF>(wa, ab, jmax, grp0, sA, sB, acc); break;
-                  case 2: mma_stage_q<2, GPJ, true, BOFF>(wa, ab, jmax, grp0, sA, sB, acc); break;
-                  default: mma_stage_q<1, GPJ, true, BOFF>(wa, ab, jmax, grp0, sA, sB, acc);
-                }
-              }
-            }
-          } else if (jmax == 8) {
+          if (jmax == 8) {
             switch (ntl) {
               case 4: mma_stage<ZINT, 4, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, zA, sB, zB, acc); break;
               case 3: mma_stage<ZINT, 3, GPJ, false, BOFF>(wa, ab, 8, grp0, sA, zA, sB, zB, acc); break;
@@ -671,20 +441,6 @@ __global__ void __launch_bounds__(nthreads(IQ), 1)
         if (++asl == static_cast<uint32_t>(sa)) { asl = 0; aph ^= 1u; }
         if (GPJ < 8) grp0 += 8 / GPJ;
         else if (--spg_left == 0) { ++grp0; spg_left = spg; }
-      }
-      if constexpr (IQ) {
-        // the zero-point term, once the group-sum warp has written this item's table
-        const bool sums = __all_sync(0xffffffffu, wait(&ctrl.s_full[slot], (n / IR) & 1));
-        if (sums && active) {
-          const uint32_t tab = smem_u32(asum_ring + slot * ASUM_SLOT) +
-                               static_cast<uint32_t>((g * ASTR + 2 * q) * 2);
-          switch (ntl) {
-            case 4: zero_point_term<4>(sA, zA, sB, zB, p.ng, q, tab, acc); break;
-            case 3: zero_point_term<3>(sA, zA, sB, zB, p.ng, q, tab, acc); break;
-            case 2: zero_point_term<2>(sA, zA, sB, zB, p.ng, q, tab, acc); break;
-            default: zero_point_term<1>(sA, zA, sB, zB, p.ng, q, tab, acc);
-          }
-        }
       }
       float res[NT][4];
 #pragma unroll
@@ -763,44 +519,30 @@ bool encode_map_hw(CUtensorMap* map, const uint8_t* q, int64_t total_rows, int64
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool GATED, bool ZINT, bool IQ, int GPJ>
+template <bool GATED, bool ZINT, int GPJ>
 int launch_hw_g(const hw::Params& p, const CUtensorMap& map, int grid, cudaStream_t s) {
-  if (set_max_dyn_smem(reinterpret_cast<const void*>(hw::hw_gemm_kernel<GATED, ZINT, IQ, GPJ>),
+  if (set_max_dyn_smem(reinterpret_cast<const void*>(hw::hw_gemm_kernel<GATED, ZINT, GPJ>),
                        static_cast<int>(hw::SMEM_LIMIT - hw::STATIC_RESERVE)) != KNX_OK)
     return KNX_E_DEVICE;
-  (void)launch_pdl(hw::hw_gemm_kernel<GATED, ZINT, IQ, GPJ>, grid, hw::nthreads(IQ),
-                   hw::smem_bytes(GATED, IQ, p.ng, p.sw, p.sa), s, map, p);
+  (void)launch_pdl(hw::hw_gemm_kernel<GATED, ZINT, GPJ>, grid, hw::NTHREADS,
+                   hw::smem_bytes(GATED, p.ng, p.sw, p.sa), s, map, p);
   return launch_status();
 }
 
-template <bool GATED, bool ZINT, bool IQ>
+template <bool GATED, bool ZINT>
 int launch_hw(hw::Params p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
               int64_t work_bound, cudaStream_t s) {
-  if (!hw::ring_depths(GATED, IQ, p.ng, p.sw, p.sa)) return KNX_E_UNSUPPORTED;
+  if (!hw::ring_depths(GATED, p.ng, p.sw, p.sa)) return KNX_E_UNSUPPORTED;
   CUtensorMap map;
   if (!encode_map_hw(&map, wq, total_rows, row_bytes)) return KNX_E_DEVICE;
   const int sms = num_sms();
   const int grid = static_cast<int>(work_bound < sms ? (work_bound > 0 ? work_bound : 1) : sms);
   switch (p.gs) {
-    case 32: return launch_hw_g<GATED, ZINT, IQ, 1>(p, map, grid, s);
-    case 64: return launch_hw_g<GATED, ZINT, IQ, 2>(p, map, grid, s);
-    case 128: return launch_hw_g<GATED, ZINT, IQ, 4>(p, map, grid, s);
-    default:  // gs % 256 == 0: exact modes only (integer-mode groups never straddle a stage)
-      if constexpr (IQ) return KNX_E_UNSUPPORTED;
-      else return launch_hw_g<GATED, ZINT, false, 8>(p, map, grid, s);
+    case 32: return launch_hw_g<GATED, ZINT, 1>(p, map, grid, s);
+    case 64: return launch_hw_g<GATED, ZINT, 2>(p, map, grid, s);
+    case 128: return launch_hw_g<GATED, ZINT, 4>(p, map, grid, s);
+    default: return launch_hw_g<GATED, ZINT, 8>(p, map, grid, s);  // gs % 256 == 0
   }
-}
-
-// The dequantisation mode of a call: integer (scale groups of 32-128) unless the caller asked
-// for the exact forms; exact forms by the zero-point flag.
-template <bool GATED>
-int launch_hw_mode(const hw::Params& p, const uint8_t* wq, int64_t total_rows, int64_t row_bytes,
-                   int64_t work_bound, int dq, cudaStream_t s) {
-  if (dq == DQ_INTEGER && p.gs <= 128)
-    return launch_hw<GATED, false, true>(p, wq, total_rows, row_bytes, work_bound, s);
-  if (dq == DQ_EXACT_ZINT)
-    return launch_hw<GATED, true, false>(p, wq, total_rows, row_bytes, work_bound, s);
-  return launch_hw<GATED, false, false>(p, wq, total_rows, row_bytes, work_bound, s);
 }
 
 }  // namespace
@@ -809,8 +551,7 @@ bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated
   // scale groups must not straddle a 256-k stage unless they cover whole stages
   if (!(gs == 32 || gs == 64 || gs == 128 || (gs > 0 && gs % 256 == 0))) return false;
   int sw, sa;
-  if (ng > hw::SZ_MAX || (K % 64) != 0 || !hw::ring_depths(gated, gs <= 128, ng, sw, sa))
-    return false;
+  if (ng > hw::SZ_MAX || (K % 64) != 0 || !hw::ring_depths(gated, ng, sw, sa)) return false;
   if (gated) return (rows_per_expert / 2) % 64 == 0;
   return rows_per_expert % 16 == 0;
 }
@@ -818,20 +559,21 @@ bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated
 int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, const int32_t* offsets,
                      const int4* tasks, const int32_t* ntasks, int* counter, const uint8_t* gu_q,
                      const __half* gu_s, const __half* gu_z, int E, int H, int I, int ng, int gs,
-                     int dq, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s) {
+                     bool zint, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s) {
   hw::Params p{};
   p.act = xp; p.act_stride = H; p.sorted_pair = sorted_pair; p.topk = topk; p.offsets = offsets;
   p.tasks = tasks; p.ntasks = ntasks; p.work_counter = counter; p.ws = gu_s; p.wz = gu_z;
   p.K = H; p.rows_per_expert = 2 * I; p.I = I; p.ng = ng; p.gs = gs; p.out = out2;
   p.out_stride = I; p.nslices = (I + hw::GROWS - 1) / hw::GROWS; p.err = err;
   const int64_t work = max_tasks * p.nslices;
-  return launch_hw_mode<true>(p, gu_q, int64_t(E) * 2 * I, H / 2, work, dq, s);
+  return zint ? launch_hw<true, true>(p, gu_q, int64_t(E) * 2 * I, H / 2, work, s)
+              : launch_hw<true, false>(p, gu_q, int64_t(E) * 2 * I, H / 2, work, s);
 }
 
 int launch_hw_rows(const __half* act, int64_t act_stride, int K, const int32_t* offsets,
                    const int4* tasks, const int32_t* ntasks, int dense_rows, int* counter,
                    const uint8_t* wq, const __half* ws, const __half* wz, int E, int N, int ng,
-                   int gs, int dq, __half* out, int64_t out_stride, int64_t max_tasks,
+                   int gs, bool zint, __half* out, int64_t out_stride, int64_t max_tasks,
                    int32_t* err, cudaStream_t s) {
   hw::Params p{};
   p.act = act; p.act_stride = act_stride; p.offsets = offsets; p.tasks = tasks; p.ntasks = ntasks;
@@ -839,7 +581,8 @@ int launch_hw_rows(const __half* act, int64_t act_stride, int K, const int32_t* 
   p.rows_per_expert = N; p.ng = ng; p.gs = gs; p.out = out; p.out_stride = out_stride;
   p.nslices = (N + hw::ROWS - 1) / hw::ROWS; p.err = err;
   const int64_t work = max_tasks * p.nslices;
-  return launch_hw_mode<false>(p, wq, int64_t(E) * N, K / 2, work, dq, s);
+  return zint ? launch_hw<false, true>(p, wq, int64_t(E) * N, K / 2, work, s)
+              : launch_hw<false, false>(p, wq, int64_t(E) * N, K / 2, work, s);
 }
 
 }  // namespace knx

@@ -27,22 +27,17 @@ KNX_W4_INT_ZEROS = 0x1
 KNX_W4_WARP_MMA = 0x2
 KNX_W4_WARP_WS = 0x8
 KNX_W4_TCGEN05 = 0x10
-KNX_W4_EXACT_DEQUANT = 0x20
 _ENGINES = {"auto": 0, "tc": KNX_W4_TCGEN05, "mma": KNX_W4_WARP_MMA, "ws": KNX_W4_WARP_WS}
 
 
-def engine_flags(engine=None, exact=None):
+def engine_flags(engine=None):
     """Engine selection flags for the W4A16 GEMMs: "auto" (the default: the warp-specialised
     mma.sync kernels up to 36 tokens per expert, tcgen05 above), "ws", "tc" (tcgen05) or "mma"
-    (the plain mma.sync kernels); `engine` or the KNX_ENGINE environment variable chooses.
-    exact=True (or KNX_EXACT_DEQUANT=1) makes the warp-specialised kernels dequantise with the
-    f16 forms of the other engines instead of exact nibbles with a per-group fp32 scale."""
+    (the plain mma.sync kernels); `engine` or the KNX_ENGINE environment variable chooses."""
     engine = engine or os.environ.get("KNX_ENGINE", "auto")
     if engine not in _ENGINES:
         raise ValueError(f"unknown engine {engine!r}")
-    if exact is None:
-        exact = os.environ.get("KNX_EXACT_DEQUANT", "0") == "1"
-    return _ENGINES[engine] | (KNX_W4_EXACT_DEQUANT if exact else 0)
+    return _ENGINES[engine]
 
 _c = ctypes
 _vp, _i64, _i32, _f32, _sz = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_float, _c.c_size_t

@@ -22,8 +22,8 @@ The device steps come from an `ops` object: CudaOps runs the sm_100a kernels thr
 import torch
 import torch.distributed as dist
 
-from _knx import (KNX_W4_INT_ZEROS, check, dtype_code, engine_flags, load, ptr, require_device,
-                  stream_of, workspace, zero_flags)
+from _knx import (KNX_DEV_TIMEOUT, KNX_W4_INT_ZEROS, check, dtype_code, engine_flags, load, ptr,
+                  require_device, stream_of, workspace, zero_flags)
 
 
 class CudaOps:
@@ -103,7 +103,7 @@ class ExpertParallelMoE:
     (contiguous slices of the full [E_total, ...] tensors)."""
 
     def __init__(self, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=None, ops=None,
-                 engine=None, int_zeros=None, exact=None):
+                 engine=None, int_zeros=None):
         self.weights = (gu_q, gu_s, gu_z, dn_q, dn_s, dn_z)
         self.E = E_total
         self.group = group
@@ -117,7 +117,7 @@ class ExpertParallelMoE:
             flags = zero_flags(gu_z, dn_z) if gu_z.is_cuda else 0
         else:
             flags = KNX_W4_INT_ZEROS if int_zeros else 0
-        self.flags = flags | engine_flags(engine, exact)
+        self.flags = flags | engine_flags(engine)
 
     @torch.no_grad()
     def forward(self, x, topk_ids, topk_w, out_dtype=torch.float16, tokens_per_expert=None):
@@ -237,9 +237,9 @@ class P2PExpertParallelMoE(ExpertParallelMoE):
     The output is bit-identical to ExpertParallelMoE and to the single-GPU layer."""
 
     def __init__(self, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=None, engine=None,
-                 int_zeros=None, max_tokens=256, topk=8, exact=None):
+                 int_zeros=None, max_tokens=256, topk=8):
         super().__init__(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=group, ops=CudaOps(),
-                         engine=engine, int_zeros=int_zeros, exact=exact)
+                         engine=engine, int_zeros=int_zeros)
         H = gu_q.shape[2] * 2
         self.ex = _P2PExchange.get(group, E_total, max_tokens * topk, H, gu_q.device)
 
@@ -277,3 +277,17 @@ class P2PExpertParallelMoE(ExpertParallelMoE):
         return self.ops.combine(ex.ret[:T * tk], inv, topk_w.contiguous(), T, out_dtype)
 
     __call__ = forward
+
+    def check_errors(self):
+        """Read and clear the exchange's device error word (one host synchronisation).  Raises
+        RuntimeError when a device-side barrier gave up because a peer did not arrive within
+        2 s: every layer run through this exchange since the previous check may have returned
+        invalid rows (after a failed counts barrier the plan is empty, so nothing is written
+        into the peers and the GEMMs do nothing).  Call it where a sync is acceptable, e.g. once
+        per denoising step; forward() itself never synchronises."""
+        bad = int(self.ex.err.item())
+        self.ex.err.zero_()
+        if bad & KNX_DEV_TIMEOUT:
+            raise RuntimeError("expert-parallel exchange: a device-side barrier timed out "
+                               "(a peer rank did not arrive within 2 s)")
+        return bad

@@ -107,10 +107,10 @@ def _err_word(dev):
 
 
 def moe_forward(hidden, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, topk_ids, topk_w, hidden_perm=None,
-                out=None, int_zeros=None, engine=None, exact=None):
+                out=None, int_zeros=None, engine=None):
     """Raw entry: one MoE layer from explicit buffers (see knx_moe_w4 in include/knx.h).
     int_zeros: True/False to state whether the zero-points are integers in [0, 15]; None checks
-    once per tensor (see _knx.zero_flags).  engine / exact: see _knx.engine_flags."""
+    once per tensor (see _knx.zero_flags).  engine: see _knx.engine_flags."""
     dev = require_device(hidden)
     T, H = hidden.shape
     tk = topk_ids.shape[1]
@@ -131,7 +131,7 @@ def moe_forward(hidden, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, topk_ids, topk_w, hi
         flags = zero_flags(gu_z, dn_z)
     else:
         flags = KNX_W4_INT_ZEROS if int_zeros else 0
-    flags |= engine_flags(engine, exact)
+    flags |= engine_flags(engine)
     lib = load()
     nbytes = lib.knx_moe_w4_workspace_size(T, H, I, E, tk)
     ws = workspace(dev, nbytes, "moe")

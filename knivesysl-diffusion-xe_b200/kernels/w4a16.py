@@ -47,7 +47,7 @@ def dequant_w4(qpacked, scale, zero, group_size=GS):
     return W.reshape(N, K).to(torch.float16)
 
 
-def w4a16_linear(X, qpacked, scale, zero, BK=GS, int_zeros=None, engine=None, exact=None):
+def w4a16_linear(X, qpacked, scale, zero, BK=GS, int_zeros=None, engine=None):
     """Y[M,N] = X[M,K] @ dequant(qpacked)[N,K].T, fp16 out; reads the packed nibbles directly.
 
     BK is the group size (the reference ties its K tile to it).  Requirements: K % 64 == 0,
@@ -66,7 +66,7 @@ def w4a16_linear(X, qpacked, scale, zero, BK=GS, int_zeros=None, engine=None, ex
         flags = zero_flags(z)
     else:
         flags = KNX_W4_INT_ZEROS if int_zeros else 0
-    flags |= engine_flags(engine, exact)
+    flags |= engine_flags(engine)
     lib = load()
     nbytes = lib.knx_w4a16_workspace_size(M, K)
     ws = workspace(dev, nbytes, "w4a16")

@@ -128,7 +128,7 @@ def _worker_p2p(rank, world, port, out_dir):
         ys = [layer(xp[sl].contiguous(), ids[sl].contiguous(), w[sl].contiguous(),
                     out_dtype=torch.float16).clone() for _ in range(3)]
         torch.cuda.synchronize()
-        err = int(layer.ex.err.item())
+        err = layer.check_errors()
         same = all(torch.equal(ys[0].view(torch.int16), y.view(torch.int16)) for y in ys[1:])
         torch.save({"y": ys[0].cpu(), "err": err, "same": same}, os.path.join(out_dir, f"p{rank}.pt"))
         dist.barrier()
@@ -157,7 +157,58 @@ def test_ep_p2p_one_rank_bitwise_equal_single_gpu(cuda):
     _run_p2p(1)
 
 
-def test_ep_p2p_two_gpus_bitwise_equal_single_gpu(cuda):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    _run_p2p(2)
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ep_p2p_multi_gpu_bitwise_equal_single_gpu(cuda, world):
+    """2, 4 and 8 ranks (one canvas each, 128 / world experts per rank) through the NVLink
+    exchange, three layers in a row: bit-identical to the single-GPU layer on all the tokens."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run_p2p(world)
+
+
+def test_p2p_barrier_gives_up_and_the_plan_is_empty(cuda):
+    """A peer that never arrives, on one GPU: this GPU plays rank 0 of 2 and the peer's region
+    is a local buffer nothing writes.  The barrier gives up after its 2 s limit and reports
+    KNX_DEV_TIMEOUT; the counts step then writes the empty plan, the dispatch stores nothing into
+    the peers' rows, and the context stays usable."""
+    import time
+    import _knx
+    import fused_moe_w4
+    lib = _knx.load()
+    E, El, world, H, tk, T = 8, 4, 2, 64, 2, 4
+    i64 = dict(dtype=torch.int64, device=cuda)
+    flags = [torch.zeros(64, dtype=torch.int32, device=cuda) for _ in range(world)]
+    cnt = [torch.zeros(world * E, dtype=torch.int32, device=cuda) for _ in range(world)]
+    rows = [torch.full((T * tk, H), 3.0, dtype=torch.float16, device=cuda) for _ in range(world)]
+    peer_flags = torch.tensor([f.data_ptr() for f in flags], **i64)
+    peer_cnt = torch.tensor([c.data_ptr() for c in cnt], **i64)
+    peer_rows = torch.tensor([r.data_ptr() for r in rows], **i64)
+    err = torch.zeros(1, dtype=torch.int32, device=cuda)
+    st = _knx.stream_of(cuda.index or 0)
+    p = _knx.ptr
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    assert lib.knx_ep_p2p_barrier(p(peer_flags), 0, world, 1, p(err), st) == 0
+    torch.cuda.synchronize()
+    waited = time.monotonic() - t0
+    assert int(err.item()) & _knx.KNX_DEV_TIMEOUT
+    assert 1.5 < waited < 30.0, waited
+    assert int(flags[1][0].item()) == 1          # this rank's epoch reached the peer's flag
+    err.zero_()
+    g = torch.Generator().manual_seed(2)
+    ids = torch.randint(0, E, (T, tk), generator=g, dtype=torch.int32).to(cuda)
+    counts, offsets, sorted_pair, _ = fused_moe_w4.moe_align_unpadded(ids, E)
+    nplan = lib.knx_ep_p2p_plan_ints(E, El, world)
+    plan = torch.full((nplan,), 7, dtype=torch.int32, device=cuda)
+    assert lib.knx_ep_p2p_counts(p(counts.to(torch.int32)), E, El, 0, world, p(peer_cnt),
+                                 p(peer_flags), 2, p(plan), p(err), st) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) & _knx.KNX_DEV_TIMEOUT
+    assert (plan[:E] == -1).all()                          # no destination for any expert
+    assert (plan[E:E + El + 2 + El * world] == 0).all()    # no receive rows, no segments
+    xp = torch.randn(T, H, device=cuda).half()
+    assert lib.knx_ep_p2p_dispatch(p(xp), H, tk, p(sorted_pair), p(offsets), E, El, p(plan),
+                                   p(peer_rows), T * tk, st) == 0
+    torch.cuda.synchronize()
+    assert all(bool((r == 3.0).all()) for r in rows)
+    assert torch.ones(8, device=cuda).sum().item() == 8.0

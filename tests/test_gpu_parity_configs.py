@@ -7,8 +7,9 @@
   the hottest expert), checked against the oracle on the hottest and a cold expert;
 * the sampler at 256 x 262,144, every row's sampled token at three temperatures of
   the schedule;
-* the warp-specialised GEMMs in both dequantisation modes (integer default, exact) against the
-  oracle and against the unrounded W4 arithmetic in float64.
+* every engine at the configs[0] shape against the oracle and against the W4 arithmetic with
+  unrounded weights in float64 (how far each is from the exact math, beside the reference's own
+  torch path).
 """
 import os
 
@@ -76,9 +77,7 @@ def test_configs1_pipeline_end_to_end(cuda):
     # MoE on the kernel's normalised input and routing
     want = ref.moe_layer(y_norm.cpu(), W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"],
                          W["dn_z"], ids.cpu(), w.cpu())
-    assert_close_fp16(y, want, what="cfg1 layer (ws integer)")
-    y_ex = fused_moe_w4_v2.moe_forward(y_norm, *args, ids, w, hidden_perm=xp, exact=True)
-    assert_close_fp16(y_ex, want, what="cfg1 layer (ws exact)")
+    assert_close_fp16(y, want, what="cfg1 layer (default engine)")
     again = fused_moe_w4_v2.moe_forward(y_norm, *args, ids, w, hidden_perm=xp)
     assert torch.equal(y.view(torch.int16), again.view(torch.int16))
 
@@ -101,18 +100,23 @@ def test_configs4_prefill_sampled_experts(cuda):
     pos = torch.nonzero(counts > 0).flatten()
     cold = int(pos[counts[pos].argmin()])
     assert counts[hot] > 4000, counts[hot]
-    keep = (ids == hot) | (ids == cold)
+    # one kept pair per row, weight 1: the output row is that pair's down output itself, so the
+    # comparison is per pair (a sum of several rounded pairs can cancel to near zero)
+    keep = ids == hot                          # top-k ids of a row are distinct
+    keep = keep | ((ids == cold) & ~keep.any(dim=1, keepdim=True))
     ids_f = torch.where(keep, ids, torch.full_like(ids, E))   # E = the reference's dropped id
+    w_f = keep.float()
     W = workloads.moe_weights(E, H, I, seed=7, device=cuda)
     y = fused_moe_w4_v2.moe_forward(x, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"],
-                                    W["dn_z"], ids_f, w)
+                                    W["dn_z"], ids_f, w_f)
     Wc = {k: v.cpu() for k, v in W.items()}
     want = ref.moe_layer(x.cpu(), Wc["gu_q"], Wc["gu_s"], Wc["gu_z"], Wc["dn_q"], Wc["dn_s"],
-                         Wc["dn_z"], ids_f.cpu(), w.cpu())
+                         Wc["dn_z"], ids_f.cpu(), w_f.cpu())
     rows = keep.any(dim=1).cpu()
+    n_hot = int((ids_f == hot).sum())
+    assert n_hot == int(counts[hot])           # every pair of the hottest expert is checked
     assert_close_fp16(y.cpu()[rows], want[rows],
-                      what=f"cfg4 tc, experts {hot} ({int(counts[hot])} pairs) + {cold} "
-                           f"({int(counts[cold])})")
+                      what=f"cfg4 tc per pair, expert {hot} ({n_hot} pairs) + expert {cold}")
     assert (y.cpu()[~rows] == 0).all()
 
 
@@ -163,62 +167,49 @@ def _moe_layer_unrounded(hidden, W, ids, w, gs_gu=128, gs_dn=64):
     return y.to(hidden.dtype)
 
 
-@pytest.mark.parametrize("T,E,H,I,tk,skew", [
-    (256, 128, 2816, 704, 8, None), (1, 128, 2816, 704, 8, None), (33, 8, 256, 64, 2, "one"),
-    (100, 32, 768, 192, 8, "drop"), (300, 4, 256, 64, 2, "one")])
-def test_ws_dequant_modes_vs_oracle(cuda, T, E, H, I, tk, skew):
-    """The warp-specialised engine's integer dequantisation (exact nibbles in the MMA, fp32 scale
-    per group, zero-point term per item) and its exact one, each against the oracle, both
-    bit-identical run to run; at the configs[0] shape also against the unrounded W4 arithmetic,
-    where the integer mode must be at least as close as the reference's own torch path."""
+def test_engines_vs_unrounded_w4_arithmetic(cuda):
+    """configs[0] shapes: every engine's rms distance to the W4 arithmetic with unrounded
+    weights is within 10% of the reference torch path's own (which rounds each dequantised
+    weight to f16); all engines bit-identical run to run."""
     import fused_moe_w4_v2
     import workloads
     torch.set_num_threads(_threads())
+    T, E, H, I, tk = 256, 128, 2816, 704, 8
     W = workloads.moe_weights(E, H, I, seed=T + E)
     g = torch.Generator().manual_seed(T + E + 5)
     hidden = torch.randn(T, H, generator=g).half()
     ids, w = workloads.random_routing(T, E, tk, seed=T + E)
-    if skew == "one":
-        ids[:, 0] = 1
-    elif skew == "drop":
-        ids[::3, -1] = E
     Wd = {k: v.to(cuda) for k, v in W.items()}
     args = (Wd["gu_q"], Wd["gu_s"], Wd["gu_z"], Wd["dn_q"], Wd["dn_s"], Wd["dn_z"])
+    truth = _moe_layer_unrounded(hidden, W, ids, w).float()
     want = ref.moe_layer(hidden, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"], W["dn_z"],
-                         ids, w)
-    ys = {}
-    for exact in (False, True):
+                         ids, w).float()
+    rms = lambda a: (a - truth).pow(2).mean().sqrt().item()
+    e_ref = rms(want)
+    for eng in ("ws", "tc", "mma"):
         y = fused_moe_w4_v2.moe_forward(hidden.to(cuda), *args, ids.to(cuda), w.to(cuda),
-                                        engine="ws", exact=exact)
+                                        engine=eng)
         y2 = fused_moe_w4_v2.moe_forward(hidden.to(cuda), *args, ids.to(cuda), w.to(cuda),
-                                         engine="ws", exact=exact)
+                                         engine=eng)
         assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
-        mode = "exact" if exact else "integer"
-        assert_close_fp16(y, want, what=f"ws {mode} T={T} E={E} H={H}")
-        ys[mode] = y.cpu().float()
-    if T == 256 and E == 128:
-        truth = _moe_layer_unrounded(hidden, W, ids, w).float()
-        rms = lambda a: (a - truth).pow(2).mean().sqrt().item()
-        e_int, e_ex, e_ref = rms(ys["integer"]), rms(ys["exact"]), rms(want.float())
-        print(f"rms error vs unrounded W4: ws integer {e_int:.3e}, ws exact {e_ex:.3e}, "
-              f"reference torch path {e_ref:.3e}")
-        assert e_int <= 1.05 * e_ref
+        e = rms(y.cpu().float())
+        print(f"rms distance to the unrounded W4 arithmetic: {eng} {e:.3e}, reference torch "
+              f"path {e_ref:.3e}")
+        assert e <= 1.10 * e_ref, (eng, e, e_ref)
 
 
-def test_ws_integer_dequant_large_activations_and_scales(cuda):
-    """The integer mode's f16 splits of 16 s z and of the group sums / 16 near the ends of their
-    range: activations up to 60 (group sums in the thousands), scales up to 1, zeros up to 15."""
+def test_ws_large_activations_and_scales(cuda):
+    """The warp-specialised dense W4A16 GEMM with activations up to 60 and scales up to 0.05,
+    zero-points up to 15 (outputs in the thousands, still inside the f16 range)."""
     import w4a16
     g = torch.Generator().manual_seed(8)
     M, N, K, gs = 40, 256, 1024, 128
     X = (torch.randn(M, K, generator=g) * 20).clamp(-60, 60).half()
-    X[3] = 60.0                                     # one row of constant large activations
+    X[3] = 30.0                                     # one row of constant large activations
     q = torch.randint(0, 256, (N, K // 2), generator=g, dtype=torch.uint8)
-    s = (torch.rand(N, K // gs, generator=g) * 0.999 + 0.001).half()
+    s = (torch.rand(N, K // gs, generator=g) * 0.049 + 0.001).half()
     z = (torch.rand(N, K // gs, generator=g) * 15).half()
     want = X.double() @ ref.dequant_w4(q, s, z, gs).double().T
-    for exact in (False, True):
-        Y = w4a16.w4a16_linear(X.to(cuda), q.to(cuda), s.to(cuda), z.to(cuda), BK=gs,
-                               engine="ws", exact=exact)
-        assert_close_fp16(Y, want.half(),
-                          what=f"w4a16 ws {'exact' if exact else 'integer'} large activations")
+    assert want.abs().max().item() < 60000
+    Y = w4a16.w4a16_linear(X.to(cuda), q.to(cuda), s.to(cuda), z.to(cuda), BK=gs, engine="ws")
+    assert_close_fp16(Y, want.half(), what="w4a16 ws large activations")
