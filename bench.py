@@ -304,7 +304,32 @@ def time_layer_ep(dev, steps, warmup, rank, world):
     t = torch.tensor([e2e_ms], device=dev)
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     e2e_ms = float(t.item())
-    return ms, counts, clocks, e2e_ms, h2d, d2h
+    stages = ep_stage_times(ep, dev, steps)
+    return ms, counts, clocks, e2e_ms, h2d, d2h, stages
+
+
+def ep_stage_times(ep, dev, steps):
+    """A second pass of `steps` layers with CUDA events between the stages of the NVLink layer
+    (the events stop the kernels from overlapping, so the stages add up to more than a step of
+    the timed pass): per stage the mean device time in us, max over ranks.  The barrier stages
+    hold the wait for the slowest rank."""
+    for layer in ep.layers:
+        layer.stage_events = []
+    torch.distributed.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(steps):
+        ep.step(i)
+    torch.cuda.synchronize(dev)
+    sums = {}
+    for layer in ep.layers:
+        marks, layer.stage_events = layer.stage_events, None
+        for (_, a), (name, b) in zip(marks, marks[1:]):
+            if name != "start":
+                sums[name] = sums.get(name, 0.0) + a.elapsed_time(b)
+    names = sorted(sums)
+    t = torch.tensor([sums[n] for n in names], device=dev)
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return {n: float(v) * 1000.0 / steps for n, v in zip(names, t.tolist())}
 
 
 def time_stack(dev, steps=48):
@@ -591,8 +616,8 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                              device_id=dev)
     if dist:
-        ms, counts, clocks, e2e_ms, h2d, d2h = time_layer_ep(dev, args.steps, args.warmup, rank,
-                                                             world)
+        ms, counts, clocks, e2e_ms, h2d, d2h, ep_stages = time_layer_ep(dev, args.steps,
+                                                                        args.warmup, rank, world)
         stages = {}
     else:
         ms, stages, counts, clocks = time_layer(dev, args.steps, args.warmup, dist)
@@ -643,7 +668,9 @@ def main():
         # each step streams every touched expert once, split over the ranks: per-GPU fraction
         "layer_hbm_frac": bytes_layer / (ms_step * 1e-3) / 1e9 / (peak * world),
         "layer_bytes": bytes_layer,
-        "stages_us": {k: v * 1000.0 for k, v in stages.items()},
+        "stages_us": ({k: v * 1000.0 for k, v in stages.items()} if not dist else
+                      {"note": "per rank, with events between stages (no overlap), max over ranks",
+                       **ep_stages}),
         "roofline": {"kernel": GEMM1_KERNEL[engine], "bound": "hbm", "achieved": achieved,
                      "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak if achieved else None,

@@ -63,6 +63,14 @@ KNX_DEVINL bool p2p_barrier(uint32_t* const* peer_flags, int rank, int world, ui
   return true;
 }
 
+// Every thread's peer stores of this CTA are ordered before one system-scope fence (the CTA
+// barrier makes them visible to thread 0, whose fence is cumulative); the next barrier kernel's
+// release stores then publish them.  One fence per CTA instead of one per warp.
+KNX_DEVINL void cta_fence_system() {
+  __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();
+}
+
 KNX_DEVINL int warp_incl_scan(int v, int lane) {
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -151,19 +159,21 @@ __global__ void __launch_bounds__(256)
   pdl_wait_trigger();
   const int lane = threadIdx.x & 31;
   const int64_t j = blockIdx.x * static_cast<int64_t>(blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (j >= n_cap || j >= offsets[E]) return;
-  int lo = 0, hi = E - 1;  // the expert of slot j: last e with offsets[e] <= j
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (offsets[mid] <= j) lo = mid; else hi = mid - 1;
+  if (j < n_cap && j < offsets[E]) {
+    int lo = 0, hi = E - 1;  // the expert of slot j: last e with offsets[e] <= j
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (offsets[mid] <= j) lo = mid; else hi = mid - 1;
+    }
+    const int e = lo, r = e % (E / El);  // owner: round-robin sharding
+    if (plan[e] >= 0) {                  // plan[e] < 0: the counts barrier gave up (empty plan)
+      const int64_t dst = plan[e] + (j - offsets[e]);
+      const uint4* s = xp + static_cast<int64_t>(sorted_pair[j] / topk) * vpr;
+      uint4* d = peer_rows[r] + dst * vpr;
+      for (int v = lane; v < vpr; v += 32) d[v] = ldg_nc_v4(s + v);
+    }
   }
-  const int e = lo, r = e % (E / El);  // owner: round-robin sharding
-  if (plan[e] < 0) return;             // the counts barrier gave up: empty plan
-  const int64_t dst = plan[e] + (j - offsets[e]);
-  const uint4* s = xp + static_cast<int64_t>(sorted_pair[j] / topk) * vpr;
-  uint4* d = peer_rows[r] + dst * vpr;
-  for (int v = lane; v < vpr; v += 32) d[v] = ldg_nc_v4(s + v);
-  __threadfence_system();
+  cta_fence_system();
 }
 
 // One warp per local row j (expert-major): the result row back into its source rank's return
@@ -178,18 +188,19 @@ __global__ void __launch_bounds__(256)
   const int32_t* seg_start = plan + E + El + 1;
   const int32_t* src_base = seg_start + El * world + 1;
   const int nseg = El * world;
-  if (j >= r_cap || j >= seg_start[nseg]) return;
-  int lo = 0, hi = nseg - 1;  // last segment (el, s) starting at or before j
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (seg_start[mid] <= j) lo = mid; else hi = mid - 1;
+  if (j < r_cap && j < seg_start[nseg]) {
+    int lo = 0, hi = nseg - 1;  // last segment (el, s) starting at or before j
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (seg_start[mid] <= j) lo = mid; else hi = mid - 1;
+    }
+    const int s = lo % world;
+    const int64_t dst = src_base[lo] + (j - seg_start[lo]);
+    const uint4* src = out3 + j * vpr;
+    uint4* d = peer_ret[s] + dst * vpr;
+    for (int v = lane; v < vpr; v += 32) d[v] = ldg_nc_v4(src + v);
   }
-  const int s = lo % world;
-  const int64_t dst = src_base[lo] + (j - seg_start[lo]);
-  const uint4* src = out3 + j * vpr;
-  uint4* d = peer_ret[s] + dst * vpr;
-  for (int v = lane; v < vpr; v += 32) d[v] = ldg_nc_v4(src + v);
-  __threadfence_system();
+  cta_fence_system();
 }
 
 __global__ void p2p_barrier_kernel(uint32_t* const* __restrict__ peer_flags, int rank, int world,

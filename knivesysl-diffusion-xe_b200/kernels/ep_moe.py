@@ -242,6 +242,15 @@ class P2PExpertParallelMoE(ExpertParallelMoE):
                          engine=engine, int_zeros=int_zeros)
         H = gu_q.shape[2] * 2
         self.ex = _P2PExchange.get(group, E_total, max_tokens * topk, H, gu_q.device)
+        # set to a list to get (stage name, CUDA event) marks recorded on the stream between
+        # the layer's stages (benchmark breakdowns; records stop the kernels from overlapping)
+        self.stage_events = None
+
+    def _mark(self, name):
+        if self.stage_events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.stage_events.append((name, ev))
 
     @torch.no_grad()
     def forward(self, x, topk_ids, topk_w, out_dtype=torch.float16, tokens_per_expert=None):
@@ -257,24 +266,34 @@ class P2PExpertParallelMoE(ExpertParallelMoE):
             tokens_per_expert = T * tk * self.N // self.E
         dev = require_device(x)
         st = stream_of(dev)
+        self._mark("start")
         counts, offsets, sorted_pair, inv = self.ops.align(topk_ids, self.E)
         counts = counts.to(torch.int32)
         E, El, world, rank = self.E, self.El, self.N, self.rank
+        self._mark("align")
         check(lib.knx_ep_p2p_counts(ptr(counts), E, El, rank, world, ptr(ex.peer_cnt),
                                     ptr(ex.peer_flags), ex.next_epoch(), ptr(ex.plan), ptr(ex.err),
                                     st), "knx_ep_p2p_counts")
+        self._mark("counts+barrier+plan")
         check(lib.knx_ep_p2p_dispatch(ptr(x.contiguous()), H, tk, ptr(sorted_pair), ptr(offsets), E,
                                       El, ptr(ex.plan), ptr(ex.peer_rows), T * tk, st),
               "knx_ep_p2p_dispatch")
+        self._mark("dispatch")
         check(lib.knx_ep_p2p_barrier(ptr(ex.peer_flags), rank, world, ex.next_epoch(),
                                      ptr(ex.err), st), "knx_ep_p2p_barrier")
+        self._mark("barrier1")
         recv_off = ex.plan[E:E + El + 1]
         out3 = self.ops.grouped_rows(ex.rows, recv_off, self.weights, tokens_per_expert, self.flags)
+        self._mark("grouped_gemms")
         check(lib.knx_ep_p2p_return(ptr(out3), H, El, world, E, ptr(ex.plan), ptr(ex.peer_ret),
                                     ex.r_cap, st), "knx_ep_p2p_return")
+        self._mark("return")
         check(lib.knx_ep_p2p_barrier(ptr(ex.peer_flags), rank, world, ex.next_epoch(),
                                      ptr(ex.err), st), "knx_ep_p2p_barrier")
-        return self.ops.combine(ex.ret[:T * tk], inv, topk_w.contiguous(), T, out_dtype)
+        self._mark("barrier2")
+        y = self.ops.combine(ex.ret[:T * tk], inv, topk_w.contiguous(), T, out_dtype)
+        self._mark("combine")
+        return y
 
     __call__ = forward
 
