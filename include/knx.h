@@ -276,6 +276,9 @@ KNX_API int knx_sampler_fused_sc(const float* logits, int64_t rows, int64_t V, f
  *     at V = 262144) return KNX_E_WORKSPACE without launching anything;
  *   - the first call on a device looks the array up (cudaGetSymbolAddress with that device
  *     current); make it before any stream capture begins;
+ *   - that address is kept for the life of the process: after cudaDeviceReset (or any other
+ *     teardown of the device's primary context) it is stale, so do not call this entry point
+ *     on that device again in the same process;
  *   - tickets/bounds/counter are zeroed in stream order by every call;
  *   - calls that can overlap in time on one device (other streams, unordered host threads) race
  *     on the shared scratch; calls in order on one stream are safe.
