@@ -313,8 +313,11 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
 
 // ------------------------------------------------------------------------------------------
 // Streaming variant for V % 4 == 0 (the configs' 262144-wide rows): one persistent CTA per SM.
-//   * work items are quarter rows (SX_CHUNK = 65536 columns, 8 stages), assigned statically (CTA
-//     c takes items c, c + grid, ...), so all roles walk the same sequence without a work queue;
+//   * work items are quarter rows (SX_CHUNK = 65536 columns, 8 stages), assigned statically in
+//     contiguous blocks (CTA c takes items c*n .. c*n + n - 1), so all roles walk the same
+//     sequence without a work queue, and a CTA mostly takes a row's quarters one after another:
+//     its Gumbel bound carries over from quarter to quarter (measured 4-7 us per step faster at
+//     T = 0.4-0.7 than CTA c taking items c, c + grid, ...);
 //   * warp 16 streams each item through a ring of 4 x 32 KB shared-memory stages with 1-D bulk
 //     copies (128 KB in flight per SM, what HBM needs at full rate);
 //   * warps 0-15 each take 512 columns of every 8192-column stage.  The running maximum and the
@@ -407,6 +410,8 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
   const uint32_t cq_q = cq_col + SX_WARPS * SX_CQ * 4;      // float [SX_WARPS][SX_CQ]
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t nitems = rows * nchunks;
+  const int64_t per_cta = (nitems + gridDim.x - 1) / gridDim.x;
+  const int64_t it_beg = blockIdx.x * per_cta, it_end = min(nitems, it_beg + per_cta);
   if (tid == 0) {
     for (int i = 0; i < SX_RING; ++i) { mbar_init(&c.full[i], 1); mbar_init(&c.empty[i], SX_WARPS); }
     for (int i = 0; i < 2; ++i) { mbar_init(&c.pfull[i], SX_WARPS); mbar_init(&c.pempty[i], 1); }
@@ -427,7 +432,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       uint32_t u = 0;
-      for (int64_t item = blockIdx.x; item < nitems && !*abort_flag; item += gridDim.x) {
+      for (int64_t item = it_beg; item < it_end && !*abort_flag; ++item) {
         const int64_t row = item / nchunks;
         const int chunk = static_cast<int>(item - row * nchunks);
         const int c_beg = min(V, chunk * SX_CHUNK), c_end = min(V, c_beg + SX_CHUNK);
@@ -452,7 +457,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     // ------------------------------------------------------------ item merger
     if (lane == 0) {
       int k = 0;
-      for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++k) {
+      for (int64_t item = it_beg; item < it_end; ++item, ++k) {
         const int b = k & 1;
         if (*abort_flag || !mbar_wait(&c.pfull[b], (k >> 1) & 1, 2000000000ull, 64)) {
           if (!*abort_flag) fail();
@@ -495,7 +500,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
     int k = 0;
     const uint32_t wcol = cq_col + warp * SX_CQ * 4;  // this warp's deferred Gumbel candidates
     const uint32_t wq = cq_q + warp * SX_CQ * 4;
-    for (int64_t item = blockIdx.x; item < nitems; item += gridDim.x, ++k) {
+    for (int64_t item = it_beg; item < it_end; ++item, ++k) {
       const int64_t row = item / nchunks;
       const int chunk = static_cast<int>(item - row * nchunks);
       const int c_beg = min(V, chunk * SX_CHUNK), c_end = min(V, c_beg + SX_CHUNK);
