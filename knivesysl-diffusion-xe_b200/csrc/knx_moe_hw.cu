@@ -101,6 +101,7 @@ struct Params {
   __half* out;
   int64_t out_stride;
   int nslices;
+  int partial_last;  // the last slice has fewer valid rows than the others (scheduled last)
   int sw;  // weight ring depth (stages)
   int sa;  // activation ring depth (stages)
   int32_t* err;
@@ -244,8 +245,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int wi = atomicAdd(p.work_counter, 1);
         Item it{};
         if (wi < nwork) {
-          const int task = wi / p.nslices;
-          it.slice = wi - task * p.nslices;
+          // items of full slices first (task-major: a task's slices run together and share its
+          // activations in L2), then the half-filled last slices of every task (gate_up with
+          // I % 128 != 0), which are the cheapest items and so fill the tail of the grid
+          const int nfull_sl = p.partial_last ? p.nslices - 1 : p.nslices;
+          const int ntask = nwork / p.nslices;
+          int task;
+          if (wi < ntask * nfull_sl) {
+            task = wi / nfull_sl;
+            it.slice = wi - task * nfull_sl;
+          } else {
+            task = wi - ntask * nfull_sl;
+            it.slice = nfull_sl;
+          }
           int t0;
           if (p.tasks) {
             const int4 tk = p.tasks[task];
@@ -565,6 +577,7 @@ int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, con
   p.tasks = tasks; p.ntasks = ntasks; p.work_counter = counter; p.ws = gu_s; p.wz = gu_z;
   p.K = H; p.rows_per_expert = 2 * I; p.I = I; p.ng = ng; p.gs = gs; p.out = out2;
   p.out_stride = I; p.nslices = (I + hw::GROWS - 1) / hw::GROWS; p.err = err;
+  p.partial_last = (I % hw::GROWS) != 0 && p.nslices > 1;
   const int64_t work = max_tasks * p.nslices;
   return zint ? launch_hw<true, true>(p, gu_q, int64_t(E) * 2 * I, H / 2, work, s)
               : launch_hw<true, false>(p, gu_q, int64_t(E) * 2 * I, H / 2, work, s);
@@ -580,6 +593,7 @@ int launch_hw_rows(const __half* act, int64_t act_stride, int K, const int32_t* 
   p.dense_rows = dense_rows; p.work_counter = counter; p.ws = ws; p.wz = wz; p.K = K;
   p.rows_per_expert = N; p.ng = ng; p.gs = gs; p.out = out; p.out_stride = out_stride;
   p.nslices = (N + hw::ROWS - 1) / hw::ROWS; p.err = err;
+  p.partial_last = (N % hw::ROWS) != 0 && p.nslices > 1;
   const int64_t work = max_tasks * p.nslices;
   return zint ? launch_hw<false, true>(p, wq, int64_t(E) * N, K / 2, work, s)
               : launch_hw<false, false>(p, wq, int64_t(E) * N, K / 2, work, s);
