@@ -234,6 +234,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (warp == WARP_WPROD) {
     // ---------------------------------------------------------------- scheduler + weights
     if (lane == 0) {
+      // the packed weights stream through once per task: evict them first, so that the
+      // intermediates (out2 for the down GEMM, out3 for the combine) stay in L2
+      const uint64_t wpol = l2_policy_evict_first();
       const int nwork = (p.tasks ? *p.ntasks : (p.dense_rows + TOK - 1) / TOK) * p.nslices;
       uint32_t wst = 0;            // stages issued
       uint32_t wsl = 0, wph = 0;   // next ring slot and its phase parity
@@ -307,12 +310,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const int x = st * WROW;
           if (GATED) {
             const int y = it.e * p.rows_per_expert + it.slice * GROWS;
-            tma_load_2d(dst, &wmap, &ctrl.w_full[s], x, y);
-            tma_load_2d(dst + BOX_ROWS * WROW, &wmap, &ctrl.w_full[s], x, y + p.I);
+            tma_load_2d_hint(dst, &wmap, &ctrl.w_full[s], x, y, wpol);
+            tma_load_2d_hint(dst + BOX_ROWS * WROW, &wmap, &ctrl.w_full[s], x, y + p.I, wpol);
           } else {
             const int y = it.e * p.rows_per_expert + it.slice * ROWS;
-            tma_load_2d(dst, &wmap, &ctrl.w_full[s], x, y);
-            tma_load_2d(dst + BOX_ROWS * WROW, &wmap, &ctrl.w_full[s], x, y + BOX_ROWS);
+            tma_load_2d_hint(dst, &wmap, &ctrl.w_full[s], x, y, wpol);
+            tma_load_2d_hint(dst + BOX_ROWS * WROW, &wmap, &ctrl.w_full[s], x, y + BOX_ROWS, wpol);
           }
         }
         if (*abort_flag) break;
