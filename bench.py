@@ -40,7 +40,7 @@ NSETS = 4
 GEMM1_KERNEL = {"tc": "tcp_gemm_kernel<1,0> (gate_up + GELU)",
                 "ws": "hw_gemm_kernel<1,0,4> (gate_up + GELU)",
                 "mma": "gateup_gelu_kernel"}
-GEMM1_NCU_TRAFFIC = {"tc": None, "ws": 288.256512e6 + 5.845248e6}
+GEMM1_NCU_TRAFFIC = {"tc": None, "ws": 302.873600e6 + 3.920896e6}
 
 
 def peaks():
