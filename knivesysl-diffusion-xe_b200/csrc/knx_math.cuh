@@ -111,4 +111,15 @@ __device__ __forceinline__ float div_rn_by(float x, float t, float r) {
   return __fmaf_rn(rem, r, q);
 }
 
+// The |x| range in which div_rn_by is the IEEE quotient for t > 0: x * r and x / t stay below
+// 3e38 (no overflow), and |x| >= 2^-100 * max(t, 1) keeps the quotient normal and the remainder
+// x - q*t (a multiple of 2^(e_x - 46)) representable.  Zeros, infinities, NaN and values outside
+// the range take the IEEE division itself (div_exact).
+__device__ __forceinline__ float div_fast_lo(float t) { return 0x1p-100f * fmaxf(t, 1.0f); }
+__device__ __forceinline__ float div_fast_hi(float t) { return 3.0e38f * fminf(t, 1.0f); }
+__device__ __forceinline__ float div_exact(float x, float t, float r, float lo, float hi) {
+  const float a = fabsf(x);
+  return (a >= lo && a <= hi) ? div_rn_by(x, t, r) : __fdiv_rn(x, t);
+}
+
 }  // namespace knx

@@ -81,6 +81,11 @@ KNX_DEVINL void arg_merge(float& v, int& i, float v2, int i2) {
   }
 }
 
+// Final index of a row.  A row with no element that could win (every q is -inf or NaN) keeps
+// index 0, as the reference's scan does: its running index starts at 0 and moves only on a
+// strict improvement of the running best (fused_sampler_ops.py:55-81).
+KNX_DEVINL int64_t row_index(int i) { return i == 0x7fffffff ? 0 : i; }
+
 KNX_DEVINL void row_key(int64_t seed, int seed_is32, int64_t row, uint32_t& k0, uint32_t& k1) {
   if (seed_is32) {
     // Triton passes a 32-bit seed as i32: seed + row wraps in i32, then sign-extends to u64.
@@ -103,6 +108,7 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
                    float* __restrict__ entropy, int64_t* __restrict__ samp,
                    int64_t* __restrict__ amax) {
   pdl_wait_trigger();
+  const float dlo = div_fast_lo(temp), dhi = div_fast_hi(temp);  // fast-division range
   __shared__ int s_item;
   __shared__ int s_last;
   __shared__ Part s_wpart[SP_WARPS];
@@ -160,7 +166,7 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         if (valid & (1u << i)) {
-          if (do_div) qv[i] = div_rn_by(qv[i], temp, rtemp);
+          if (do_div) qv[i] = div_exact(qv[i], temp, rtemp, dlo, dhi);
           if (qv[i] > tm) {
             tm = qv[i];
             ti = base + 128 * (i >> 2) + 4 * lane + (i & 3);
@@ -304,8 +310,8 @@ __global__ void __launch_bounds__(SP_THREADS, 3)
         arg_merge(acc.bg, acc.bgi, b.z, __float_as_int(b.y));
       }
       if (entropy) entropy[row] = log1pf(acc.s) - acc.t / (1.0f + acc.s);
-      if (amax) amax[row] = acc.bqi;
-      if (samp) samp[row] = acc.bgi;
+      if (amax) amax[row] = row_index(acc.bqi);
+      if (samp) samp[row] = row_index(acc.bgi);
     }
     __syncthreads();
   }
@@ -398,6 +404,7 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
                           const __nv_bfloat16* __restrict__ sc_prev,
                           const uint8_t* __restrict__ finished, int canvas_len) {
   pdl_wait_trigger();
+  const float dlo = div_fast_lo(temp), dhi = div_fast_hi(temp);  // fast-division range
   using namespace sm100;
   extern __shared__ uint8_t sx_raw[];
   __shared__ SxCtrl c;
@@ -596,15 +603,18 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
             }
           }
           if (do_div) {
-            float xabs = 0.f;
+            float xhi = 0.f, xlo = INFINITY;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) xabs = fmaxf(xabs, fabsf(q[i]));
-            if (__all_sync(0xffffffffu, xabs <= 3.0e38f)) {  // finite: Markstein = IEEE quotient
+            for (int i = 0; i < 16; ++i) {
+              xhi = fmaxf(xhi, fabsf(q[i]));
+              xlo = fminf(xlo, fabsf(q[i]));
+            }
+            if (__all_sync(0xffffffffu, xhi <= dhi && xlo >= dlo)) {  // Markstein = IEEE quotient
 #pragma unroll
               for (int i = 0; i < 16; ++i) q[i] = div_rn_by(q[i], temp, rtemp);
             } else {
 #pragma unroll
-              for (int i = 0; i < 16; ++i) q[i] = isfinite(q[i]) ? div_rn_by(q[i], temp, rtemp) : q[i] * rtemp;
+              for (int i = 0; i < 16; ++i) q[i] = div_exact(q[i], temp, rtemp, dlo, dhi);
             }
           }
           if constexpr (SC) {
@@ -780,8 +790,8 @@ __global__ void row_merge_kernel(const Part* __restrict__ parts, int64_t rows, i
     arg_merge(acc.bg, acc.bgi, p.bg, p.bgi);
   }
   if (entropy) entropy[row] = log1pf(acc.s) - acc.t / (1.0f + acc.s);
-  if (amax) amax[row] = acc.bqi;
-  if (samp) samp[row] = acc.bgi;
+  if (amax) amax[row] = row_index(acc.bqi);
+  if (samp) samp[row] = row_index(acc.bgi);
 }
 
 // ------------------------------------------------------------------------------------------

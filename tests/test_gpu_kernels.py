@@ -358,6 +358,42 @@ def test_sampler_full_size_properties(cuda):
     assert ((h.cpu().double() - rh).abs() <= 1e-4 * rh.abs() + 1e-7).all()
 
 
+@pytest.mark.parametrize("V,step", [(262144, 0), (262144, 30), (262144, 47), (4099, 30)])
+def test_sampler_masked_and_infinite_rows(cuda, V, step):
+    """Rows that bound or index handling could get wrong, on the streaming path (V = 262144) and
+    the generic one (V = 4099): masked (-inf) rows, a fully masked row (index 0, as the
+    reference's scan keeps its initial index), +inf entries (the first wins), NaN entries, a far
+    spike and ties."""
+    import fused_sampler_ops
+    import workloads
+    g = torch.Generator().manual_seed(step + 11)
+    x = torch.randn(8, V, generator=g) * 3.0
+    x[1][torch.rand(V, generator=g) < 0.99] = -float("inf")     # 99% masked
+    x[2][:] = -float("inf")
+    x[2][[5, (3 * V) // 4]] = torch.tensor([1.0, 2.0])           # two finite columns
+    x[3][[V // 250, V // 2 + 7]] = float("inf")                  # +inf twice: the first wins
+    x[4][:] = -float("inf")                                      # fully masked row
+    x[5][3] += 40.0                                              # one far spike
+    x[6][:] = 1.0                                                # all equal
+    x[7][[7, V // 3, V - 1]] = float("nan")
+    T = np.float32(workloads.temperature(step))
+    seed = workloads.step_seed(1234, step)
+    h, s, a = fused_sampler_ops.sample_step(x.to(cuda), seed, float(T))
+    rs, ra = ref.gumbel_argmax(x, seed, temperature=float(T))
+    assert np.array_equal(s.cpu().numpy(), rs.numpy())
+    assert np.array_equal(a.cpu().numpy(), ra.numpy())
+    assert s[3].item() == V // 250 and s[4].item() == 0 and a[4].item() == 0
+    # entropy of the finite entries (rows with -inf entries: the reference's x * e term is
+    # -inf * 0 = NaN there, this library leaves masked entries out of the sum)
+    q = x.double() / float(T)
+    for r in (0, 1, 2, 5, 6):
+        qr = q[r][torch.isfinite(q[r])]
+        p = torch.softmax(qr, 0)
+        want = -(p * torch.log_softmax(qr, 0)).sum().item()
+        assert abs(h[r].item() - want) <= 1e-4 * abs(want) + 1e-6, (r, h[r].item(), want)
+    assert h[4].item() == 0.0
+
+
 # ------------------------------------------------------------------------------ accept / stop
 @pytest.mark.parametrize("tag", ["a", "b", "c"])
 def test_accept_stop_vs_reference_golden(cuda, tag):
