@@ -343,20 +343,15 @@ constexpr int SX_CHUNK = 8 * SX_COLS;       // columns per work item
 constexpr int SX_RING = 4;
 constexpr int SX_WARPS = 16;                // math warps
 constexpr int SX_THREADS = (SX_WARPS + 3) * 32;
-// deferred Gumbel candidates per warp: flushed as soon as SX_FLUSH are pending, so a tile (at
-// most SP_TILE candidates) always fits on top of the at most SX_FLUSH - 1 left over
-#ifndef KNX_SX_FLUSH
-#define KNX_SX_FLUSH 32
-#endif
-constexpr int SX_FLUSH = KNX_SX_FLUSH;
-constexpr int SX_CQ = SP_TILE + SX_FLUSH;
 // Philox chains per lane in one pass over the deferred candidates (32 candidates each).  Two
-// beat four on B200 (8-10 us per step at T 0.4-0.6): with a flush every 32 candidates, most
-// of a four-chain pass would run on empty slots.
-#ifndef KNX_SX_CHAINS
-#define KNX_SX_CHAINS 2
-#endif
-constexpr int SX_CHAINS = KNX_SX_CHAINS;
+// beat four on B200 (8-10 us per step at T 0.4-0.6).
+constexpr int SX_CHAINS = 2;
+// Deferred Gumbel candidates per warp.  Once SX_FLUSH (one full pass) are pending, the whole
+// multiples of SX_FLUSH are evaluated and the rest stays for the next tile, so a tile (at most
+// SP_TILE candidates) always fits on top of the at most SX_FLUSH - 1 left over; the last flush
+// of an item takes everything.
+constexpr int SX_FLUSH = 32 * SX_CHAINS;
+constexpr int SX_CQ = SP_TILE + SX_FLUSH;
 constexpr size_t SX_SMEM = 128 + static_cast<size_t>(SX_RING) * SX_BYTES +
                            static_cast<size_t>(SX_WARPS) * SX_CQ * 8;
 
@@ -384,7 +379,6 @@ KNX_DEVINL int warp_min_i(int v) {
   for (int o = 16; o > 0; o >>= 1) v = min(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
-
 // bf16 bits of v rounded to nearest even; NaN -> 0x7FC0 (torch's float -> bfloat16 conversion)
 KNX_DEVINL uint32_t bf16_bits(float v) {
   return v != v ? 0x7FC0u : static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
@@ -526,15 +520,19 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
       float W = -INFINITY;  // best exact q + g known for the row (warp view)
       bool first = true;
       int nbuf = 0;         // deferred candidates in wcol/wq
-      // Evaluates the deferred candidates, 32 at a time.  Each is re-tested against the newest
-      // bound; its Philox word is then screened with the exact-safe test u >= e^(-e^(-y)) - 2e-6
-      // (y = best - q, u the clamped uniform; q + g(u) >= best needs u >= e^(-e^(-y)), and the
-      // approximate exponentials err by far less than the margin), and only survivors get the
-      // exact Gumbel value and enter the argmax.
-      auto flush = [&]() {
+      // Evaluates deferred candidates, 64 at a time (two Philox chains per lane): all of them on
+      // the item's last flush, else the whole multiples of 64, the rest moving to the front of
+      // the buffer.  Each is re-tested against the newest bound; its Philox word is then screened
+      // with the exact-safe test u >= e^(-e^(-y)) - 2e-6 (y = best - q, u the clamped uniform;
+      // q + g(u) >= best needs u >= e^(-e^(-y)), and the approximate exponentials err by far less
+      // than the margin), and only survivors get the exact Gumbel value and enter the argmax.  The
+      // test is written !(u < ...) so that y = inf - inf (a q = +inf candidate once the bound is
+      // +inf) keeps the candidate: of several +inf elements the first must still win.
+      auto flush = [&](bool last) {
         __syncwarp();
         const float thr_now = W - GUMBEL_MAX;
-        for (int i0 = 0; i0 < nbuf; i0 += 32 * SX_CHAINS) {
+        const int nproc = last ? nbuf : nbuf - nbuf % SX_FLUSH;
+        for (int i0 = 0; i0 < nproc; i0 += 32 * SX_CHAINS) {
           // SX_CHAINS independent Philox chains per lane (latency hiding), in column order
           uint32_t wv[SX_CHAINS];
           float qv[SX_CHAINS];
@@ -542,11 +540,11 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
 #pragma unroll
           for (int r = 0; r < SX_CHAINS; ++r) {
             const int i = i0 + 32 * r + lane;
-            qv[r] = i < nbuf ? __uint_as_float(lds32(wq + 4 * i)) : -INFINITY;
-            colv[r] = i < nbuf ? static_cast<int>(lds32(wcol + 4 * i)) : 0;
+            qv[r] = i < nproc ? __uint_as_float(lds32(wq + 4 * i)) : -INFINITY;
+            colv[r] = i < nproc ? static_cast<int>(lds32(wcol + 4 * i)) : 0;
           }
           if constexpr (SX_CHAINS == 2) {
-            if (nbuf - i0 > 32) {  // both chains hold candidates: one pass, key schedule once
+            if (nproc - i0 > 32) {  // both chains hold candidates: one pass, key schedule once
               philox_w0_x2(static_cast<uint32_t>(colv[0]), static_cast<uint32_t>(colv[1]), k0,
                            k1, wv[0], wv[1]);
             } else {
@@ -564,12 +562,32 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
               const float u = fminf(fmaxf(uint_to_uniform(wv[r]), 0x1.b7cdfep-34f), 0x1.fffffcp-1f);
               const float y = fmaxf(W, bg) - qv[r];
               const float umin = ex2(-ex2(-y * L) * L);
-              if (u >= umin - 2e-6f) arg_merge(bg, bgi, qv[r] + gumbel_from_word(wv[r]), colv[r]);
+              if (!(u < umin - 2e-6f)) arg_merge(bg, bgi, qv[r] + gumbel_from_word(wv[r]), colv[r]);
+            }
+          }
+        }
+        // the left-over (< SX_FLUSH) moves to the front: read both halves, then write
+        const int rem = nbuf - nproc;
+        if (rem > 0) {
+          uint32_t cc[2] = {0u, 0u}, qq[2] = {0u, 0u};
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            if (32 * r + lane < rem) {
+              cc[r] = lds32(wcol + 4 * (nproc + 32 * r + lane));
+              qq[r] = lds32(wq + 4 * (nproc + 32 * r + lane));
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            if (32 * r + lane < rem) {
+              sts32(wcol + 4 * (32 * r + lane), cc[r]);
+              sts32(wq + 4 * (32 * r + lane), qq[r]);
             }
           }
         }
         __syncwarp();
-        nbuf = 0;
+        nbuf = rem;
         const float wm = warp_max(bg);
         if (wm > W) {
           W = wm;
@@ -736,14 +754,14 @@ __global__ void __launch_bounds__(SX_THREADS, 1)
                 }
               }
               nbuf += total;
-              if (nbuf >= SX_FLUSH) flush();
+              if (nbuf >= SX_FLUSH) flush(false);
             }
           }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&c.empty[slot]);
       }
-      if (want_gumbel && nbuf > 0) flush();
+      if (want_gumbel && nbuf > 0) flush(true);
       // ---- item result: m and the argmax are warp-uniform; sp, t2 add up in a fixed tree
       float spw = sp, t2w = t2;
 #pragma unroll
