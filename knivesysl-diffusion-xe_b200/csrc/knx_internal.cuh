@@ -4,6 +4,19 @@
 
 namespace knx {
 
+// Position of channel n inside the MoE K-interleave of its 8-group (the layout the down GEMM
+// reads the gated intermediate in).
+KNX_DEVINL int perm_pos(int n) { return (n & ~7) + 2 * (n & 3) + ((n >> 2) & 1); }
+
+// tanh-form GELU of the gated epilogue, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
+// (fused_moe_w4_v2.py:136-138), with tanh(y) = 1 - 2 / (1 + e^(2y)) from the fast exponential
+// and division: ~1e-6 relative, far below the f16 rounding of GELU(gate) * up that follows.
+KNX_DEVINL float gelu_tanh(float x) {
+  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  const float th = 1.0f - __fdividef(2.0f, 1.0f + __expf(2.0f * inner));
+  return 0.5f * x * (1.0f + th);
+}
+
 constexpr int64_t ALIGN_MAX_PAIRS = 32768;  // single-CTA counting sort limit (pairs)
 constexpr int MAX_TASK_TOKENS = 128;        // largest task size the task-list builders accept
 constexpr int ALIGN_MAX_EXPERTS = 256;

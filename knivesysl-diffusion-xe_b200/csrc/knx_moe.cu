@@ -58,16 +58,6 @@ KNX_DEVINL void unpack_sz(uint2 v, __half2& s, __half2& s16, __half2& c, __half2
   c16 = __high2half2(u32_as_h2(v.y));
 }
 
-// position of channel n inside the MoE K-interleave of its 8-group
-KNX_DEVINL int perm_pos(int n) { return (n & ~7) + 2 * (n & 3) + ((n >> 2) & 1); }
-
-KNX_DEVINL float gelu_tanh(float x) {
-  // 0.5*x*(1 + tanh(sqrt(2/pi)*(x + 0.044715 x^3))), tanh(y) = 2/(1+exp(-2y)) - 1
-  // (fused_moe_w4_v2.py:136-138)
-  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  const float th = 2.0f / (1.0f + expf(-2.0f * inner)) - 1.0f;
-  return 0.5f * x * (1.0f + th);
-}
 
 // ------------------------------------------------------------------------------------------
 template <bool ZINT>

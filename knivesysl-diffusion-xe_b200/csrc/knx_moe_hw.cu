@@ -126,12 +126,6 @@ inline bool ring_depths(bool gated, int ng, int& sw, int& sa) {
   return false;
 }
 
-KNX_DEVINL float gelu_tanh(float x) {
-  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  const float th = 2.0f / (1.0f + expf(-2.0f * inner)) - 1.0f;
-  return 0.5f * x * (1.0f + th);
-}
-KNX_DEVINL int perm_pos(int n) { return (n & ~7) + 2 * (n & 3) + ((n >> 2) & 1); }
 
 // Dequant constants of one (row, group) as f16x2 broadcasts; the same values as make_sz (every
 // operation below is exact or a single rounding of the exact result).

@@ -131,11 +131,6 @@ static_assert(1024 + OFF_SZ + IR * 2 * NROWS * SZ_MAX_NG * 2 + EPI_WARPS * EPI_W
                   227 * 1024,
               "shared memory");
 
-KNX_DEVINL float gelu_tanh(float x) {
-  const float inner = 0.7978845608028654f * (x + 0.044715f * x * x * x);
-  const float th = 2.0f / (1.0f + expf(-2.0f * inner)) - 1.0f;
-  return 0.5f * x * (1.0f + th);
-}
 
 // f16x2 of two floats, low half = a
 KNX_DEVINL void cp_async16_s(uint32_t saddr, const void* gmem) {
