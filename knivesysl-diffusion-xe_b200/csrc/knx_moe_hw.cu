@@ -132,14 +132,14 @@ inline bool ring_depths(bool gated, int ng, int& sw, int& sa) {
 template <bool ZINT>
 KNX_DEVINL void group_consts(__half s, __half z, __half2& s2, __half2& s16, __half2& c2,
                              __half2& c16) {
-  const __half k16 = __ushort_as_half(0x4c00u), k1024 = __ushort_as_half(0x6400u);
-  const __half sh = __hmul(s, __ushort_as_half(0x2c00u));  // s / 16
-  const __half c = ZINT ? __hadd(z, k1024) : z;
-  const __half ch = ZINT ? __hfma(z, k16, k1024) : __hmul(z, k16);
+  // broadcast first, then one f16x2 operation per constant (each lane: the same single rounding)
+  const __half2 k16 = __half2half2(__ushort_as_half(0x4c00u));
+  const __half2 k1024 = __half2half2(__ushort_as_half(0x6400u));
   s2 = __half2half2(s);
-  s16 = __half2half2(sh);
-  c2 = __half2half2(c);
-  c16 = __half2half2(ch);
+  s16 = __hmul2(s2, __half2half2(__ushort_as_half(0x2c00u)));  // s / 16
+  const __half2 z2 = __half2half2(z);
+  c2 = ZINT ? __hadd2(z2, k1024) : z2;
+  c16 = ZINT ? __hfma2(z2, k16, k1024) : __hmul2(z2, k16);
 }
 
 // One stage (256 k) of one warp's m16 tile: 8 k32 steps (jmax in the K tail), NTT n8 token
