@@ -33,8 +33,9 @@ KNX_DEVINL void unpack8<__nv_bfloat16>(const uint4& v, float (&f)[8]) {
   }
 }
 
-// Eight weights starting at element 8v, as fp32 (WT = void: no weight, all ones).
-template <typename WT>
+// Eight weights starting at element 8v, as fp32 (WT = void: no weight, all ones).  WS: w points
+// to shared memory (a plain load instead of the read-only global path).
+template <typename WT, bool WS = false>
 KNX_DEVINL void load_w8(const void* w, int v, float (&f)[8]) {
   if constexpr (std::is_same<WT, void>::value) {
 #pragma unroll
@@ -43,6 +44,8 @@ KNX_DEVINL void load_w8(const void* w, int v, float (&f)[8]) {
     const float4* p = reinterpret_cast<const float4*>(w) + 2 * v;
     const float4 a = __ldg(p), b = __ldg(p + 1);
     f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else if constexpr (WS) {
+    unpack8<WT>(reinterpret_cast<const uint4*>(w)[v], f);
   } else {
     unpack8<WT>(__ldg(reinterpret_cast<const uint4*>(w) + v), f);
   }
@@ -61,7 +64,8 @@ KNX_DEVINL T from_f32(float v, bool round_bf16) {
 // One row: y = x * (1 / sqrt(sum(x^2) / cols + eps)) * w, optionally also the MoE K-interleaved
 // f16 copy p (xperm).  The row is read once with 16-byte loads and kept in registers (up to
 // RMS_MAX_VEC vectors per lane); wider rows are re-read for the second pass.  Returns 1/rms.
-template <typename T, typename WT>
+// WS: the weights are in shared memory (same arithmetic).
+template <typename T, typename WT, bool WS = false>
 KNX_DEVINL float rms_row(const T* __restrict__ xrow, const void* __restrict__ w,
                          T* __restrict__ yrow, __half* __restrict__ prow, int cols, float eps,
                          bool round_bf16, int lane) {
@@ -95,7 +99,7 @@ KNX_DEVINL float rms_row(const T* __restrict__ xrow, const void* __restrict__ w,
   auto emit = [&](int v, const uint4& c) {
     float f[8], wf[8];
     unpack8<T>(c, f);
-    load_w8<WT>(w, v, wf);
+    load_w8<WT, WS>(w, v, wf);
     T out[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {

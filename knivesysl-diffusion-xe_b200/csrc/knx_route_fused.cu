@@ -5,12 +5,12 @@
 // experts [64 eb, 64 eb + 64) over the K-split `split` (H/4 columns), exactly as
 // router_logits_kernel does (same 64-column chunks, same m16n8k16 sequence per output), so the
 // partials are the same numbers.  The steps:
-//   1. cp.async brings the split's K-slice of the 32 token rows and of the 64 expert rows
-//      (everything in flight at once);
+//   1. one 1-D bulk copy per row brings the split's K-slice of the 32 token rows and of the 64
+//      expert rows (96 copies in flight at once), and one more the norm weights;
 //   2. meanwhile each warp normalises whole rows with the RMSNorm row routine of
-//      rmsnorm_kernel (rms::rms_row: same loads, same summation order), writing y and the MoE
-//      K-interleaved copy, and publishes 1/rms in shared memory — the cluster's CTAs share the
-//      32 rows, 4 or 8 each;
+//      rmsnorm_kernel (rms::rms_row: same loads, same summation order; the weights from shared
+//      memory), writing y and the MoE K-interleaved copy, and publishes 1/rms in shared memory —
+//      the cluster's CTAs share the 32 rows, 4 or 8 each;
 //   3. after a cluster barrier every CTA reads the 32 values of 1/rms over distributed shared
 //      memory and normalises its K-slice in place with the same formula as the row routine;
 //   4. the MMAs produce the [32 x 64] partial tile (16 tokens x 16 experts per warp), kept in
@@ -24,6 +24,7 @@
 
 #include "knx_common.cuh"
 #include "knx_rms_row.cuh"
+#include "knx_sm100.cuh"
 #include "knx_topk.cuh"
 
 namespace cg = cooperative_groups;
@@ -34,15 +35,17 @@ namespace {
 constexpr int RF_TOK = 32;                        // tokens per cluster (8 clusters: one wave)
 constexpr int RF_EXP = 64;                        // experts per CTA
 constexpr int RF_KSPLIT = 4;                      // K-splits (= router_logits_kernel's)
-constexpr int RF_BK = 64;                         // k per chunk
-constexpr int RF_ROWB = RF_BK * 2 + 16;           // 144-byte padded rows (conflict-free u32 loads)
-constexpr int RF_CHUNK_BYTES = (RF_TOK + RF_EXP) * RF_ROWB;
+constexpr int RF_BK = 64;                         // k per MMA chunk
 constexpr int RF_THREADS = 256;                   // 8 warps
 constexpr int RF_MAX_CHUNKS = 15;                 // H <= 3840
-constexpr size_t rf_smem_bytes(int nchunk) {
-  return static_cast<size_t>(nchunk) * RF_CHUNK_BYTES + (RF_TOK * RF_EXP + 8 + RF_TOK + 8) * 4 +
-         static_cast<size_t>(nchunk) * RF_BK * 2;  // + the norm weights of the K-slice
-}
+constexpr int RF_ROWS = RF_TOK + RF_EXP;          // token rows, then expert rows, per CTA
+// A row's K-slice (H/4 f16) padded by 16 bytes: rows 4 banks apart, so the fragment loads of the
+// 8 row groups x 4 lanes hit 32 different banks.
+constexpr int rf_row_stride(int H) { return (H / RF_KSPLIT) * 2 + 16; }
+constexpr size_t rf_part_off(int H) { return static_cast<size_t>(RF_ROWS) * rf_row_stride(H); }
+constexpr size_t rf_nw_off(int H) { return rf_part_off(H) + (RF_TOK * RF_EXP + 8 + RF_TOK + 8) * 4; }
+constexpr size_t rf_bar_off(int H) { return rf_nw_off(H) + static_cast<size_t>(H) * 2; }
+constexpr size_t rf_smem_bytes(int H) { return rf_bar_off(H) + 16; }  // + two mbarriers
 
 __global__ void __launch_bounds__(RF_THREADS)
     route_fused_kernel(const __half* __restrict__ x, const __half* __restrict__ nw, float eps,
@@ -62,41 +65,47 @@ __global__ void __launch_bounds__(RF_THREADS)
   const int t0 = blockIdx.x * RF_TOK;
   const int kper = H / RF_KSPLIT, nchunk = kper / RF_BK, kbeg = split * kper;
   const int e0 = eb * RF_EXP;
-  uint8_t* slices = rf_smem;                                        // [nchunk][96 rows][144 B]
-  float* part = reinterpret_cast<float*>(rf_smem + nchunk * RF_CHUNK_BYTES);  // [32][64]
-  float* inv_pub = part + RF_TOK * RF_EXP;                          // [8] 1/rms of own rows
-  float* inv_all = inv_pub + 8;                                     // [32] the cluster's rows
-  uint8_t* nws = reinterpret_cast<uint8_t*>(inv_all + RF_TOK + 8); // [kper] norm weights, f16
+  const int RS = rf_row_stride(H);
+  uint8_t* slices = rf_smem;                                   // [96 rows][RS]: K-slice per row
+  float* part = reinterpret_cast<float*>(rf_smem + rf_part_off(H));  // [32][64]
+  float* inv_pub = part + RF_TOK * RF_EXP;                     // [8] 1/rms of own rows
+  float* inv_all = inv_pub + 8;                                // [32] the cluster's rows
+  __half* nwf = reinterpret_cast<__half*>(rf_smem + rf_nw_off(H));  // [H] norm weights
+  uint64_t* bar = reinterpret_cast<uint64_t*>(rf_smem + rf_bar_off(H));  // slices, norm weights
 
-  // 1. the K-slices (token rows first, then expert rows), all chunks in one cp.async group
-  for (int c = 0; c < nchunk; ++c) {
-    uint8_t* sl = slices + c * RF_CHUNK_BYTES;
-    const int k0 = kbeg + c * RF_BK;
-    for (int i = tid; i < (RF_TOK + RF_EXP) * 8; i += RF_THREADS) {
-      const int r = i >> 3, ch = i & 7;
-      const __half* src;
-      if (r < RF_TOK) {
-        const int t = t0 + r;
-        src = x + static_cast<int64_t>(t < T ? t : T - 1) * H + k0 + ch * 8;
-      } else {
-        src = wr + static_cast<int64_t>(e0 + r - RF_TOK) * H + k0 + ch * 8;
-      }
-      cp_async16(sl + r * RF_ROWB + ch * 16, src);
-    }
+  // 1. one bulk copy per row K-slice (token rows first, then expert rows) and one of the norm
+  //    weights, each group on its own mbarrier
+  if (tid == 0) {
+    sm100::mbar_init(&bar[0], 1);
+    sm100::mbar_init(&bar[1], 1);
+    sm100::fence_mbar_init();
+    sm100::mbar_arrive_expect_tx(&bar[0], static_cast<uint32_t>(RF_ROWS * kper * 2));
+    sm100::mbar_arrive_expect_tx(&bar[1], static_cast<uint32_t>(H * 2));
+    sm100::bulk_load(nwf, nw, static_cast<uint32_t>(H * 2), &bar[1]);
   }
-  for (int i = tid; i < kper / 8; i += RF_THREADS) cp_async16(nws + 16 * i, nw + kbeg + 8 * i);
-  cp_async_commit();
+  __syncthreads();
+  if (tid < RF_ROWS) {
+    const __half* src;
+    if (tid < RF_TOK) {
+      const int t = t0 + tid;
+      src = x + static_cast<int64_t>(t < T ? t : T - 1) * H + kbeg;
+    } else {
+      src = wr + static_cast<int64_t>(e0 + tid - RF_TOK) * H + kbeg;
+    }
+    sm100::bulk_load(slices + tid * RS, src, static_cast<uint32_t>(kper * 2), &bar[0]);
+  }
 
   // 2. RMSNorm of this CTA's rows of the cluster's 32 (whole rows, one warp per row)
   const int rpc = RF_TOK / csize;  // 4 or 8
+  if (warp < rpc) (void)sm100::mbar_wait(&bar[1], 0);  // norm weights in shared memory
   for (int r = warp; r < rpc; r += RF_THREADS / 32) {
     const int t = t0 + rank * rpc + r;
     float inv = 0.f;
     if (t < T)
-      inv = rms::rms_row<__half, __half>(x + static_cast<int64_t>(t) * H, nw,
-                                         y + static_cast<int64_t>(t) * H,
-                                         xperm ? xperm + static_cast<int64_t>(t) * H : nullptr,
-                                         H, eps, round_bf16, lane);
+      inv = rms::rms_row<__half, __half, true>(x + static_cast<int64_t>(t) * H, nwf,
+                                               y + static_cast<int64_t>(t) * H,
+                                               xperm ? xperm + static_cast<int64_t>(t) * H : nullptr,
+                                               H, eps, round_bf16, lane);
     if (lane == 0) inv_pub[r] = inv;
   }
   cluster.sync();  // 1/rms of every row of the cluster published
@@ -106,14 +115,17 @@ __global__ void __launch_bounds__(RF_THREADS)
     const float* src = cluster.map_shared_rank(inv_pub, tid / rpc);
     inv_all[tid] = src[tid % rpc];
   }
-  cp_async_wait<0>();
+  // a wait that ran out leaves the slices undefined but keeps every CTA on the cluster barriers
+  (void)sm100::mbar_wait(&bar[0], 0);
+  (void)sm100::mbar_wait(&bar[1], 0);
   __syncthreads();
-  for (int i = tid; i < nchunk * RF_TOK * 8; i += RF_THREADS) {
-    const int c = i / (RF_TOK * 8), rem = i - c * (RF_TOK * 8), r = rem >> 3, ch = rem & 7;
-    const uint32_t a = smem_u32(slices + c * RF_CHUNK_BYTES + r * RF_ROWB + ch * 16);
+  const int vpr = kper / 8;  // 16-byte vectors per row slice
+  for (int i = tid; i < RF_TOK * vpr; i += RF_THREADS) {
+    const int r = i / vpr, v = i - r * vpr;
+    const uint32_t a = smem_u32(slices + r * RS + v * 16);
     float f[8], wf[8];
     rms::unpack8<__half>(lds128(a), f);
-    rms::unpack8<__half>(lds128(smem_u32(nws) + 16u * (c * (RF_BK / 8) + ch)), wf);
+    rms::unpack8<__half>(lds128(smem_u32(nwf + kbeg) + 16u * v), wf);
     const float inv = inv_all[r];
     __half out[8];
 #pragma unroll
@@ -131,19 +143,19 @@ __global__ void __launch_bounds__(RF_THREADS)
   const int tm = 16 * (warp & 1), en = 16 * (warp >> 1);
   float acc[2][4] = {};
   for (int c = 0; c < nchunk; ++c) {
-    const uint32_t bx = smem_u32(slices + c * RF_CHUNK_BYTES);
-    const uint32_t bw = bx + RF_TOK * RF_ROWB;
+    const uint32_t bx = smem_u32(slices) + c * (RF_BK * 2);
+    const uint32_t bw = bx + RF_TOK * RS;
 #pragma unroll
     for (int ks = 0; ks < RF_BK / 16; ++ks) {
       const int kb = ks * 32 + q * 4;  // byte offset of k = 16*ks + 2q
-      const uint32_t a0 = lds32(bx + (tm + g) * RF_ROWB + kb);
-      const uint32_t a1 = lds32(bx + (tm + g + 8) * RF_ROWB + kb);
-      const uint32_t a2 = lds32(bx + (tm + g) * RF_ROWB + kb + 16);
-      const uint32_t a3 = lds32(bx + (tm + g + 8) * RF_ROWB + kb + 16);
+      const uint32_t a0 = lds32(bx + (tm + g) * RS + kb);
+      const uint32_t a1 = lds32(bx + (tm + g + 8) * RS + kb);
+      const uint32_t a2 = lds32(bx + (tm + g) * RS + kb + 16);
+      const uint32_t a3 = lds32(bx + (tm + g + 8) * RS + kb + 16);
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) {
-        const uint32_t b0 = lds32(bw + (en + 8 * nt + g) * RF_ROWB + kb);
-        const uint32_t b1 = lds32(bw + (en + 8 * nt + g) * RF_ROWB + kb + 16);
+        const uint32_t b0 = lds32(bw + (en + 8 * nt + g) * RS + kb);
+        const uint32_t b1 = lds32(bw + (en + 8 * nt + g) * RS + kb + 16);
         mma_16816(acc[nt], a0, a1, a2, a3, b0, b1);
       }
     }
@@ -197,15 +209,14 @@ extern "C" int knx_rmsnorm_router_topk(const void* x, const void* norm_w, float 
       (xperm && !aligned(xperm, 16)))
     return KNX_E_ALIGN;
   if (T == 0) return KNX_OK;
-  const int nchunk = static_cast<int>(H / RF_KSPLIT / RF_BK);
   if (set_max_dyn_smem(reinterpret_cast<const void*>(route_fused_kernel),
-                       static_cast<int>(rf_smem_bytes(RF_MAX_CHUNKS))) != KNX_OK)
+                       static_cast<int>(rf_smem_bytes(RF_MAX_CHUNKS * 256))) != KNX_OK)
     return KNX_E_DEVICE;
   const int neb = E / RF_EXP;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((T + RF_TOK - 1) / RF_TOK), neb, RF_KSPLIT);
   cfg.blockDim = dim3(RF_THREADS);
-  cfg.dynamicSmemBytes = rf_smem_bytes(nchunk);
+  cfg.dynamicSmemBytes = rf_smem_bytes(static_cast<int>(H));
   cfg.stream = static_cast<cudaStream_t>(stream);
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -8,9 +8,21 @@ namespace knx {
 constexpr int TK_MAXE = 256;  // experts at most
 constexpr int TK_PER = TK_MAXE / 32;
 
+// Order-preserving map of a non-NaN float to uint32 (larger float -> larger key), and back.
+KNX_DEVINL uint32_t tk_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+KNX_DEVINL float tk_unkey(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
 // l[i]: the logit of expert lane + 32 i (-inf for e >= E).  Top-k by logit, ties to the lower
 // expert id; weights are the selected softmax probabilities renormalised to sum 1.  Lane k < topk
-// writes selection k.
+// writes selection k.  Each selection round is two warp reductions (the largest key, then the
+// lowest expert id holding it); the probabilities of the k winners are then formed in parallel,
+// each as expf(l - max) / den, and summed in selection order (the arithmetic of a sequential
+// round-by-round evaluation, bit for bit).
 KNX_DEVINL void topk_select(const float (&l_in)[TK_PER], int E, int topk, int lane,
                             int32_t* __restrict__ ids_row, float* __restrict__ w_row) {
   constexpr int PER = TK_PER;
@@ -21,18 +33,15 @@ KNX_DEVINL void topk_select(const float (&l_in)[TK_PER], int E, int topk, int la
     l[i] = l_in[i];
     mx = fmaxf(mx, l[i]);
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  mx = tk_unkey(__reduce_max_sync(0xffffffffu, tk_key(fmaxf(mx, -INFINITY))));
   float den = 0.f;
 #pragma unroll
   for (int i = 0; i < PER; ++i) den += (lane + 32 * i < E) ? expf(l[i] - mx) : 0.f;
   den = warp_sum(den);
-  // top-k selection: k rounds of a warp-wide (max value, min index) reduction; lane k keeps
-  // selection k (topk <= 16), so nothing goes through local memory
-  float my_p = 0.f;
+  float my_v = -INFINITY;
   int my_i = 0;
-  float psum = 0.f;
   for (int k = 0; k < topk; ++k) {
+    // this lane's best: the lowest expert id among its largest values (never NaN)
     float bv = -INFINITY;
     int bi = 0x7fffffff;
 #pragma unroll
@@ -43,28 +52,24 @@ KNX_DEVINL void topk_select(const float (&l_in)[TK_PER], int E, int topk, int la
         bi = e;
       }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
+    const uint32_t key = tk_key(bv);
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+    const int win = static_cast<int>(
+        __reduce_min_sync(0xffffffffu, key == kmax ? static_cast<uint32_t>(bi) : 0xffffffffu));
 #pragma unroll
     for (int i = 0; i < PER; ++i)
-      if (lane + 32 * i == bi) l[i] = -INFINITY;  // remove the winner
-    const float p = expf(bv - mx) / den;
+      if (lane + 32 * i == win) l[i] = -INFINITY;  // remove the winner
     if (lane == k) {
-      my_p = p;
-      my_i = bi;
+      my_v = tk_unkey(kmax);
+      my_i = win;
     }
-    psum += p;
   }
+  const float p = lane < topk ? expf(my_v - mx) / den : 0.f;
+  float psum = 0.f;
+  for (int k = 0; k < topk; ++k) psum += __shfl_sync(0xffffffffu, p, k);
   if (lane < topk) {
     ids_row[lane] = my_i;
-    w_row[lane] = my_p / psum;
+    w_row[lane] = p / psum;
   }
 }
 
