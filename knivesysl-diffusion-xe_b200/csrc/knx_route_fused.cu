@@ -22,6 +22,8 @@
 // knx_router_topk.  A third cluster barrier keeps every CTA's tile alive until all reads are done.
 #include <cooperative_groups.h>
 
+#include <type_traits>
+
 #include "knx_common.cuh"
 #include "knx_rms_row.cuh"
 #include "knx_sm100.cuh"
@@ -47,6 +49,8 @@ constexpr size_t rf_nw_off(int H) { return rf_part_off(H) + (RF_TOK * RF_EXP + 8
 constexpr size_t rf_bar_off(int H) { return rf_nw_off(H) + static_cast<size_t>(H) * 2; }
 constexpr size_t rf_smem_bytes(int H) { return rf_bar_off(H) + 16; }  // + two mbarriers
 
+// NEB: expert blocks of 64 (E = 64 NEB).
+template <int NEB>
 __global__ void __launch_bounds__(RF_THREADS)
     route_fused_kernel(const __half* __restrict__ x, const __half* __restrict__ nw, float eps,
                        bool round_bf16, const __half* __restrict__ wr, const float* __restrict__ bias, int T, int H,
@@ -58,7 +62,8 @@ __global__ void __launch_bounds__(RF_THREADS)
   extern __shared__ __align__(16) uint8_t rf_smem[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int g = lane >> 2, q = lane & 3;
-  const int neb = E / RF_EXP;          // expert blocks (the cluster's y extent)
+  constexpr int neb = NEB;             // expert blocks (the cluster's y extent)
+  constexpr int PER = 2 * NEB;         // logits per lane in the top-k
   const int csize = neb * RF_KSPLIT;   // CTAs per cluster
   const int rank = static_cast<int>(cluster.block_rank());  // = eb + neb * split
   const int eb = blockIdx.y, split = blockIdx.z;
@@ -120,22 +125,37 @@ __global__ void __launch_bounds__(RF_THREADS)
   (void)sm100::mbar_wait(&bar[1], 0);
   __syncthreads();
   const int vpr = kper / 8;  // 16-byte vectors per row slice
-  for (int i = tid; i < RF_TOK * vpr; i += RF_THREADS) {
-    const int r = i / vpr, v = i - r * vpr;
-    const uint32_t a = smem_u32(slices + r * RS + v * 16);
-    float f[8], wf[8];
-    rms::unpack8<__half>(lds128(a), f);
-    rms::unpack8<__half>(lds128(smem_u32(nwf + kbeg) + 16u * v), wf);
-    const float inv = inv_all[r];
-    __half out[8];
+  // thread i of the CTA takes vectors i, i + 256, ... of the 32 x vpr: (row, vector) advanced
+  // incrementally; the bf16 rounding flag is folded at compile time
+  auto normalise = [&](auto rb) {
+    constexpr bool RB = decltype(rb)::value;
+    const int dr = RF_THREADS / vpr, dv = RF_THREADS - dr * vpr;
+    int r = tid / vpr, v = tid - r * vpr;
+    const uint32_t wbase = smem_u32(nwf + kbeg);
+    while (r < RF_TOK) {
+      const uint32_t a = smem_u32(slices + r * RS + v * 16);
+      float f[8], wf[8];
+      rms::unpack8<__half>(lds128(a), f);
+      rms::unpack8<__half>(lds128(wbase + 16u * v), wf);
+      const float inv = inv_all[r];
+      __half out[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
-      out[j] = rms::from_f32<__half>(__fmul_rn(__fmul_rn(f[j], inv), wf[j]), round_bf16);
-    const uint4 o = *reinterpret_cast<const uint4*>(out);
-    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(o.x), "r"(o.y), "r"(o.z),
-                 "r"(o.w)
-                 : "memory");
-  }
+      for (int j = 0; j < 8; ++j)
+        out[j] = rms::from_f32<__half>(__fmul_rn(__fmul_rn(f[j], inv), wf[j]), RB);
+      const uint4 o = *reinterpret_cast<const uint4*>(out);
+      asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(o.x), "r"(o.y), "r"(o.z),
+                   "r"(o.w)
+                   : "memory");
+      v += dv;
+      r += dr;
+      if (v >= vpr) {
+        v -= vpr;
+        ++r;
+      }
+    }
+  };
+  if (round_bf16) normalise(std::true_type{});
+  else normalise(std::false_type{});
   __syncthreads();
 
   // 4. partial logits of this K-split: warp w takes tokens [16 (w & 1), +16) (one m16 tile) and
@@ -174,23 +194,43 @@ __global__ void __launch_bounds__(RF_THREADS)
   for (int j = rank * rpc + warp; j < (rank + 1) * rpc; j += RF_THREADS / 32) {
     const int t = t0 + j;
     if (t >= T) continue;  // warp-uniform
+    // every partial (and bias) load first, all in flight together; then the sums in split order
+    float pv[PER][RF_KSPLIT], bv[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E) {
+        const int ebk = e / RF_EXP, el = e - ebk * RF_EXP;
+#pragma unroll
+        for (int s = 0; s < RF_KSPLIT; ++s)
+          pv[i][s] = cluster.map_shared_rank(part, ebk + neb * s)[j * RF_EXP + el];
+        bv[i] = bias ? bias[e] : 0.f;
+      }
+    }
     float l[TK_PER];
 #pragma unroll
     for (int i = 0; i < TK_PER; ++i) {
       const int e = lane + 32 * i;
       float v = -INFINITY;
+      if (i >= PER) {  // experts past E
+        l[i] = v;
+        continue;
+      }
       if (e < E) {
-        const int ebk = e / RF_EXP, el = e - ebk * RF_EXP;
         v = 0.f;
-        for (int s = 0; s < RF_KSPLIT; ++s)
-          v += cluster.map_shared_rank(part, ebk + neb * s)[j * RF_EXP + el];
-        if (bias) v += bias[e];
+#pragma unroll
+        for (int s = 0; s < RF_KSPLIT; ++s) v += pv[i][s];
+        if (bias) v += bv[i];
         if (logits_out) logits_out[static_cast<int64_t>(t) * E + e] = v;
       }
       l[i] = v;
     }
-    topk_select(l, E, topk, lane, ids + static_cast<int64_t>(t) * topk,
-                weights + static_cast<int64_t>(t) * topk);
+    if (topk == 8)
+      topk_select_t<PER, 8>(l, E, topk, lane, ids + static_cast<int64_t>(t) * topk,
+                            weights + static_cast<int64_t>(t) * topk);
+    else
+      topk_select_t<PER, 0>(l, E, topk, lane, ids + static_cast<int64_t>(t) * topk,
+                            weights + static_cast<int64_t>(t) * topk);
   }
   cluster.sync();  // no CTA leaves while another still reads its tile
 }
@@ -209,10 +249,11 @@ extern "C" int knx_rmsnorm_router_topk(const void* x, const void* norm_w, float 
       (xperm && !aligned(xperm, 16)))
     return KNX_E_ALIGN;
   if (T == 0) return KNX_OK;
-  if (set_max_dyn_smem(reinterpret_cast<const void*>(route_fused_kernel),
+  const int neb = E / RF_EXP;
+  auto kern = neb == 1 ? route_fused_kernel<1> : route_fused_kernel<2>;
+  if (set_max_dyn_smem(reinterpret_cast<const void*>(kern),
                        static_cast<int>(rf_smem_bytes(RF_MAX_CHUNKS * 256))) != KNX_OK)
     return KNX_E_DEVICE;
-  const int neb = E / RF_EXP;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>((T + RF_TOK - 1) / RF_TOK), neb, RF_KSPLIT);
   cfg.blockDim = dim3(RF_THREADS);
@@ -227,7 +268,7 @@ extern "C" int knx_rmsnorm_router_topk(const void* x, const void* norm_w, float 
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 2;
-  if (cudaLaunchKernelEx(&cfg, route_fused_kernel, static_cast<const __half*>(x),
+  if (cudaLaunchKernelEx(&cfg, kern, static_cast<const __half*>(x),
                          static_cast<const __half*>(norm_w), eps,
                          (flags & KNX_RMS_ROUND_BF16) != 0, static_cast<const __half*>(wr),
                          bias, static_cast<int>(T), static_cast<int>(H), E, topk,

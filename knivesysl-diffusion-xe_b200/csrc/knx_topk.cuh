@@ -23,9 +23,14 @@ KNX_DEVINL float tk_unkey(uint32_t k) {
 // lowest expert id holding it); the probabilities of the k winners are then formed in parallel,
 // each as expf(l - max) / den, and summed in selection order (the arithmetic of a sequential
 // round-by-round evaluation, bit for bit).
-KNX_DEVINL void topk_select(const float (&l_in)[TK_PER], int E, int topk, int lane,
-                            int32_t* __restrict__ ids_row, float* __restrict__ w_row) {
-  constexpr int PER = TK_PER;
+// PER: logits per lane that can be valid (32 * PER >= E; the entries past it are -inf and add
+// exact zeros), TOPK: topk at compile time (0: the runtime value).  Every instantiation gives the
+// same bits for the same inputs.
+template <int PER, int TOPK>
+KNX_DEVINL void topk_select_t(const float (&l_in)[TK_PER], int E, int topk_rt, int lane,
+                              int32_t* __restrict__ ids_row, float* __restrict__ w_row) {
+  static_assert(PER <= TK_PER, "logits per lane");
+  const int topk = TOPK > 0 ? TOPK : topk_rt;
   float l[PER];
   float mx = -INFINITY;
 #pragma unroll
@@ -40,7 +45,8 @@ KNX_DEVINL void topk_select(const float (&l_in)[TK_PER], int E, int topk, int la
   den = warp_sum(den);
   float my_v = -INFINITY;
   int my_i = 0;
-  for (int k = 0; k < topk; ++k) {
+#pragma unroll
+  for (int k = 0; k < (TOPK > 0 ? TOPK : topk); ++k) {
     // this lane's best: the lowest expert id among its largest values (never NaN)
     float bv = -INFINITY;
     int bi = 0x7fffffff;
@@ -66,10 +72,28 @@ KNX_DEVINL void topk_select(const float (&l_in)[TK_PER], int E, int topk, int la
   }
   const float p = lane < topk ? expf(my_v - mx) / den : 0.f;
   float psum = 0.f;
-  for (int k = 0; k < topk; ++k) psum += __shfl_sync(0xffffffffu, p, k);
+#pragma unroll
+  for (int k = 0; k < (TOPK > 0 ? TOPK : topk); ++k) psum += __shfl_sync(0xffffffffu, p, k);
   if (lane < topk) {
     ids_row[lane] = my_i;
     w_row[lane] = p / psum;
+  }
+}
+
+
+// The routine for E experts (<= 256) and topk (<= 16): specialised for 8 selections and for the
+// logits per lane that E needs.
+KNX_DEVINL void topk_select(const float (&l)[TK_PER], int E, int topk, int lane,
+                            int32_t* __restrict__ ids_row, float* __restrict__ w_row) {
+  const int per = (E + 31) / 32;
+  if (topk == 8) {
+    if (per <= 2) topk_select_t<2, 8>(l, E, topk, lane, ids_row, w_row);
+    else if (per <= 4) topk_select_t<4, 8>(l, E, topk, lane, ids_row, w_row);
+    else topk_select_t<8, 8>(l, E, topk, lane, ids_row, w_row);
+  } else {
+    if (per <= 2) topk_select_t<2, 0>(l, E, topk, lane, ids_row, w_row);
+    else if (per <= 4) topk_select_t<4, 0>(l, E, topk, lane, ids_row, w_row);
+    else topk_select_t<8, 0>(l, E, topk, lane, ids_row, w_row);
   }
 }
 
