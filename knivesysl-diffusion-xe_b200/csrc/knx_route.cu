@@ -80,7 +80,9 @@ __global__ void __launch_bounds__(128)
 
   // warp tile: tokens [16*(warp&1), +16) as MMA rows, experts [16*(warp>>1), +16) as 2 n8 tiles
   const int tm = 16 * (warp & 1), en = 16 * (warp >> 1);
-  float acc[2][4] = {};
+  // two accumulator sets (even / odd k16 steps), added once at the end: half the dependent
+  // MMA chain; the fused and the standalone router use the same order
+  float acc[2][2][4] = {};
   int issued = 0;
   for (; issued < ring; ++issued) load(issued);
   for (int c = 0; c < nchunk; ++c) {
@@ -99,7 +101,7 @@ __global__ void __launch_bounds__(128)
       for (int nt = 0; nt < 2; ++nt) {
         const uint32_t b0 = lds32(bw + (en + 8 * nt + g) * RT_ROWB + kb);
         const uint32_t b1 = lds32(bw + (en + 8 * nt + g) * RT_ROWB + kb + 16);
-        mma_16816(acc[nt], a0, a1, a2, a3, b0, b1);
+        mma_16816(acc[nt][ks & 1], a0, a1, a2, a3, b0, b1);
       }
     }
     __syncthreads();  // every warp is done with the slot before it is refilled
@@ -111,12 +113,12 @@ __global__ void __launch_bounds__(128)
     const int e = e0 + en + 8 * nt + 2 * q;
     const int ta = t0 + tm + g, tb = ta + 8;
     if (ta < T) {
-      out[static_cast<int64_t>(ta) * E + e] = acc[nt][0];
-      out[static_cast<int64_t>(ta) * E + e + 1] = acc[nt][1];
+      out[static_cast<int64_t>(ta) * E + e] = acc[nt][0][0] + acc[nt][1][0];
+      out[static_cast<int64_t>(ta) * E + e + 1] = acc[nt][0][1] + acc[nt][1][1];
     }
     if (tb < T) {
-      out[static_cast<int64_t>(tb) * E + e] = acc[nt][2];
-      out[static_cast<int64_t>(tb) * E + e + 1] = acc[nt][3];
+      out[static_cast<int64_t>(tb) * E + e] = acc[nt][0][2] + acc[nt][1][2];
+      out[static_cast<int64_t>(tb) * E + e + 1] = acc[nt][0][3] + acc[nt][1][3];
     }
   }
 }

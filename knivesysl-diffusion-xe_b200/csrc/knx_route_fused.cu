@@ -89,15 +89,17 @@ __global__ void __launch_bounds__(RF_THREADS)
     sm100::bulk_load(nwf, nw, static_cast<uint32_t>(H * 2), &bar[1]);
   }
   __syncthreads();
-  if (tid < RF_ROWS) {
+  // issued by warps 4-7, which have no RMSNorm row: warps 0-3 start their rows at once
+  if (tid >= RF_THREADS / 2 && tid < RF_THREADS / 2 + RF_ROWS) {
+    const int r = tid - RF_THREADS / 2;
     const __half* src;
-    if (tid < RF_TOK) {
-      const int t = t0 + tid;
+    if (r < RF_TOK) {
+      const int t = t0 + r;
       src = x + static_cast<int64_t>(t < T ? t : T - 1) * H + kbeg;
     } else {
-      src = wr + static_cast<int64_t>(e0 + tid - RF_TOK) * H + kbeg;
+      src = wr + static_cast<int64_t>(e0 + r - RF_TOK) * H + kbeg;
     }
-    sm100::bulk_load(slices + tid * RS, src, static_cast<uint32_t>(kper * 2), &bar[0]);
+    sm100::bulk_load(slices + r * RS, src, static_cast<uint32_t>(kper * 2), &bar[0]);
   }
 
   // 2. RMSNorm of this CTA's rows of the cluster's 32 (whole rows, one warp per row)
@@ -130,14 +132,19 @@ __global__ void __launch_bounds__(RF_THREADS)
   auto normalise = [&](auto rb) {
     constexpr bool RB = decltype(rb)::value;
     const int dr = RF_THREADS / vpr, dv = RF_THREADS - dr * vpr;
-    int r = tid / vpr, v = tid - r * vpr;
     const uint32_t wbase = smem_u32(nwf + kbeg);
-    while (r < RF_TOK) {
-      const uint32_t a = smem_u32(slices + r * RS + v * 16);
+    auto advance = [&](int& r, int& v) {
+      v += dv;
+      r += dr;
+      if (v >= vpr) {
+        v -= vpr;
+        ++r;
+      }
+    };
+    auto emit = [&](uint32_t a, const uint4& xv, const uint4& wv, float inv) {
       float f[8], wf[8];
-      rms::unpack8<__half>(lds128(a), f);
-      rms::unpack8<__half>(lds128(wbase + 16u * v), wf);
-      const float inv = inv_all[r];
+      rms::unpack8<__half>(xv, f);
+      rms::unpack8<__half>(wv, wf);
       __half out[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j)
@@ -146,12 +153,27 @@ __global__ void __launch_bounds__(RF_THREADS)
       asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(o.x), "r"(o.y), "r"(o.z),
                    "r"(o.w)
                    : "memory");
-      v += dv;
-      r += dr;
-      if (v >= vpr) {
-        v -= vpr;
-        ++r;
+    };
+    int r = tid / vpr, v = tid - r * vpr;
+    // two vectors per pass: both loads are issued before either store
+    while (r < RF_TOK) {
+      int r2 = r, v2 = v;
+      advance(r2, v2);
+      const uint32_t a1 = smem_u32(slices + r * RS + v * 16);
+      const uint4 x1 = lds128(a1), w1 = lds128(wbase + 16u * v);
+      const float i1 = inv_all[r];
+      if (r2 < RF_TOK) {
+        const uint32_t a2 = smem_u32(slices + r2 * RS + v2 * 16);
+        const uint4 x2 = lds128(a2), w2 = lds128(wbase + 16u * v2);
+        const float i2 = inv_all[r2];
+        emit(a1, x1, w1, i1);
+        emit(a2, x2, w2, i2);
+      } else {
+        emit(a1, x1, w1, i1);
       }
+      r = r2;
+      v = v2;
+      advance(r, v);
     }
   };
   if (round_bf16) normalise(std::true_type{});
@@ -161,7 +183,9 @@ __global__ void __launch_bounds__(RF_THREADS)
   // 4. partial logits of this K-split: warp w takes tokens [16 (w & 1), +16) (one m16 tile) and
   //    experts [16 (w >> 1), +16) (two n8 tiles)
   const int tm = 16 * (warp & 1), en = 16 * (warp >> 1);
-  float acc[2][4] = {};
+  // two accumulator sets (even / odd k16 steps), added once at the end: half the dependent
+  // MMA chain; the fused and the standalone router use the same order
+  float acc[2][2][4] = {};
   for (int c = 0; c < nchunk; ++c) {
     const uint32_t bx = smem_u32(slices) + c * (RF_BK * 2);
     const uint32_t bw = bx + RF_TOK * RS;
@@ -176,17 +200,17 @@ __global__ void __launch_bounds__(RF_THREADS)
       for (int nt = 0; nt < 2; ++nt) {
         const uint32_t b0 = lds32(bw + (en + 8 * nt + g) * RS + kb);
         const uint32_t b1 = lds32(bw + (en + 8 * nt + g) * RS + kb + 16);
-        mma_16816(acc[nt], a0, a1, a2, a3, b0, b1);
+        mma_16816(acc[nt][ks & 1], a0, a1, a2, a3, b0, b1);
       }
     }
   }
 #pragma unroll
   for (int nt = 0; nt < 2; ++nt) {
     const int e = en + 8 * nt + 2 * q;
-    part[(tm + g) * RF_EXP + e] = acc[nt][0];
-    part[(tm + g) * RF_EXP + e + 1] = acc[nt][1];
-    part[(tm + g + 8) * RF_EXP + e] = acc[nt][2];
-    part[(tm + g + 8) * RF_EXP + e + 1] = acc[nt][3];
+    part[(tm + g) * RF_EXP + e] = acc[nt][0][0] + acc[nt][1][0];
+    part[(tm + g) * RF_EXP + e + 1] = acc[nt][0][1] + acc[nt][1][1];
+    part[(tm + g + 8) * RF_EXP + e] = acc[nt][0][2] + acc[nt][1][2];
+    part[(tm + g + 8) * RF_EXP + e + 1] = acc[nt][0][3] + acc[nt][1][3];
   }
   cluster.sync();  // every partial tile of the cluster complete
 
