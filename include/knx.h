@@ -211,7 +211,12 @@ KNX_API int knx_moe_combine(const void* out3, const int32_t* inv, const void* to
  *                        T*topk: slots beyond offsets[E] are skipped).
  *   knx_ep_p2p_barrier   a barrier.
  *   knx_ep_p2p_return    result rows out3 [r_cap][H] (local, expert-major) into the sources'
- *                        return rows at their align slots (for knx_moe_combine there). */
+ *                        return rows at their align slots (for knx_moe_combine there).
+ *   knx_ep_p2p_dispatch_barrier, knx_ep_p2p_return_barrier
+ *                        dispatch (return) followed by the barrier in one launch: the CTA that
+ *                        finishes last runs the barrier.  arrive: one device uint32 per entry
+ *                        point, zero before the first call, owned by this rank (left at zero
+ *                        after every call).  Every rank takes the barrier even with no rows. */
 KNX_API size_t knx_ep_p2p_plan_ints(int E, int El, int world);
 KNX_API int knx_ep_p2p_counts(const int32_t* counts, int E, int El, int rank, int world,
                               int32_t* const* peer_cnt, uint32_t* const* peer_flags,
@@ -219,6 +224,16 @@ KNX_API int knx_ep_p2p_counts(const int32_t* counts, int E, int El, int rank, in
 KNX_API int knx_ep_p2p_dispatch(const void* xp, int64_t H, int topk, const int32_t* sorted_pair,
                                 const int32_t* offsets, int E, int El, const int32_t* plan,
                                 void* const* peer_rows, int64_t n_cap, void* stream);
+KNX_API int knx_ep_p2p_dispatch_barrier(const void* xp, int64_t H, int topk,
+                                        const int32_t* sorted_pair, const int32_t* offsets, int E,
+                                        int El, const int32_t* plan, void* const* peer_rows,
+                                        int64_t n_cap, uint32_t* const* peer_flags, int rank,
+                                        int world, uint32_t epoch, uint32_t* arrive, int32_t* err,
+                                        void* stream);
+KNX_API int knx_ep_p2p_return_barrier(const void* out3, int64_t H, int El, int world, int E,
+                                      const int32_t* plan, void* const* peer_ret, int64_t r_cap,
+                                      uint32_t* const* peer_flags, int rank, uint32_t epoch,
+                                      uint32_t* arrive, int32_t* err, void* stream);
 KNX_API int knx_ep_p2p_barrier(uint32_t* const* peer_flags, int rank, int world, uint32_t epoch,
                                int32_t* err, void* stream);
 KNX_API int knx_ep_p2p_return(const void* out3, int64_t H, int El, int world, int E,

@@ -203,6 +203,94 @@ __global__ void __launch_bounds__(256)
   cta_fence_system();
 }
 
+// Dispatch, then the barrier, in one launch.  Warps take the slots in a grid-stride loop (the
+// expert of a slot by binary search over the offsets staged in shared memory); every CTA orders
+// its peer stores before one system-scope fence and then counts itself in `arrive`; the CTA that
+// arrives last resets the counter and runs the epoch barrier.  A CTA's fence precedes its
+// increment, and the last CTA fences again after reading the full count, so every CTA's stores
+// are ordered before the release stores of the epoch (fence-to-fence synchronisation through the
+// counter).
+__global__ void __launch_bounds__(256)
+    p2p_dispatch_bar_kernel(const uint4* __restrict__ xp, int vpr, int topk,
+                            const int32_t* __restrict__ sorted_pair,
+                            const int32_t* __restrict__ offsets, int E, int El,
+                            const int32_t* __restrict__ plan, uint4* const* __restrict__ peer_rows,
+                            int64_t n_cap, uint32_t* const* __restrict__ peer_flags, int rank,
+                            int world, uint32_t epoch, uint32_t* __restrict__ arrive,
+                            int32_t* __restrict__ err) {
+  pdl_wait_trigger();
+  __shared__ int s_off[P2P_MAX_E + 1];
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) s_off[i] = offsets[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+  const int64_t nslots = min(n_cap, static_cast<int64_t>(s_off[E]));
+  const int64_t step = static_cast<int64_t>(gridDim.x) * wpb;
+  for (int64_t j = blockIdx.x * static_cast<int64_t>(wpb) + (threadIdx.x >> 5); j < nslots;
+       j += step) {
+    int lo = 0, hi = E - 1;  // the expert of slot j: last e with offsets[e] <= j
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_off[mid] <= j) lo = mid; else hi = mid - 1;
+    }
+    const int e = lo, r = e % (E / El);  // owner: round-robin sharding
+    if (plan[e] >= 0) {                  // plan[e] < 0: the counts barrier gave up (empty plan)
+      const int64_t dst = plan[e] + (j - s_off[e]);
+      const uint4* src = xp + static_cast<int64_t>(sorted_pair[j] / topk) * vpr;
+      uint4* d = peer_rows[r] + dst * vpr;
+      for (int v = lane; v < vpr; v += 32) d[v] = ldg_nc_v4(src + v);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(arrive, 1u) == gridDim.x - 1) {
+      *arrive = 0u;  // the next launch starts after this kernel has completed
+      p2p_barrier(peer_flags, rank, world, epoch, err);
+    }
+  }
+}
+
+// Return, then the barrier, in one launch (the same pattern as p2p_dispatch_bar_kernel; the
+// segment of a local row by binary search over the segment starts staged in shared memory).
+__global__ void __launch_bounds__(256)
+    p2p_return_bar_kernel(const uint4* __restrict__ out3, int vpr, int El, int world,
+                          const int32_t* __restrict__ plan, int E,
+                          uint4* const* __restrict__ peer_ret, int64_t r_cap,
+                          uint32_t* const* __restrict__ peer_flags, int rank, uint32_t epoch,
+                          uint32_t* __restrict__ arrive, int32_t* __restrict__ err) {
+  pdl_wait_trigger();
+  __shared__ int s_seg[P2P_MAX_E + 1];
+  const int32_t* seg_start = plan + E + El + 1;
+  const int32_t* src_base = seg_start + El * world + 1;
+  const int nseg = El * world;
+  for (int i = threadIdx.x; i <= nseg; i += blockDim.x) s_seg[i] = seg_start[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+  const int64_t nrows = min(r_cap, static_cast<int64_t>(s_seg[nseg]));
+  const int64_t step = static_cast<int64_t>(gridDim.x) * wpb;
+  for (int64_t j = blockIdx.x * static_cast<int64_t>(wpb) + (threadIdx.x >> 5); j < nrows;
+       j += step) {
+    int lo = 0, hi = nseg - 1;  // last segment (el, s) starting at or before j
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_seg[mid] <= j) lo = mid; else hi = mid - 1;
+    }
+    const int s = lo % world;
+    const int64_t dst = src_base[lo] + (j - s_seg[lo]);
+    const uint4* src = out3 + j * vpr;
+    uint4* d = peer_ret[s] + dst * vpr;
+    for (int v = lane; v < vpr; v += 32) d[v] = ldg_nc_v4(src + v);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    if (atomicAdd(arrive, 1u) == gridDim.x - 1) {
+      *arrive = 0u;
+      p2p_barrier(peer_flags, rank, world, epoch, err);
+    }
+  }
+}
+
 __global__ void p2p_barrier_kernel(uint32_t* const* __restrict__ peer_flags, int rank, int world,
                                    uint32_t epoch, int32_t* __restrict__ err) {
   pdl_wait_trigger();
@@ -257,6 +345,52 @@ extern "C" int knx_ep_p2p_return(const void* out3, int64_t H, int El, int world,
                    static_cast<cudaStream_t>(stream), static_cast<const uint4*>(out3),
                    static_cast<int>(H / 8), El, world, plan, E,
                    reinterpret_cast<uint4* const*>(peer_ret), r_cap);
+  return launch_status();
+}
+
+// Copy grid of the fused exchange kernels: enough warps for the rows, at most two CTAs per SM.
+static unsigned p2p_grid(int64_t rows) {
+  const int64_t need = (rows + 7) / 8;
+  const int64_t cap = 2 * static_cast<int64_t>(knx::num_sms());
+  return static_cast<unsigned>(need < cap ? (need > 0 ? need : 1) : cap);
+}
+
+extern "C" int knx_ep_p2p_dispatch_barrier(const void* xp, int64_t H, int topk,
+                                           const int32_t* sorted_pair, const int32_t* offsets,
+                                           int E, int El, const int32_t* plan,
+                                           void* const* peer_rows, int64_t n_cap,
+                                           uint32_t* const* peer_flags, int rank, int world,
+                                           uint32_t epoch, uint32_t* arrive, int32_t* err,
+                                           void* stream) {
+  using namespace knx;
+  if (H <= 0 || (H % 8) != 0 || topk < 1 || E < 1 || E > P2P_MAX_E || El < 1 || n_cap < 0 ||
+      world < 1 || world > P2P_MAX_WORLD || rank < 0 || rank >= world || arrive == nullptr)
+    return KNX_E_INVALID;
+  if (!aligned(xp, 16)) return KNX_E_ALIGN;
+  (void)launch_pdl(p2p_dispatch_bar_kernel, p2p_grid(n_cap), 256, 0,
+                   static_cast<cudaStream_t>(stream), static_cast<const uint4*>(xp),
+                   static_cast<int>(H / 8), topk, sorted_pair, offsets, E, El, plan,
+                   reinterpret_cast<uint4* const*>(peer_rows), n_cap, peer_flags, rank, world,
+                   epoch, arrive, err);
+  return launch_status();
+}
+
+extern "C" int knx_ep_p2p_return_barrier(const void* out3, int64_t H, int El, int world, int E,
+                                         const int32_t* plan, void* const* peer_ret,
+                                         int64_t r_cap, uint32_t* const* peer_flags, int rank,
+                                         uint32_t epoch, uint32_t* arrive, int32_t* err,
+                                         void* stream) {
+  using namespace knx;
+  if (H <= 0 || (H % 8) != 0 || El < 1 || world < 1 || world > P2P_MAX_WORLD || E < 1 ||
+      E > P2P_MAX_E || El * world > P2P_MAX_E || r_cap < 0 || rank < 0 || rank >= world ||
+      arrive == nullptr)
+    return KNX_E_INVALID;
+  if (!aligned(out3, 16)) return KNX_E_ALIGN;
+  (void)launch_pdl(p2p_return_bar_kernel, p2p_grid(r_cap), 256, 0,
+                   static_cast<cudaStream_t>(stream), static_cast<const uint4*>(out3),
+                   static_cast<int>(H / 8), El, world, plan, E,
+                   reinterpret_cast<uint4* const*>(peer_ret), r_cap, peer_flags, rank, epoch,
+                   arrive, err);
   return launch_status();
 }
 

@@ -54,6 +54,10 @@ _SIGS = {
     "knx_ep_p2p_dispatch": (_i32, [_vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _i64, _vp]),
     "knx_ep_p2p_barrier": (_i32, [_vp, _i32, _i32, _c.c_uint32, _vp, _vp]),
     "knx_ep_p2p_return": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _i64, _vp]),
+    "knx_ep_p2p_dispatch_barrier": (_i32, [_vp, _i64, _i32, _vp, _vp, _i32, _i32, _vp, _vp, _i64,
+                                           _vp, _i32, _i32, _c.c_uint32, _vp, _vp, _vp]),
+    "knx_ep_p2p_return_barrier": (_i32, [_vp, _i64, _i32, _i32, _i32, _vp, _vp, _i64, _vp, _i32,
+                                         _c.c_uint32, _vp, _vp, _vp]),
     "knx_rmsnorm_router_topk": (_i32, [_vp, _vp, _f32, _i32, _vp, _vp, _i64, _i64, _i32, _i32,
                                        _vp, _vp, _vp, _vp, _vp, _vp]),
     "knx_moe_align": (_i32, [_vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp,

@@ -219,6 +219,8 @@ class _P2PExchange:
         self.plan = torch.empty(load().knx_ep_p2p_plan_ints(E, self.El, self.world), dtype=torch.int32,
                                 device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        # arrival counters of the fused dispatch + barrier and return + barrier launches
+        self.arrive = torch.zeros(2, dtype=torch.int32, device=device)
         self.epoch = 0
         torch.cuda.synchronize(device)
         dist.barrier(group=group)  # every rank's flags are zero before anyone signals
@@ -231,7 +233,8 @@ class _P2PExchange:
 class P2PExpertParallelMoE(ExpertParallelMoE):
     """ExpertParallelMoE with the exchange done by the device over NVLink: the pairs' rows are
     stored straight into the owning ranks' memory and the results straight back (three
-    device-side barriers per layer), so no step of the layer waits for the host.  The local
+    device-side barriers per layer, two of them run by the last CTA of the copy launch before
+    them), so no step of the layer waits for the host.  The local
     experts are rank, rank + world, ... (shard_experts(..., interleaved=True)).  Needs every
     rank on one node with peer access, and the same token count T <= max_tokens on every rank.
     The output is bit-identical to ExpertParallelMoE and to the single-GPU layer."""
@@ -275,22 +278,20 @@ class P2PExpertParallelMoE(ExpertParallelMoE):
                                     ptr(ex.peer_flags), ex.next_epoch(), ptr(ex.plan), ptr(ex.err),
                                     st), "knx_ep_p2p_counts")
         self._mark("counts+barrier+plan")
-        check(lib.knx_ep_p2p_dispatch(ptr(x.contiguous()), H, tk, ptr(sorted_pair), ptr(offsets), E,
-                                      El, ptr(ex.plan), ptr(ex.peer_rows), T * tk, st),
-              "knx_ep_p2p_dispatch")
-        self._mark("dispatch")
-        check(lib.knx_ep_p2p_barrier(ptr(ex.peer_flags), rank, world, ex.next_epoch(),
-                                     ptr(ex.err), st), "knx_ep_p2p_barrier")
-        self._mark("barrier1")
+        check(lib.knx_ep_p2p_dispatch_barrier(ptr(x.contiguous()), H, tk, ptr(sorted_pair),
+                                              ptr(offsets), E, El, ptr(ex.plan), ptr(ex.peer_rows),
+                                              T * tk, ptr(ex.peer_flags), rank, world,
+                                              ex.next_epoch(), ptr(ex.arrive[0:1]), ptr(ex.err), st),
+              "knx_ep_p2p_dispatch_barrier")
+        self._mark("dispatch+barrier")
         recv_off = ex.plan[E:E + El + 1]
         out3 = self.ops.grouped_rows(ex.rows, recv_off, self.weights, tokens_per_expert, self.flags)
         self._mark("grouped_gemms")
-        check(lib.knx_ep_p2p_return(ptr(out3), H, El, world, E, ptr(ex.plan), ptr(ex.peer_ret),
-                                    ex.r_cap, st), "knx_ep_p2p_return")
-        self._mark("return")
-        check(lib.knx_ep_p2p_barrier(ptr(ex.peer_flags), rank, world, ex.next_epoch(),
-                                     ptr(ex.err), st), "knx_ep_p2p_barrier")
-        self._mark("barrier2")
+        check(lib.knx_ep_p2p_return_barrier(ptr(out3), H, El, world, E, ptr(ex.plan),
+                                            ptr(ex.peer_ret), ex.r_cap, ptr(ex.peer_flags), rank,
+                                            ex.next_epoch(), ptr(ex.arrive[1:2]), ptr(ex.err), st),
+              "knx_ep_p2p_return_barrier")
+        self._mark("return+barrier")
         y = self.ops.combine(ex.ret[:T * tk], inv, topk_w.contiguous(), T, out_dtype)
         self._mark("combine")
         return y
