@@ -77,3 +77,28 @@ def test_sampler_selfcond_rejects_bad_arguments_on_host():
     assert f(None, 4, 100, 1.0, 1, None, None, None, sc + 1, None, None, 1, None, 0, None) == -2
     # valid arguments reach the workspace check, which fails without touching the device
     assert f(None, 4, 100, 1.0, 1, None, None, None, sc, prev, fin, 2, None, 0, None) == -3
+
+
+def test_ep_exchange_rejects_bad_arguments_on_host():
+    """The NVLink exchange entry points check their arguments before any launch (the pointers
+    below are never dereferenced): world and rank ranges, the expert split, row widths and
+    alignment, and the fused copy-and-barrier forms' arrival counter."""
+    lib = _knx.load()
+    fl, cnt, x = 4096, 8192, 12288
+    # world beyond 8, rank outside the world, E not El * world
+    assert lib.knx_ep_p2p_counts(None, 128, 16, 0, 9, None, None, 1, None, None, None) == -1
+    assert lib.knx_ep_p2p_counts(None, 128, 64, 2, 2, None, None, 1, None, None, None) == -1
+    assert lib.knx_ep_p2p_counts(None, 128, 60, 0, 2, None, None, 1, None, None, None) == -1
+    assert lib.knx_ep_p2p_barrier(fl, 2, 2, 1, None, None) == -1
+    # dispatch + barrier: H not a multiple of 8, no arrival counter, misaligned rows
+    d = lib.knx_ep_p2p_dispatch_barrier
+    assert d(x, 2817, 8, None, None, 128, 64, None, None, 2048, fl, 0, 2, 1, cnt, None, None) == -1
+    assert d(x, 2816, 8, None, None, 128, 64, None, None, 2048, fl, 0, 2, 1, None, None, None) == -1
+    assert d(x, 2816, 8, None, None, 128, 64, None, None, 2048, fl, 2, 2, 1, cnt, None, None) == -1
+    assert d(x + 8, 2816, 8, None, None, 128, 64, None, None, 2048, fl, 0, 2, 1, cnt, None,
+             None) == -2
+    # return + barrier: world beyond 8, El * world beyond 256 experts, no arrival counter
+    r = lib.knx_ep_p2p_return_barrier
+    assert r(x, 2816, 16, 9, 144, None, None, 4096, fl, 0, 1, cnt, None, None) == -1
+    assert r(x, 2816, 200, 2, 400, None, None, 4096, fl, 0, 1, cnt, None, None) == -1
+    assert r(x, 2816, 64, 2, 128, None, None, 4096, fl, 0, 1, None, None, None) == -1
