@@ -116,13 +116,26 @@ def _free_port():
     return p
 
 
+def _spawn(fn, world, out_dir, attempts=3):
+    """mp.spawn with a fresh rendezvous port per attempt: the port _free_port() released can be
+    taken by another process before rank 0 binds it (EADDRINUSE), which says nothing about the
+    code under test."""
+    for i in range(attempts):
+        try:
+            mp.spawn(fn, args=(world, _free_port(), out_dir), nprocs=world, join=True)
+            return
+        except Exception as exc:  # the ranks' error arrives as ProcessRaisedException text
+            if "EADDRINUSE" not in str(exc) or i == attempts - 1:
+                raise
+
+
 @pytest.mark.parametrize("world", [1, 2])
 def test_expert_parallel_matches_single_process(world):
     W, hidden, ids, w = _data()
     want = ref.moe_layer(hidden, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"], W["dn_z"],
                          ids, w, out_dtype=torch.float16)
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(world, _free_port(), d), nprocs=world, join=True)
+        _spawn(_worker, world, d)
         got = torch.cat([torch.load(os.path.join(d, f"y{r}.pt")) for r in range(world)])
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
@@ -156,7 +169,7 @@ def _straggler_worker(rank, world, port, out_dir):
 
 def test_rank_that_never_joins_is_reported_on_the_host():
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_straggler_worker, args=(2, _free_port(), d), nprocs=2, join=True)
+        _spawn(_straggler_worker, 2, d)
         outcome, secs = open(os.path.join(d, "rank0.txt")).read().split()
     assert outcome != "returned"
     assert float(secs) < 11.0      # ended by the 3 s group timeout, before the straggler left

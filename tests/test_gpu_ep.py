@@ -67,6 +67,20 @@ def _free_port():
     return p
 
 
+def _spawn(fn, world, out_dir, attempts=3):
+    """mp.spawn with a fresh rendezvous port per attempt: the port _free_port() released can be
+    taken by another process before rank 0 binds it (EADDRINUSE), which says nothing about the
+    code under test."""
+    import torch.multiprocessing as mp
+    for i in range(attempts):
+        try:
+            mp.spawn(fn, args=(world, _free_port(), out_dir), nprocs=world, join=True)
+            return
+        except Exception as exc:  # the ranks' error arrives as ProcessRaisedException text
+            if "EADDRINUSE" not in str(exc) or i == attempts - 1:
+                raise
+
+
 def _worker(rank, world, port, out_dir):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -94,7 +108,6 @@ def _worker(rank, world, port, out_dir):
 def test_ep_two_gpus_bitwise_equal_single_gpu(cuda):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
-    import torch.multiprocessing as mp
     import fused_moe_w4_v2
     world = 2
     W, hidden, xp, ids, w = _case(128, 2816, 704, 256 * world, 8, 41, cuda)
@@ -102,7 +115,7 @@ def test_ep_two_gpus_bitwise_equal_single_gpu(cuda):
                                        W["dn_s"], W["dn_z"], ids, w, hidden_perm=xp,
                                        engine="auto").cpu()
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker, args=(world, _free_port(), d), nprocs=world, join=True)
+        _spawn(_worker, world, d)
         got = torch.cat([torch.load(os.path.join(d, f"y{r}.pt")) for r in range(world)])
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
@@ -137,14 +150,13 @@ def _worker_p2p(rank, world, port, out_dir):
 
 
 def _run_p2p(world):
-    import torch.multiprocessing as mp
     import fused_moe_w4_v2
     W, hidden, xp, ids, w = _case(128, 2816, 704, 256 * world, 8, 41, torch.device("cuda", 0))
     want = fused_moe_w4_v2.moe_forward(hidden, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"],
                                        W["dn_s"], W["dn_z"], ids, w, hidden_perm=xp,
                                        engine="auto").cpu()
     with tempfile.TemporaryDirectory() as d:
-        mp.spawn(_worker_p2p, args=(world, _free_port(), d), nprocs=world, join=True)
+        _spawn(_worker_p2p, world, d)
         res = [torch.load(os.path.join(d, f"p{r}.pt")) for r in range(world)]
     for r in res:
         assert r["err"] == 0 and r["same"]
