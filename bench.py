@@ -6,8 +6,9 @@ and HBM GB/s, plus the configs[2] sampler step in microseconds.
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 Prints ONE JSON line on rank 0.  `value` is microseconds per canvas-layer for the whole job (lower
-is better); for N > 1 every rank runs its own canvas through its own copy of the layer (replicas),
-so value = max-over-ranks time / (N * K).  Inputs are synthetic (workloads.py) with the BASELINE
+is better); for N > 1 the 128 experts are sharded over the ranks (128/N each, device-initiated
+exchange over NVLink) and every rank brings its own canvas, so value = max-over-ranks time /
+(N * K).  Inputs are synthetic (workloads.py) with the BASELINE
 shapes and distributions; four distinct weight sets (4 x 416 MB) rotate between steps so every
 step streams its weights from HBM, not L2.
 
@@ -40,7 +41,7 @@ NSETS = 4
 GEMM1_KERNEL = {"tc": "tcp_gemm_kernel<1,0> (gate_up + GELU)",
                 "ws": "hw_gemm_kernel<1,0,4> (gate_up + GELU)",
                 "mma": "gateup_gelu_kernel"}
-GEMM1_NCU_TRAFFIC = {"tc": None, "ws": 302.873600e6 + 3.920896e6}
+GEMM1_NCU_TRAFFIC = {"tc": None, "ws": 302.726912e6 + 4.080384e6}
 
 
 def peaks():
