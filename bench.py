@@ -235,27 +235,49 @@ def time_layer_e2e(dev, steps, warmup):
     return pipelined_e2e(dev, step, inp["hidden"].cpu(), steps, warmup)
 
 
+def balanced_owners(Tr, seeds, world, tpe, dev):
+    """Expert labels that balance the ranks' grouped-GEMM work (ep_moe.balanced_relabel) for
+    the job's routing: every rank routes every rank's synthetic tokens (the same counts on all
+    ranks, no communication).  Tasks of the engine the layer will pick (32 tokens for ws, 128
+    for tc).  -> (relabel, order)."""
+    import ep_moe
+    import moe_router
+    import workloads
+    counts = torch.zeros(E, dtype=torch.int64)
+    for sd in seeds:
+        inp = workloads.moe_inputs(Tr, H, E, seed=sd, device=dev)
+        xp = torch.empty(Tr, H, dtype=torch.float16, device=dev)
+        _, ids, _, _ = moe_router.rmsnorm_route_topk(inp["hidden"], inp["norm_w"], 1e-6,
+                                                     inp["router_w"], TOPK, bias=inp["bias"],
+                                                     xperm=xp, want_logits=False)
+        counts += torch.bincount(ids.flatten().long(), minlength=E).cpu()
+    return ep_moe.balanced_relabel(counts.tolist(), world, 32 if tpe <= 36 else 128)
+
+
 class EpLayer:
     """N > 1: the same configs[1] layer with the 128 experts sharded over the ranks (expert
-    parallelism; dispatch and return by device-initiated stores over NVLink); each rank runs its
-    own 256-token canvas."""
+    parallelism; dispatch and return by device-initiated stores over NVLink; owners balanced by
+    the job's routing); each rank runs its own 256-token canvas."""
 
     def __init__(self, dev, rank, world):
         import ep_moe
         import workloads
+        self.tpe = T * TOPK * world // E  # job-wide pairs per expert (engine choice)
+        relabel, order = balanced_owners(T, range(world), world, self.tpe, dev)
         self.layers = []
         for i in range(NSETS):
             Wf = workloads.moe_weights(E, H, I, seed=100 + i, device=dev)
             local = ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"], Wf["gu_z"], Wf["dn_q"],
-                                         Wf["dn_s"], Wf["dn_z"], rank, world, interleaved=True)
+                                         Wf["dn_s"], Wf["dn_z"], rank, world, interleaved=True,
+                                         order=order)
             del Wf
             # the exchange runs on the device over NVLink (no host sync per layer)
             self.layers.append(ep_moe.P2PExpertParallelMoE(*local, E_total=E, int_zeros=False,
-                                                           max_tokens=T, topk=TOPK))
+                                                           max_tokens=T, topk=TOPK,
+                                                           relabel=relabel))
         torch.cuda.empty_cache()
         self.inp = workloads.moe_inputs(T, H, E, seed=rank, device=dev)  # this rank's canvas
         self.xp = torch.empty(T, H, dtype=torch.float16, device=dev)
-        self.tpe = T * TOPK * world // E  # job-wide pairs per expert (engine choice)
 
     def step(self, i, hidden=None):
         import moe_router
@@ -268,8 +290,8 @@ class EpLayer:
                                       tokens_per_expert=self.tpe), ids
 
 
-EP_LAUNCHES_PER_LAYER = 11  # RMSNorm + router, align, counts exchange + plan, dispatch, barrier,
-                            # task list, gate_up, down, return, barrier, combine (NVLink exchange)
+EP_LAUNCHES_PER_LAYER = 9  # RMSNorm + router, align, counts exchange + plan, dispatch + barrier,
+                           # task list, gate_up, down, return + barrier, combine (NVLink exchange)
 
 
 def time_layer_ep(dev, steps, warmup, rank, world):
@@ -391,15 +413,18 @@ def time_prefill(dev, steps, rank, world):
     Wf = workloads.moe_weights(E, H, I, seed=400, device=dev)
     inp = workloads.moe_inputs(Tr, H, E, seed=500 + rank, device=dev)
     xp = torch.empty(Tr, H, dtype=torch.float16, device=dev)
+    tpe = PREFILL_TOKENS * TOPK // E
     if world > 1:
         import ep_moe
+        relabel, order = balanced_owners(Tr, [500 + r for r in range(world)], world, tpe, dev)
         layer = ep_moe.P2PExpertParallelMoE(*ep_moe.shard_experts(Wf["gu_q"], Wf["gu_s"],
                                                                     Wf["gu_z"], Wf["dn_q"],
                                                                     Wf["dn_s"], Wf["dn_z"], rank,
-                                                                    world, interleaved=True),
-                                            E_total=E, int_zeros=False, max_tokens=Tr, topk=TOPK)
+                                                                    world, interleaved=True,
+                                                                    order=order),
+                                            E_total=E, int_zeros=False, max_tokens=Tr, topk=TOPK,
+                                            relabel=relabel)
         del Wf
-    tpe = PREFILL_TOKENS * TOPK // E
 
     def step():
         yn, ids, w, _ = moe_router.rmsnorm_route_topk(inp["hidden"], inp["norm_w"], 1e-6,
@@ -660,9 +685,9 @@ def main():
                                "T=256 H=2816 I=704 E=128 top-8, gate_up gs128 / down gs64",
                    "l2": f"{NSETS} rotating weight sets ({NSETS} x 416 MB) > 126 MB L2",
                    "parallelism": (f"expert-parallel x{world} (128/{world} experts per GPU, "
-                                   f"one 256-token canvas per GPU, device-initiated NVLink "
-                                   f"exchange through symmetric memory)"
-                                   if world > 1 else "single GPU"),
+                                   f"owners balanced by the job's routing, one 256-token canvas "
+                                   f"per GPU, device-initiated NVLink exchange through symmetric "
+                                   f"memory)" if world > 1 else "single GPU"),
                    "touched_experts": touched,
                    "max_tokens_per_expert": int(counts.max())},
         "layer_hbm_gbs": bytes_layer / (ms_step * 1e-3) / 1e9,

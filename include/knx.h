@@ -129,6 +129,16 @@ KNX_API int knx_moe_align_large(const void* topk_ids, int ids_dtype, int64_t T, 
                                 int32_t* counts, int32_t* offsets, int32_t* sorted_pair, int32_t* inv,
                                 void* scratch, size_t scratch_bytes, int32_t* err, void* stream);
 
+/* The same unpadded permutation for relabelled experts: pair p counts as expert relabel[ids[p]]
+ * (relabel: E int32 on the device, a permutation of 0..E-1; a label outside it is reported as
+ * KNX_DEV_BAD_EXPERT_ID and the pair dropped).  Used by the expert-parallel layer so that
+ * round-robin ownership of the labels spreads the load.  scratch as knx_moe_align_large when
+ * T*topk > 32768 (else unused). */
+KNX_API int knx_moe_align_relabeled(const void* topk_ids, int ids_dtype, int64_t T, int topk, int E,
+                                    const int32_t* relabel, int32_t* counts, int32_t* offsets,
+                                    int32_t* sorted_pair, int32_t* inv, void* scratch,
+                                    size_t scratch_bytes, int32_t* err, void* stream);
+
 /* ---- one W4A16 MoE layer ------------------------------------------------------------------
  * Replaces fused_moe_w4_v2 (fused_moe_w4_v2.py:319-371) and fused_moe_w4 (fused_moe_w4.py:104-128).
  * Weight buffers are the pack_experts layout, read unchanged (pack_experts.py:34-41, 87-106):

@@ -27,14 +27,14 @@ int launch_align(const void* ids, int ids_dtype, int T, int topk, int E, int blo
                  int32_t* counts, int32_t* offsets, int32_t* sorted_pair, int32_t* inv,
                  int32_t* sorted_rows, int32_t* expert_ids, int32_t* padded_inv, int4* tasks,
                  int32_t* ntasks, int32_t* work_counters, int n_work_counters, int32_t* err,
-                 cudaStream_t stream);
+                 cudaStream_t stream, const int32_t* relabel = nullptr);
 int launch_permute(const void* x, int dtype, __half* xp, int64_t elems, cudaStream_t stream);
 // Counting sort for N > ALIGN_MAX_PAIRS (unpadded outputs only; scratch of
 // align_large_scratch_bytes), and the task list from per-expert offsets (one CTA).
 size_t align_large_scratch_bytes(int64_t N, int E);
 int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t* counts,
                        int32_t* offsets, int32_t* sorted_pair, int32_t* inv, void* scratch,
-                       int32_t* err, cudaStream_t s);
+                       int32_t* err, cudaStream_t s, const int32_t* relabel = nullptr);
 int launch_tasks_from_offsets(const int32_t* offsets, int E, int m, int4* tasks, int32_t* ntasks,
                               int32_t* counters, cudaStream_t s);
 

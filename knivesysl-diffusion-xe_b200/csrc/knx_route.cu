@@ -218,6 +218,26 @@ __device__ void block_excl_scan3(const int (&v)[3], int* sbuf, int (&ex)[3], int
   __syncthreads();
 }
 
+// The label of pair p: ids[p] (0..E-1; E or anything outside means dropped), through the
+// optional relabelling table (a permutation of 0..E-1; a label outside it is an invalid id).
+// Returns E for a dropped or invalid pair and sets `bad` for an invalid one.
+KNX_DEVINL int pair_label(const void* ids, int ids_dtype, int64_t p, int E,
+                          const int32_t* __restrict__ relabel, int& bad) {
+  int64_t v = load_as_i64(ids, ids_dtype, p);
+  if (v < 0 || v > E) {
+    bad = 1;
+    return E;
+  }
+  if (relabel && v < E) {
+    v = relabel[v];
+    if (v < 0 || v >= E) {
+      bad = 1;
+      return E;
+    }
+  }
+  return static_cast<int>(v);
+}
+
 __global__ void __launch_bounds__(AL_THREADS)
     align_kernel(const void* __restrict__ ids, int ids_dtype, int T, int topk, int E, int block_m,
                  int m_max, int32_t* __restrict__ counts, int32_t* __restrict__ offsets,
@@ -225,7 +245,8 @@ __global__ void __launch_bounds__(AL_THREADS)
                  int32_t* __restrict__ sorted_rows, int32_t* __restrict__ expert_ids,
                  int32_t* __restrict__ padded_inv, int4* __restrict__ tasks,
                  int32_t* __restrict__ ntasks, int32_t* __restrict__ work_counters,
-                 int n_work_counters, int32_t* __restrict__ err) {
+                 int n_work_counters, int32_t* __restrict__ err,
+                 const int32_t* __restrict__ relabel) {
   pdl_wait_trigger();
   extern __shared__ __align__(16) uint8_t sm_raw[];
   const int N = T * topk;
@@ -247,14 +268,8 @@ __global__ void __launch_bounds__(AL_THREADS)
   for (int i = tid; i <= m_max; i += AL_THREADS) size_hist[i] = 0;
   if (tid < n_work_counters) work_counters[tid] = 0;
   int bad = 0;
-  for (int p = tid; p < N; p += AL_THREADS) {
-    int64_t v = load_as_i64(ids, ids_dtype, p);
-    if (v < 0 || v > E) {
-      bad = 1;
-      v = E;
-    }
-    sid[p] = static_cast<int16_t>(v);
-  }
+  for (int p = tid; p < N; p += AL_THREADS)
+    sid[p] = static_cast<int16_t>(pair_label(ids, ids_dtype, p, E, relabel, bad));
   if (bad && err) atomicOr(err, KNX_DEV_BAD_EXPERT_ID);
   __syncthreads();
 
@@ -475,7 +490,7 @@ constexpr int LB = 4096;  // pairs per block
 __global__ void __launch_bounds__(AL_THREADS)
     align_large_count_kernel(const void* __restrict__ ids, int ids_dtype, int64_t N, int E,
                              int32_t* __restrict__ blkcnt, int32_t* __restrict__ lrank,
-                             int32_t* __restrict__ err) {
+                             int32_t* __restrict__ err, const int32_t* __restrict__ relabel) {
   pdl_wait_trigger();
   __shared__ int whist[32 * 256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -490,14 +505,7 @@ __global__ void __launch_bounds__(AL_THREADS)
   for (int r = 0; r < PER_WARP / 32; ++r) {
     const int64_t p = b0 + warp * PER_WARP + r * 32 + lane;
     int e = E;
-    if (p < N) {
-      int64_t v = load_as_i64(ids, ids_dtype, p);
-      if (v < 0 || v > E) {
-        bad = 1;
-        v = E;
-      }
-      e = static_cast<int>(v);
-    }
+    if (p < N) e = pair_label(ids, ids_dtype, p, E, relabel, bad);
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int before = __popc(peers & lt_mask);
     const int leader = __ffs(peers) - 1;
@@ -566,7 +574,8 @@ __global__ void align_large_scatter_kernel(const void* __restrict__ ids, int ids
                                            const int32_t* __restrict__ lrank,
                                            const int32_t* __restrict__ offsets,
                                            int32_t* __restrict__ sorted_pair,
-                                           int32_t* __restrict__ inv) {
+                                           int32_t* __restrict__ inv,
+                                           const int32_t* __restrict__ relabel) {
   pdl_wait_trigger();
   const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (p >= N) return;
@@ -574,7 +583,8 @@ __global__ void align_large_scatter_kernel(const void* __restrict__ ids, int ids
   if (r < 0) {
     if (inv) inv[p] = -1;
   } else {
-    const int e = static_cast<int>(load_as_i64(ids, ids_dtype, p));
+    int bad = 0;  // a valid pair here (lrank >= 0): its label is in range
+    const int e = pair_label(ids, ids_dtype, p, E, relabel, bad);
     const int slot = blkbase[(p / LB) * E + e] + r;
     if (sorted_pair) sorted_pair[slot] = static_cast<int32_t>(p);
     if (inv) inv[p] = slot;
@@ -622,7 +632,7 @@ int launch_align(const void* ids, int ids_dtype, int T, int topk, int E, int blo
                  int32_t* counts, int32_t* offsets, int32_t* sorted_pair, int32_t* inv,
                  int32_t* sorted_rows, int32_t* expert_ids, int32_t* padded_inv, int4* tasks,
                  int32_t* ntasks, int32_t* work_counters, int n_work_counters, int32_t* err,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const int32_t* relabel) {
   const int N = T * topk;
   if (tasks && (m_max < 1 || m_max > MAX_TASK_TOKENS)) return KNX_E_UNSUPPORTED;  // one warp scan
   const size_t smem = align_smem_bytes(N, E, m_max);
@@ -630,7 +640,7 @@ int launch_align(const void* ids, int ids_dtype, int T, int topk, int E, int blo
     return KNX_E_DEVICE;
   (void)launch_pdl(align_kernel, 1, AL_THREADS, smem, stream, ids, ids_dtype, T, topk, E, block_m,
                    m_max, counts, offsets, sorted_pair, inv, sorted_rows, expert_ids, padded_inv,
-                   tasks, ntasks, work_counters, n_work_counters, err);
+                   tasks, ntasks, work_counters, n_work_counters, err, relabel);
   return launch_status();
 }
 
@@ -656,7 +666,7 @@ size_t align_large_scratch_bytes(int64_t N, int E) {
 
 int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t* counts,
                        int32_t* offsets, int32_t* sorted_pair, int32_t* inv, void* scratch,
-                       int32_t* err, cudaStream_t s) {
+                       int32_t* err, cudaStream_t s, const int32_t* relabel) {
   if (E > 256 || N > (1LL << 30)) return KNX_E_UNSUPPORTED;
   if (N == 0) return KNX_OK;
   const int nblk = static_cast<int>((N + LB - 1) / LB);
@@ -664,11 +674,11 @@ int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t
   int32_t* blkcnt = lrank + ((N + 63) & ~int64_t(63));
   int32_t* blkbase = blkcnt + static_cast<int64_t>(nblk) * E;
   (void)launch_pdl(align_large_count_kernel, nblk, AL_THREADS, 0, s, ids, ids_dtype, N, E, blkcnt,
-                   lrank, err);
+                   lrank, err, relabel);
   (void)launch_pdl(align_large_scan_kernel, 1, 256, 0, s, blkcnt, nblk, E, blkbase, counts,
                    offsets);
   (void)launch_pdl(align_large_scatter_kernel, static_cast<unsigned>((N + 255) / 256), 256, 0, s,
-                   ids, ids_dtype, N, E, blkbase, lrank, offsets, sorted_pair, inv);
+                   ids, ids_dtype, N, E, blkbase, lrank, offsets, sorted_pair, inv, relabel);
   return launch_status();
 }
 
@@ -736,6 +746,28 @@ extern "C" int knx_moe_align_large(const void* topk_ids, int ids_dtype, int64_t 
   if (!aligned(scratch, 16)) return KNX_E_ALIGN;
   return launch_align_large(topk_ids, ids_dtype, N, E, counts, offsets, sorted_pair, inv, scratch,
                             err, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int knx_moe_align_relabeled(const void* topk_ids, int ids_dtype, int64_t T, int topk,
+                                       int E, const int32_t* relabel, int32_t* counts,
+                                       int32_t* offsets, int32_t* sorted_pair, int32_t* inv,
+                                       void* scratch, size_t scratch_bytes, int32_t* err,
+                                       void* stream) {
+  using namespace knx;
+  if (T < 0 || topk < 1 || topk > 64 || E < 1 || E > ALIGN_MAX_EXPERTS || relabel == nullptr)
+    return KNX_E_INVALID;
+  if (ids_dtype != KNX_I32 && ids_dtype != KNX_I64) return KNX_E_INVALID;
+  const int64_t N = T * topk;
+  if (N == 0) return KNX_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (align_supported(N, E))
+    return launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0, 1, counts, offsets,
+                        sorted_pair, inv, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, 0,
+                        err, s, relabel);
+  if (scratch == nullptr || scratch_bytes < align_large_scratch_bytes(N, E)) return KNX_E_WORKSPACE;
+  if (!aligned(scratch, 16)) return KNX_E_ALIGN;
+  return launch_align_large(topk_ids, ids_dtype, N, E, counts, offsets, sorted_pair, inv, scratch,
+                            err, s, relabel);
 }
 
 extern "C" int knx_moe_align(const void* topk_ids, int ids_dtype, int64_t T, int topk, int E,

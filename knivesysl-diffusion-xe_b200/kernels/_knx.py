@@ -65,6 +65,8 @@ _SIGS = {
     "knx_moe_align_large_scratch_size": (_sz, [_i64, _i32]),
     "knx_moe_align_large": (_i32, [_vp, _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _sz, _vp,
                                    _vp]),
+    "knx_moe_align_relabeled": (_i32, [_vp, _i32, _i64, _i32, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
+                                       _sz, _vp, _vp]),
     "knx_moe_w4_workspace_size": (_sz, [_i64, _i64, _i64, _i32, _i32]),
     "knx_moe_w4": (_i32, [_vp, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
                           _i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32, _vp, _sz, _vp, _vp,

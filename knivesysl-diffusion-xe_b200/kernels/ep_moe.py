@@ -29,9 +29,9 @@ from _knx import (KNX_DEV_TIMEOUT, KNX_W4_INT_ZEROS, check, dtype_code, engine_f
 class CudaOps:
     """The device steps on sm_100a (libknx.so)."""
 
-    def align(self, ids, E):
+    def align(self, ids, E, relabel=None):
         from fused_moe_w4 import moe_align_unpadded
-        return moe_align_unpadded(ids, E)
+        return moe_align_unpadded(ids, E, relabel)
 
     def gather_rows(self, src, idx, div, n):
         dev = require_device(src)
@@ -164,14 +164,49 @@ class ExpertParallelMoE:
     __call__ = forward
 
 
-def shard_experts(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, rank, world, interleaved=False):
+def shard_experts(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, rank, world, interleaved=False, order=None):
     """This rank's experts of full pack_experts buffers: the contiguous slice
     [rank * E / world, (rank + 1) * E / world) (ExpertParallelMoE), or with interleaved=True the
-    experts rank, rank + world, ... (P2PExpertParallelMoE)."""
+    experts rank, rank + world, ... (P2PExpertParallelMoE).  order (with interleaved=True): the
+    expert behind each label (balanced_relabel), so that this rank holds the experts labelled
+    rank, rank + world, ..."""
     E = gu_q.shape[0]
     El = E // world
+    if order is not None:
+        if not interleaved:
+            raise ValueError("order needs interleaved=True")
+        idx = torch.as_tensor(list(order), dtype=torch.long)[rank::world].to(gu_q.device)
+        return tuple(t.index_select(0, idx).contiguous() for t in (gu_q, gu_s, gu_z, dn_q, dn_s, dn_z))
     sl = slice(rank, E, world) if interleaved else slice(rank * El, (rank + 1) * El)
     return tuple(t[sl].contiguous() for t in (gu_q, gu_s, gu_z, dn_q, dn_s, dn_z))
+
+
+def balanced_relabel(counts, world, task_tokens=32):
+    """Labels for the experts so that round-robin ownership of the labels (rank r holds labels
+    r, r + world, ...) balances the grouped-GEMM work: experts by descending task count
+    (ceil(pairs / task_tokens); ties by expert id) go to the least loaded rank that still has room
+    (E / world each; ties to the lower rank), and rank r's k-th expert gets label k * world + r.
+    counts: pairs per expert over the whole job (e.g. measured on a calibration batch).
+    -> (relabel, order): relabel[e] = label of expert e, order[label] = expert."""
+    import math
+    counts = [int(c) for c in counts]
+    E = len(counts)
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    cap = E // world
+    load = [0] * world
+    owned = [[] for _ in range(world)]
+    for e in sorted(range(E), key=lambda e: (-math.ceil(counts[e] / task_tokens), e)):
+        r = min((r for r in range(world) if len(owned[r]) < cap), key=lambda r: (load[r], r))
+        owned[r].append(e)
+        load[r] += math.ceil(counts[e] / task_tokens)
+    relabel = [0] * E
+    order = [0] * E
+    for r in range(world):
+        for k, e in enumerate(owned[r]):
+            relabel[e] = k * world + r
+            order[k * world + r] = e
+    return relabel, order
 
 
 class _P2PExchange:
@@ -235,16 +270,21 @@ class P2PExpertParallelMoE(ExpertParallelMoE):
     stored straight into the owning ranks' memory and the results straight back (three
     device-side barriers per layer, two of them run by the last CTA of the copy launch before
     them), so no step of the layer waits for the host.  The local
-    experts are rank, rank + world, ... (shard_experts(..., interleaved=True)).  Needs every
-    rank on one node with peer access, and the same token count T <= max_tokens on every rank.
-    The output is bit-identical to ExpertParallelMoE and to the single-GPU layer."""
+    experts are rank, rank + world, ... (shard_experts(..., interleaved=True)), or with
+    relabel the experts labelled so (shard_experts(..., interleaved=True, order=...) with the
+    same balanced_relabel result): the router's ids are relabelled inside the counting sort.
+    Needs every rank on one node with peer access, and the same token count T <= max_tokens on
+    every rank.  The output is bit-identical to ExpertParallelMoE and to the single-GPU layer
+    (relabelling moves experts between ranks; every expert sees the same rows in the same order)."""
 
     def __init__(self, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=None, engine=None,
-                 int_zeros=None, max_tokens=256, topk=8):
+                 int_zeros=None, max_tokens=256, topk=8, relabel=None):
         super().__init__(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, E_total, group=group, ops=CudaOps(),
                          engine=engine, int_zeros=int_zeros)
         H = gu_q.shape[2] * 2
         self.ex = _P2PExchange.get(group, E_total, max_tokens * topk, H, gu_q.device)
+        self.relabel = (None if relabel is None else
+                        torch.as_tensor(list(relabel), dtype=torch.int32).to(gu_q.device))
         # set to a list to get (stage name, CUDA event) marks recorded on the stream between
         # the layer's stages (benchmark breakdowns; records stop the kernels from overlapping)
         self.stage_events = None
@@ -270,7 +310,7 @@ class P2PExpertParallelMoE(ExpertParallelMoE):
         dev = require_device(x)
         st = stream_of(dev)
         self._mark("start")
-        counts, offsets, sorted_pair, inv = self.ops.align(topk_ids, self.E)
+        counts, offsets, sorted_pair, inv = self.ops.align(topk_ids, self.E, self.relabel)
         counts = counts.to(torch.int32)
         E, El, world, rank = self.E, self.El, self.N, self.rank
         self._mark("align")

@@ -43,9 +43,10 @@ def moe_align(topk_ids, block_m, E):
 
 
 @torch.no_grad()
-def moe_align_unpadded(topk_ids, E):
+def moe_align_unpadded(topk_ids, E, relabel=None):
     """(counts i32[E], offsets i32[E+1], sorted_pair i32[N], inv i32[N]): the unpadded stable
-    permutation the GEMMs use (inv = -1 for dropped pairs)."""
+    permutation the GEMMs use (inv = -1 for dropped pairs).  relabel: optional int32 device
+    tensor of E labels (a permutation of 0..E-1); pair p then counts as expert relabel[ids[p]]."""
     dev = require_device(topk_ids)
     T, tk = topk_ids.shape
     N = T * tk
@@ -58,7 +59,17 @@ def moe_align_unpadded(topk_ids, E):
     sorted_pair = torch.empty(N, **i32)
     inv = torch.empty(N, **i32)
     lib = load()
-    if N <= 32768:
+    if relabel is not None:
+        if relabel.dtype != torch.int32 or relabel.numel() != E or relabel.device != topk_ids.device:
+            raise ValueError("relabel must be an int32 tensor of E labels on the ids' device")
+        nbytes = lib.knx_moe_align_large_scratch_size(N, E) if N > 32768 else 0
+        scratch = workspace(dev, nbytes, "align_large") if nbytes else None
+        check(lib.knx_moe_align_relabeled(ptr(ids), dtype_code(ids.dtype), T, tk, E,
+                                          ptr(relabel.contiguous()), ptr(counts), ptr(offsets),
+                                          ptr(sorted_pair), ptr(inv), ptr(scratch),
+                                          scratch.numel() if scratch is not None else 0, None,
+                                          stream_of(dev)), "knx_moe_align_relabeled")
+    elif N <= 32768:
         check(lib.knx_moe_align(ptr(ids), dtype_code(ids.dtype), T, tk, E, 0, ptr(counts),
                                 ptr(offsets), ptr(sorted_pair), ptr(inv), None, None, None, None,
                                 stream_of(dev)), "knx_moe_align")

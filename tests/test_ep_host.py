@@ -173,3 +173,27 @@ def test_rank_that_never_joins_is_reported_on_the_host():
         outcome, secs = open(os.path.join(d, "rank0.txt")).read().split()
     assert outcome != "returned"
     assert float(secs) < 11.0      # ended by the 3 s group timeout, before the straggler left
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_balanced_relabel_is_a_permutation_that_spreads_the_tasks(world):
+    import math
+    import ep_moe
+    g = torch.Generator().manual_seed(world)
+    # Zipf-like pairs per expert, as the router's bias gives them
+    counts = [int(600 / (1 + e) ** 0.8 + torch.randint(0, 8, (1,), generator=g)) for e in range(E)]
+    relabel, order = ep_moe.balanced_relabel(counts, world)
+    assert sorted(relabel) == list(range(E)) and sorted(order) == list(range(E))
+    assert all(order[relabel[e]] == e for e in range(E))
+    tasks = [math.ceil(c / 32) for c in counts]
+    per_rank = [sum(tasks[order[lab]] for lab in range(r, E, world)) for r in range(world)]
+    rr = [sum(tasks[r::world]) for r in range(world)]
+    assert max(per_rank) - min(per_rank) <= max(tasks)       # greedy bound
+    assert max(per_rank) <= max(rr)                          # never worse than round-robin
+    # the labels a rank holds are exactly the experts shard_experts(order=...) gives it
+    W, _, _, _ = _data()
+    for r in range(world):
+        local = ep_moe.shard_experts(W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"],
+                                     W["dn_z"], r, world, interleaved=True, order=order)
+        want = torch.stack([W["gu_q"][order[lab]] for lab in range(r, E, world)])
+        assert torch.equal(local[0], want)

@@ -67,14 +67,15 @@ def _free_port():
     return p
 
 
-def _spawn(fn, world, out_dir, attempts=3):
+def _spawn(fn, world, out_dir, attempts=3, extra=()):
     """mp.spawn with a fresh rendezvous port per attempt: the port _free_port() released can be
     taken by another process before rank 0 binds it (EADDRINUSE), which says nothing about the
     code under test."""
     import torch.multiprocessing as mp
     for i in range(attempts):
         try:
-            mp.spawn(fn, args=(world, _free_port(), out_dir), nprocs=world, join=True)
+            mp.spawn(fn, args=(world, _free_port(), out_dir) + tuple(extra), nprocs=world,
+                     join=True)
             return
         except Exception as exc:  # the ranks' error arrives as ProcessRaisedException text
             if "EADDRINUSE" not in str(exc) or i == attempts - 1:
@@ -120,7 +121,7 @@ def test_ep_two_gpus_bitwise_equal_single_gpu(cuda):
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
 
-def _worker_p2p(rank, world, port, out_dir):
+def _worker_p2p(rank, world, port, out_dir, balanced=False):
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -133,10 +134,19 @@ def _worker_p2p(rank, world, port, out_dir):
     try:
         import ep_moe
         W, hidden, xp, ids, w = _case(128, 2816, 704, 256 * world, 8, 41, dev)
+        relabel = order = None
+        if balanced:  # owners dealt by the job-wide pairs per expert (every rank sees all ids)
+            counts = torch.bincount(ids.flatten().long(), minlength=128).tolist()
+            relabel, order = ep_moe.balanced_relabel(counts, world)
+            if world == 1:  # one rank: any permutation must still give the same rows
+                relabel = [(e * 37) % 128 for e in range(128)]
+                order = [0] * 128
+                for e, lab in enumerate(relabel):
+                    order[lab] = e
         local = ep_moe.shard_experts(W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"],
-                                     W["dn_z"], rank, world, interleaved=True)
+                                     W["dn_z"], rank, world, interleaved=True, order=order)
         sl = slice(rank * 256, (rank + 1) * 256)
-        layer = ep_moe.P2PExpertParallelMoE(*local, E_total=128)
+        layer = ep_moe.P2PExpertParallelMoE(*local, E_total=128, relabel=relabel)
         # three layers in a row through the same exchange region (epochs, reuse of the rows)
         ys = [layer(xp[sl].contiguous(), ids[sl].contiguous(), w[sl].contiguous(),
                     out_dtype=torch.float16).clone() for _ in range(3)]
@@ -149,14 +159,14 @@ def _worker_p2p(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def _run_p2p(world):
+def _run_p2p(world, balanced=False):
     import fused_moe_w4_v2
     W, hidden, xp, ids, w = _case(128, 2816, 704, 256 * world, 8, 41, torch.device("cuda", 0))
     want = fused_moe_w4_v2.moe_forward(hidden, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"],
                                        W["dn_s"], W["dn_z"], ids, w, hidden_perm=xp,
                                        engine="auto").cpu()
     with tempfile.TemporaryDirectory() as d:
-        _spawn(_worker_p2p, world, d)
+        _spawn(_worker_p2p, world, d, extra=(balanced,))
         res = [torch.load(os.path.join(d, f"p{r}.pt")) for r in range(world)]
     for r in res:
         assert r["err"] == 0 and r["same"]
@@ -164,18 +174,21 @@ def _run_p2p(world):
     assert torch.equal(got.view(torch.int16), want.view(torch.int16))
 
 
-def test_ep_p2p_one_rank_bitwise_equal_single_gpu(cuda):
-    """The NVLink exchange at one rank (stores into its own region) equals the single-GPU layer."""
-    _run_p2p(1)
+@pytest.mark.parametrize("balanced", [False, True])
+def test_ep_p2p_one_rank_bitwise_equal_single_gpu(cuda, balanced):
+    """The NVLink exchange at one rank (stores into its own region) equals the single-GPU layer,
+    also with the experts relabelled (a permutation applied inside the counting sort)."""
+    _run_p2p(1, balanced)
 
 
+@pytest.mark.parametrize("balanced", [False, True])
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_ep_p2p_multi_gpu_bitwise_equal_single_gpu(cuda, world):
+def test_ep_p2p_multi_gpu_bitwise_equal_single_gpu(cuda, world, balanced):
     """2, 4 and 8 ranks (one canvas each, 128 / world experts per rank) through the NVLink
     exchange, three layers in a row: bit-identical to the single-GPU layer on all the tokens."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    _run_p2p(world)
+    _run_p2p(world, balanced)
 
 
 def test_p2p_barrier_gives_up_and_the_plan_is_empty(cuda):
