@@ -102,3 +102,18 @@ def test_ep_exchange_rejects_bad_arguments_on_host():
     assert r(x, 2816, 16, 9, 144, None, None, 4096, fl, 0, 1, cnt, None, None) == -1
     assert r(x, 2816, 200, 2, 400, None, None, 4096, fl, 0, 1, cnt, None, None) == -1
     assert r(x, 2816, 64, 2, 128, None, None, 4096, fl, 0, 1, None, None, None) == -1
+
+
+def test_relabeled_align_rejects_bad_arguments_on_host():
+    """knx_moe_align_relabeled needs its table and a supported id type and expert count, and
+    the multi-CTA size needs its scratch (checked before any launch)."""
+    lib = _knx.load()
+    f = lib.knx_moe_align_relabeled
+    ids, tab = 4096, 8192
+    assert f(ids, _knx.KNX_I32, 256, 8, 128, None, None, None, None, None, None, 0, None, None) == -1
+    assert f(ids, _knx.KNX_F16, 256, 8, 128, tab, None, None, None, None, None, 0, None, None) == -1
+    assert f(ids, _knx.KNX_I32, 256, 8, 512, tab, None, None, None, None, None, 0, None, None) == -1
+    # 8192 tokens x top-8 needs the multi-CTA sort and its scratch
+    assert f(ids, _knx.KNX_I32, 8192, 8, 128, tab, None, None, None, None, None, 0, None,
+             None) == -3
+    assert f(ids, _knx.KNX_I32, 0, 8, 128, tab, None, None, None, None, None, 0, None, None) == 0
