@@ -550,14 +550,9 @@ def cpu_layer(nthreads):
     restatement of the reference's torch path (RMSNorm, router, per-expert F.linear on
     dequant_w4 weights, tanh-GELU, fixed-order combine), with the dequantisation inside the
     timed region.  Returns microseconds."""
-    import workloads
     from oracle import ref
     torch.set_num_threads(nthreads)
-    W = _CPU_CACHE.get("W")
-    if W is None:
-        W = _CPU_CACHE["W"] = workloads.moe_weights(E, H, I, seed=100)
-        _CPU_CACHE["inp"] = workloads.moe_inputs(T, H, E, seed=0)
-    inp = _CPU_CACHE["inp"]
+    W, inp = _cpu_inputs()
     t0 = time.perf_counter()
     xn = ref.rmsnorm(inp["hidden"], inp["norm_w"], 1e-6)
     ids, w, _ = ref.router_topk(xn, inp["router_w"], inp["bias"], TOPK)
@@ -566,8 +561,58 @@ def cpu_layer(nthreads):
 
 
 _CPU_CACHE = {}
+
+
+def _cpu_inputs():
+    """The CPU layer's packed weights and inputs (built once)."""
+    import workloads
+    if "W" not in _CPU_CACHE:
+        _CPU_CACHE["W"] = workloads.moe_weights(E, H, I, seed=100)
+        _CPU_CACHE["inp"] = workloads.moe_inputs(T, H, E, seed=0)
+    return _CPU_CACHE["W"], _CPU_CACHE["inp"]
+
+
 CPU_SAMPLE = ("the full configs[1] layer (RMSNorm + router + all 128 experts, dequant inside the "
               "timed region) per step")
+
+
+def cpu_layer_predequant(nthreads):
+    """The same CPU layer with every expert's weights dequantised to fp32 before the timed region
+    (the second way the reference's torch path can run).  Returns microseconds."""
+    from oracle import ref
+    torch.set_num_threads(nthreads)
+    W, inp = _cpu_inputs()
+    dense = _CPU_CACHE.get("dense")
+    if dense is None:
+        dense = _CPU_CACHE["dense"] = ref.dense_experts(W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"],
+                                                        W["dn_s"], W["dn_z"])
+    t0 = time.perf_counter()
+    xn = ref.rmsnorm(inp["hidden"], inp["norm_w"], 1e-6)
+    ids, w, _ = ref.router_topk(xn, inp["router_w"], inp["bias"], TOPK)
+    ref.moe_layer(xn, W["gu_q"], W["gu_s"], W["gu_z"], W["dn_q"], W["dn_s"], W["dn_z"], ids, w,
+                  dense=dense)
+    return (time.perf_counter() - t0) * 1e6
+
+
+def cpu_sampler_step(nthreads):
+    """One configs[2] sampler step of the reference algorithm on the host (temperature of step
+    24): Categorical entropy of the processed logits, the Philox Gumbel-max sample and argmax
+    (the oracle's C restatement on `nthreads` threads) and the entropy-bound acceptance.
+    Returns microseconds."""
+    import workloads
+    from oracle import ref
+    torch.set_num_threads(nthreads)
+    x = _CPU_CACHE.get("logits")
+    if x is None:
+        x = _CPU_CACHE["logits"] = workloads.sampler_logits(256, V_SAMPLER, seed=0)
+    cur = torch.zeros(1, 256, dtype=torch.int64)
+    step = 24
+    Tm = workloads.temperature(step)
+    t0 = time.perf_counter()
+    h = ref.entropy(x / Tm)
+    s, _ = ref.gumbel_argmax(x, workloads.step_seed(1234, step), temperature=Tm, nthreads=nthreads)
+    ref.accept_canvas(h.view(1, 256), cur, s.view(1, 256), 0.1)
+    return (time.perf_counter() - t0) * 1e6
 
 
 def cpu_baseline(nthreads, runs=5, warmup=1):
@@ -666,12 +711,25 @@ def main():
         torch.distributed.destroy_process_group()
     if rank != 0:
         return
-    cpu = None
-    if not args.no_cpu_baseline:
+    cpu = cpu_extra = None
+    if not args.no_cpu_baseline and not dist:  # rank 0 at N = 1 only
         ncores = len(os.sched_getaffinity(0))
         us, spread = cpu_baseline(ncores)
         cpu = {"value": us, "unit": "us", "cores": ncores, "kind": "port",
                "sample": CPU_SAMPLE + ", median of 5 after 1 warm-up", "spread": spread}
+        pre = [cpu_layer_predequant(ncores) for _ in range(4)][1:]
+        samp = [cpu_sampler_step(ncores) for _ in range(4)][1:]
+        cpu_extra = {
+            "layer_predequantised": {"value": statistics.median(pre), "unit": "us",
+                                     "cores": ncores, "kind": "port",
+                                     "sample": "the same layer with every expert's weights "
+                                               "dequantised to fp32 before the timed region, "
+                                               "median of 3 after 1 warm-up"},
+            "sampler_step": {"value": statistics.median(samp), "unit": "us", "cores": ncores,
+                             "kind": "port",
+                             "sample": "one configs[2] step at step 24's temperature (entropy, "
+                                       "Philox Gumbel-max and argmax, acceptance) over all 256 "
+                                       "rows, median of 3 after 1 warm-up"}}
     # the kernel roofline is the single-GPU layer's (per-stage events exist only there)
     achieved = gemm1_bytes / (gemm1_ms * 1e-3) / 1e9 if gemm1_ms else None
     engine = os.environ.get("KNX_ENGINE", "auto")
@@ -716,6 +774,7 @@ def main():
         "gpu_launches": (EP_LAUNCHES_PER_LAYER if dist else LAUNCHES_PER_LAYER) * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
+        "cpu_baselines_extra": cpu_extra,
         "configs3_stack": cfg3,
         "configs4_prefill": cfg4,
         "sampler_selfcond": selfcond,

@@ -125,9 +125,11 @@ def gelu_tanh(x):
 
 
 def moe_layer(hidden, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, topk_ids, topk_w, gs_gu=128, gs_dn=64,
-              out_dtype=None, return_pairs=False):
+              out_dtype=None, return_pairs=False, dense=None):
     """One MoE layer on CPU.  Per pair p = t*k + j with expert e: out3[p] = f16(down_e(
-    f16(gelu(gate_e(x_t)) * up_e(x_t)))); y[t] = sum_j w[t,j] * f32(out3[p]) in j order."""
+    f16(gelu(gate_e(x_t)) * up_e(x_t)))); y[t] = sum_j w[t,j] * f32(out3[p]) in j order.
+    dense: optional list of (gate_up, down) fp32 weights per expert, dequantised beforehand
+    (dense_experts), used instead of dequantising inside the call."""
     T, H = hidden.shape
     tk = topk_ids.shape[1]
     E, twoI, _ = gu_q.shape
@@ -140,8 +142,11 @@ def moe_layer(hidden, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, topk_ids, topk_w, gs_g
         t_idx, j_idx = torch.where(ids == e)
         if t_idx.numel() == 0:
             continue
-        Wgu = dequant_w4(gu_q[e], gu_s[e], gu_z[e], gs_gu).float()
-        Wdn = dequant_w4(dn_q[e], dn_s[e], dn_z[e], gs_dn).float()
+        if dense is not None:
+            Wgu, Wdn = dense[e]
+        else:
+            Wgu = dequant_w4(gu_q[e], gu_s[e], gu_z[e], gs_gu).float()
+            Wdn = dequant_w4(dn_q[e], dn_s[e], dn_z[e], gs_dn).float()
         gu = x[t_idx] @ Wgu.T
         act = (gelu_tanh(gu[:, :I]) * gu[:, I:]).half().float()
         o = (act @ Wdn.T).half()
@@ -153,6 +158,12 @@ def moe_layer(hidden, gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, topk_ids, topk_w, gs_g
         y = y + torch.where(valid[:, j, None], w[:, j, None] * o3[:, j], torch.zeros(()))
     y = y.to(out_dtype or hidden.dtype)
     return (y, out3) if return_pairs else y
+
+
+def dense_experts(gu_q, gu_s, gu_z, dn_q, dn_s, dn_z, gs_gu=128, gs_dn=64):
+    """Every expert's weights dequantised once to fp32 (moe_layer(..., dense=...))."""
+    return [(dequant_w4(gu_q[e], gu_s[e], gu_z[e], gs_gu).float(),
+             dequant_w4(dn_q[e], dn_s[e], dn_z[e], gs_dn).float()) for e in range(gu_q.shape[0])]
 
 
 # ---------------------------------------------------------------------------------- RMSNorm
