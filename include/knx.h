@@ -210,7 +210,8 @@ KNX_API int knx_moe_combine(const void* out3, const int32_t* inv, const void* to
  * uint32), cnt [world][E] int32, receive rows [r_cap][H] f16, return rows [n_cap][H] f16.
  * peer_* are device arrays of `world` pointers to those regions on each rank (index = rank).
  * E = El * world, world <= 8, E <= 256; rank r owns the experts e = el * world + r (local
- * expert el; round-robin sharding, see ep_moe.shard_experts(..., interleaved=True)).  epoch: one more than the previous barrier's, the same
+ * expert el; round-robin sharding, see ep_moe.shard_experts(..., interleaved=True); when the
+ * counting sort relabels the experts (knx_moe_align_relabeled), e is the label).  epoch: one more than the previous barrier's, the same
  * on every rank (each call below that takes one is a barrier).  err: KNX_DEV_TIMEOUT when a
  * barrier waited 2 s.
  *   knx_ep_p2p_counts    counts[E] of this rank's pairs (knx_moe_align) to every peer; barrier;
