@@ -163,7 +163,7 @@ def _denoising_step_parity(self, decoder_forward, current_canvas, argmax_canvas,
         if copy_in_pass:
             # No finished.any() on the host (a device sync per step): the two B x L selects run
             # unconditionally, the copy above already holds the logits select, and the stopping
-            # test sees the logits as sampled (a cache hit).  Its verdict is OR-ed into
+            # test sees the logits as sampled (a cache hit).  Its result is OR-ed into
             # `finished`, so what it says about canvases already finished changes nothing.
             keep = finished_denoising[:, None]
             new_argmax = torch.where(keep, argmax_canvas, new_argmax)
