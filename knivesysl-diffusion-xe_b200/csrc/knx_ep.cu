@@ -99,6 +99,7 @@ struct GroupedWs {
   int4* tasks;
   int32_t* ntasks;
   int32_t* counters;
+  int n_counters;
   __half* out2;
   size_t bytes;
 };
@@ -114,7 +115,8 @@ GroupedWs carve_grouped(uint8_t* base, int64_t R, int64_t I, int E) {
   const int64_t max_tasks = (R + MIN_TASK_TOKENS - 1) / MIN_TASK_TOKENS + E;
   w.tasks = reinterpret_cast<int4*>(take(size_t(max_tasks) * 16));
   w.ntasks = reinterpret_cast<int32_t*>(take(16));
-  w.counters = reinterpret_cast<int32_t*>(take(16));
+  w.counters = reinterpret_cast<int32_t*>(take(size_t(gemm_counter_ints(max_tasks)) * 4));
+  w.n_counters = static_cast<int>(gemm_counter_ints(max_tasks));
   w.out2 = reinterpret_cast<__half*>(take(size_t(R) * I * 2));
   w.bytes = o;
   return w;
@@ -182,7 +184,8 @@ extern "C" int knx_moe_w4_grouped(const void* xrows, const int32_t* rows, int64_
   GroupedWs w = carve_grouped(static_cast<uint8_t*>(workspace), R, I, E);
   const int eng = moe_engine(flags, tokens_per_expert, H, I, gs_gu, gs_dn);
   int st = launch_tasks_from_offsets(offsets, E, engine_task_tokens(eng), w.tasks, w.ntasks,
-                                     w.counters, s);
+                                     w.counters,
+                                     eng == KNX_W4_WARP_WS ? w.n_counters : GEMM_COUNTERS, s);
   if (st != KNX_OK) return st;
   GemmArgs ga{};
   ga.xp = static_cast<const __half*>(xrows);

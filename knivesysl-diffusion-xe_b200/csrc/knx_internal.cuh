@@ -36,7 +36,7 @@ int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t
                        int32_t* offsets, int32_t* sorted_pair, int32_t* inv, void* scratch,
                        int32_t* err, cudaStream_t s, const int32_t* relabel = nullptr);
 int launch_tasks_from_offsets(const int32_t* offsets, int E, int m, int4* tasks, int32_t* ntasks,
-                              int32_t* counters, cudaStream_t s);
+                              int32_t* counters, int n_counters, cudaStream_t s);
 
 // tcgen05 grouped W4A16 GEMMs (knx_moe_tcp.cu): MMA M = the tokens of one task
 constexpr int TC_TASK_TOKENS = 128;  // tokens per task on the tcgen05 path
@@ -55,25 +55,39 @@ int launch_tc_rows(const __half* act, int64_t act_stride, int K, const int32_t* 
 constexpr int HW_TASK_TOKENS = 32;
 constexpr int MIN_TASK_TOKENS = 16;  // smallest task size of any engine (sizes the task list)
 bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated);
+// task_done (gate_up, may be NULL): one count per task, incremented once per finished item of
+// the task (after its rows are written), and *items_done once per finished item;
+// hw_gateup_items(I) items per task.
+int hw_gateup_items(int I);
 int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, const int32_t* offsets,
                      const int4* tasks, const int32_t* ntasks, int* counter, const uint8_t* gu_q,
                      const __half* gu_s, const __half* gu_z, int E, int H, int I, int ng, int gs,
-                     bool zint, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s);
+                     bool zint, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s,
+                     int* task_done = nullptr, int* items_done = nullptr);
+// task_ready (may be NULL): the down GEMM gathers a task's rows once task_ready[task] reaches
+// ready_target (or *items_done reaches ready_target * tasks), instead of waiting for the whole
+// previous kernel (programmatic dependent launch) before it starts; the other inputs must be
+// complete before the previous kernel started.
 int launch_hw_rows(const __half* act, int64_t act_stride, int K, const int32_t* offsets,
                    const int4* tasks, const int32_t* ntasks, int dense_rows, int* counter,
                    const uint8_t* wq, const __half* ws, const __half* wz, int E, int N, int ng,
                    int gs, bool zint, __half* out, int64_t out_stride, int64_t max_tasks,
-                   int32_t* err, cudaStream_t s);
+                   int32_t* err, cudaStream_t s, const int* task_ready = nullptr,
+                   int* items_done = nullptr, int ready_target = 0);
 
 // The grouped expert GEMMs of one MoE layer over a task list (knx_moe.cu).
+constexpr int GEMM_COUNTERS = 4;  // ints before the per-task ready counts in GemmArgs::counters
+inline int64_t gemm_counter_ints(int64_t max_tasks) { return GEMM_COUNTERS + max_tasks; }
 struct GemmArgs {
   const __half* xp;           // activation rows (K-interleaved f16)
   const int32_t* sorted_pair; // slot -> activation row * topk (+ k); NULL = row = slot
   int topk;
   const int32_t* offsets;     // [E + 1] slot offsets per expert
-  const int4* tasks;
+  const int4* tasks;          // (expert, first token in the expert, tokens, first slot)
   const int32_t* ntasks;
-  int32_t* counters;          // two work counters, zero at entry
+  int32_t* counters;          // GEMM_COUNTERS + max tasks ints, zero at entry: two work
+                              // counters, the finished gate_up items, then (from GEMM_COUNTERS)
+                              // one ready count per task
   const uint8_t* gu_q;
   const __half* gu_s;
   const __half* gu_z;

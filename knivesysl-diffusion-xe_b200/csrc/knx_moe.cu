@@ -472,6 +472,7 @@ struct MoeWs {
   int4* tasks;
   int32_t* ntasks;
   int32_t* counters;
+  int n_counters;
   __half* out2;
   __half* out3;
   void* align_scratch;  // multi-CTA counting sort (N > ALIGN_MAX_PAIRS only)
@@ -509,7 +510,8 @@ MoeWs carve_moe_ws(uint8_t* base, int64_t T, int64_t H, int64_t I, int E, int to
   w.inv = reinterpret_cast<int32_t*>(take(size_t(N) * 4));
   w.tasks = reinterpret_cast<int4*>(take(size_t(max_tasks) * 16));
   w.ntasks = reinterpret_cast<int32_t*>(take(16));
-  w.counters = reinterpret_cast<int32_t*>(take(16));
+  w.counters = reinterpret_cast<int32_t*>(take(size_t(gemm_counter_ints(max_tasks)) * 4));
+  w.n_counters = static_cast<int>(gemm_counter_ints(max_tasks));
   w.out2 = reinterpret_cast<__half*>(take(size_t(N) * I * 2));
   w.out3 = reinterpret_cast<__half*>(take(size_t(N) * H * 2));
   w.align_scratch = N > ALIGN_MAX_PAIRS ? take(align_large_scratch_bytes(N, E)) : nullptr;
@@ -563,14 +565,17 @@ int run_moe_gemms(const GemmArgs& a, int eng, int pc, cudaStream_t s) {
                           a.err, s);
   }
   if (eng == KNX_W4_WARP_WS) {
+    // gate_up counts the finished items of every task; down gathers a task's rows as soon as
+    // all of its gate_up items are written, so its CTAs work on the SMs gate_up's tail frees
+    int* ready = a.counters + GEMM_COUNTERS;
     st = launch_hw_gateup(a.xp, a.sorted_pair, a.topk, a.offsets, a.tasks, a.ntasks, a.counters,
                           a.gu_q, a.gu_s, a.gu_z, a.E, H, I, ng1, a.gs_gu, a.zint, a.out2,
-                          max_tasks, a.err, s);
+                          max_tasks, a.err, s, ready, a.counters + 2);
     if (st != KNX_OK) return st;
     prof::mark(pc, 2, s);
     return launch_hw_rows(a.out2, I, I, a.offsets, a.tasks, a.ntasks, 0, a.counters + 1, a.dn_q,
                           a.dn_s, a.dn_z, a.E, H, ng2, a.gs_dn, a.zint, a.out3, H, max_tasks,
-                          a.err, s);
+                          a.err, s, ready, a.counters + 2, hw_gateup_items(I));
   }
   if (!set_smem_attrs()) return KNX_E_DEVICE;
   const int sms = num_sms();
@@ -667,16 +672,18 @@ extern "C" int knx_moe_w4(const void* hidden, const void* hidden_perm, int hidde
     xp = w.xp;
   }
   const int eng = moe_engine(flags, T * topk / E, H, I, gs_gu, gs_dn);
+  // the per-task ready counts are used (and zeroed) by the ws engine only
+  const int nc = eng == KNX_W4_WARP_WS ? w.n_counters : GEMM_COUNTERS;
   if (align_supported(T * topk, E)) {
     st = launch_align(topk_ids, ids_dtype, static_cast<int>(T), topk, E, 0,
                       engine_task_tokens(eng), w.counts, w.offsets, w.sorted_pair, w.inv, nullptr,
-                      nullptr, nullptr, w.tasks, w.ntasks, w.counters, 2, err, s);
+                      nullptr, nullptr, w.tasks, w.ntasks, w.counters, nc, err, s);
   } else {
     st = launch_align_large(topk_ids, ids_dtype, T * topk, E, w.counts, w.offsets, w.sorted_pair,
                             w.inv, w.align_scratch, err, s);
     if (st == KNX_OK)
       st = launch_tasks_from_offsets(w.offsets, E, engine_task_tokens(eng), w.tasks, w.ntasks,
-                                     w.counters, s);
+                                     w.counters, nc, s);
   }
   if (st != KNX_OK) return st;
   prof::mark(pc, 1, s);

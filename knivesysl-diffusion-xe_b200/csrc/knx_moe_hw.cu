@@ -74,7 +74,7 @@ constexpr uint32_t PROD_BACKOFF_NS = KNX_HW_PROD_BACKOFF;
 
 struct Item {
   int valid, e, cnt, slice;
-  int slot0, nvalid, pad0, pad1;
+  int slot0, nvalid, task, pad;
 };
 
 struct Ctrl {
@@ -90,7 +90,6 @@ struct Params {
   int64_t act_stride;
   const int32_t* sorted_pair;
   int topk;
-  const int32_t* offsets;
   const int4* tasks;
   const int32_t* ntasks;
   int dense_rows;
@@ -105,6 +104,16 @@ struct Params {
   int sw;  // weight ring depth (stages)
   int sa;  // activation ring depth (stages)
   int32_t* err;
+  // Task readiness between the two GEMMs of a layer.  task_done (gated kernel only): incremented
+  // once per finished item of a task, after all its output rows are written, and *items_done
+  // once per finished item.  task_ready (plain kernel only; NULL = wait for the previous kernel):
+  // a task's rows are gathered once task_ready[task] reaches ready_target (items per task), or
+  // at once after *items_done has reached ready_target * tasks; the kernel then starts without
+  // waiting for the previous kernel to finish.
+  int* task_done;
+  const int* task_ready;
+  int* items_done;
+  int ready_target;
 };
 
 KNX_HOST_DEVINL size_t sz_slot_bytes(int ng) { return static_cast<size_t>(ROWS) * ng * 4; }
@@ -187,7 +196,12 @@ KNX_DEVINL void mma_stage(uint32_t wa, uint32_t ab, int jmax, int grp0,
 template <bool GATED, bool ZINT, int GPJ>
 __global__ void __launch_bounds__(NTHREADS, 1)
     hw_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const Params p) {
-  pdl_wait_trigger();
+  // With per-task readiness the kernel runs alongside the tail of the previous one (its CTAs take
+  // the SMs that kernel's CTAs leave): the activation rows are read only after their task's
+  // count is complete, and the task list and counters were written before the previous kernel
+  // started (they are read from L2 below).
+  if (!GATED && p.task_ready) asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  else pdl_wait_trigger();
   extern __shared__ uint8_t dsm_raw[];
   __shared__ Ctrl ctrl;
   // 1024-byte aligned base (the 128-byte swizzle needs it), by an offset from dsm_raw so that the
@@ -231,14 +245,31 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       // the packed weights stream through once per task: evict them first, so that the
       // intermediates (out2 for the down GEMM, out3 for the combine) stay in L2
       const uint64_t wpol = l2_policy_evict_first();
-      const int nwork = (p.tasks ? *p.ntasks : (p.dense_rows + TOK - 1) / TOK) * p.nslices;
+      // the plain kernel may start before the previous kernel has finished (task_ready): its
+      // task list is read from L2
+      const int ntasks = p.tasks ? (GATED ? *p.ntasks : __ldcg(p.ntasks)) : 0;
+      const int nwork = (p.tasks ? ntasks : (p.dense_rows + TOK - 1) / TOK) * p.nslices;
       uint32_t wst = 0;            // stages issued
       uint32_t wsl = 0, wph = 0;   // next ring slot and its phase parity
       int last_on_slot[IR];  // newest item per slot whose scale/zero copies were issued (-1: none)
       for (int i = 0; i < IR; ++i) last_on_slot[i] = -1;
+      // gated kernel with task readiness: an item is counted once its slot's i_empty phase has
+      // completed, i.e. every math warp has written its rows and arrived (release at CTA scope);
+      // that wait acquires, and the GPU-scope fence here orders all those rows before the counts.
+      // The producer, not a math warp, pays for the fence, after it has issued the next item's
+      // first weight stage.
+      auto count_done = [&](int task) {
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        fence_proxy_async_global();
+        atomicAdd(p.task_done + task, 1);
+        atomicAdd(p.items_done, 1);
+      };
       for (int n = 0;; ++n) {
         const int slot = n % IR;
         if (!wait(&ctrl.i_empty[slot], ((n / IR) & 1) ^ 1, PROD_BACKOFF_NS)) break;
+        // the item that last used this slot (n - IR), now finished, is counted below
+        int done_task =
+            (GATED && p.task_done && last_on_slot[slot] >= 0) ? ctrl.items[slot].task : -1;
         const int wi = atomicAdd(p.work_counter, 1);
         Item it{};
         if (wi < nwork) {
@@ -255,14 +286,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             task = wi - ntask * nfull_sl;
             it.slice = nfull_sl;
           }
-          int t0;
           if (p.tasks) {
-            const int4 tk = p.tasks[task];
-            it.e = tk.x; t0 = tk.y; it.cnt = tk.z;
+            // (expert, first token, tokens, first slot)
+            const int4 tk = GATED ? p.tasks[task] : __ldcg(p.tasks + task);
+            it.e = tk.x; it.cnt = tk.z; it.slot0 = tk.w;
           } else {
-            it.e = 0; t0 = task * TOK; it.cnt = min(TOK, p.dense_rows - t0);
+            it.e = 0; it.slot0 = task * TOK; it.cnt = min(TOK, p.dense_rows - it.slot0);
           }
-          it.slot0 = (p.offsets ? p.offsets[it.e] : 0) + t0;
+          it.task = task;
           it.nvalid = GATED ? min(GROWS, p.I - it.slice * GROWS)
                             : min(ROWS, p.rows_per_expert - it.slice * ROWS);
           it.valid = 1;
@@ -271,6 +302,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (!it.valid) {
           last_on_slot[slot] = -1;
           mbar_arrive(&ctrl.i_full[slot]);
+          if (GATED && done_task >= 0) count_done(done_task);
           break;
         }
         last_on_slot[slot] = n;
@@ -311,8 +343,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tma_load_2d_hint(dst, &wmap, &ctrl.w_full[s], x, y, wpol);
             tma_load_2d_hint(dst + BOX_ROWS * WROW, &wmap, &ctrl.w_full[s], x, y + BOX_ROWS, wpol);
           }
+          if (GATED && done_task >= 0) {
+            count_done(done_task);
+            done_task = -1;
+          }
         }
+        if (GATED && done_task >= 0) count_done(done_task);  // the stage loop gave up
         if (*abort_flag) break;
+      }
+      // the valid items posted after the last one counted above (the others were counted when
+      // their slot was reused)
+      if (GATED && p.task_done && !*abort_flag) {
+        for (int i = 0; i < IR; ++i) {
+          const int m = last_on_slot[i];
+          if (m >= 0 && wait(&ctrl.i_empty[i], (m / IR) & 1, PROD_BACKOFF_NS))
+            count_done(ctrl.items[i].task);
+        }
       }
       // Copies already issued must land before the CTA exits (only pending after an abort): the
       // newest phase of every weight stage and of every item slot is waited for, bounded.
@@ -326,6 +372,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // ---------------------------------------------------------------- activation gather
     uint32_t ast = 0;            // stages issued
     uint32_t asl = 0, aph = 0;   // next ring slot and its phase parity
+    int ready_task = -1;         // task whose rows are known to be written (task_ready)
+    bool all_ready = false;      // every task's rows are written
     for (int n = 0;; ++n) {
       const int slot = n % IR;
       // lane 0 waits and the warp follows its answer (a timeout is seen by every lane alike)
@@ -337,6 +385,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctrl.i_empty[slot]);
         break;
+      }
+      if (!GATED && p.task_ready && !all_ready && it.task != ready_task) {
+        // the task's rows are complete once every item of it has been counted (or every item
+        // of every task): lane 0 waits (acquire), the warp barrier orders the lanes after it,
+        // and each lane's proxy fence orders its bulk copies below after the rows
+        bool rd = true, all = false;
+        if (lane == 0) {
+          all = ld_acquire_gpu(p.items_done) >= __ldcg(p.ntasks) * p.ready_target;
+          rd = all || (!*abort_flag && wait_count_geq(p.task_ready + it.task, p.ready_target));
+          if (!rd && !*abort_flag) {
+            *abort_flag = 1;
+            if (p.err) atomicOr(p.err, KNX_DEV_TIMEOUT);
+          }
+        }
+        rd = __shfl_sync(0xffffffffu, rd, 0);
+        all_ready = __shfl_sync(0xffffffffu, all, 0);
+        __syncwarp();
+        if (!rd) break;
+        fence_proxy_async_global();
+        ready_task = it.task;
       }
       const __half* src = nullptr;
       if (lane < it.cnt)
@@ -565,15 +633,20 @@ bool hw_supported(int64_t K, int gs, int ng, int64_t rows_per_expert, bool gated
   return rows_per_expert % 16 == 0;
 }
 
+int hw_gateup_items(int I) { return (I + hw::GROWS - 1) / hw::GROWS; }
+
 int launch_hw_gateup(const __half* xp, const int32_t* sorted_pair, int topk, const int32_t* offsets,
                      const int4* tasks, const int32_t* ntasks, int* counter, const uint8_t* gu_q,
                      const __half* gu_s, const __half* gu_z, int E, int H, int I, int ng, int gs,
-                     bool zint, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s) {
+                     bool zint, __half* out2, int64_t max_tasks, int32_t* err, cudaStream_t s,
+                     int* task_done, int* items_done) {
+  if (task_done && !(items_done && tasks)) return KNX_E_INVALID;
   hw::Params p{};
-  p.act = xp; p.act_stride = H; p.sorted_pair = sorted_pair; p.topk = topk; p.offsets = offsets;
+  p.act = xp; p.act_stride = H; p.sorted_pair = sorted_pair; p.topk = topk;
   p.tasks = tasks; p.ntasks = ntasks; p.work_counter = counter; p.ws = gu_s; p.wz = gu_z;
   p.K = H; p.rows_per_expert = 2 * I; p.I = I; p.ng = ng; p.gs = gs; p.out = out2;
-  p.out_stride = I; p.nslices = (I + hw::GROWS - 1) / hw::GROWS; p.err = err;
+  p.out_stride = I; p.nslices = hw_gateup_items(I); p.err = err; p.task_done = task_done;
+  p.items_done = items_done;
   p.partial_last = (I % hw::GROWS) != 0 && p.nslices > 1;
   const int64_t work = max_tasks * p.nslices;
   return zint ? launch_hw<true, true>(p, gu_q, int64_t(E) * 2 * I, H / 2, work, s)
@@ -584,12 +657,15 @@ int launch_hw_rows(const __half* act, int64_t act_stride, int K, const int32_t* 
                    const int4* tasks, const int32_t* ntasks, int dense_rows, int* counter,
                    const uint8_t* wq, const __half* ws, const __half* wz, int E, int N, int ng,
                    int gs, bool zint, __half* out, int64_t out_stride, int64_t max_tasks,
-                   int32_t* err, cudaStream_t s) {
+                   int32_t* err, cudaStream_t s, const int* task_ready, int* items_done,
+                   int ready_target) {
+  if (task_ready && !(items_done && tasks)) return KNX_E_INVALID;
   hw::Params p{};
-  p.act = act; p.act_stride = act_stride; p.offsets = offsets; p.tasks = tasks; p.ntasks = ntasks;
+  p.act = act; p.act_stride = act_stride; p.tasks = tasks; p.ntasks = ntasks;
   p.dense_rows = dense_rows; p.work_counter = counter; p.ws = ws; p.wz = wz; p.K = K;
   p.rows_per_expert = N; p.ng = ng; p.gs = gs; p.out = out; p.out_stride = out_stride;
   p.nslices = (N + hw::ROWS - 1) / hw::ROWS; p.err = err;
+  p.task_ready = task_ready; p.items_done = items_done; p.ready_target = ready_target;
   p.partial_last = (N % hw::ROWS) != 0 && p.nslices > 1;
   const int64_t work = max_tasks * p.nslices;
   return zint ? launch_hw<false, true>(p, wq, int64_t(E) * N, K / 2, work, s)

@@ -156,8 +156,8 @@ __global__ void __launch_bounds__(256)
 // holding the same expert id (match_by_bits), so the rank of pair p inside its expert is
 //   (pairs of that expert in earlier warps) + (earlier pairs in the same warp),
 // which is exactly the stable order.  Also builds the GEMM task list (expert token chunks of at
-// most m_max, ordered by chunk size descending, then expert, then chunk) and zeroes the GEMMs'
-// dynamic work counters.
+// most m_max, ordered by chunk size descending, then expert, then chunk; each task is
+// (expert, first token in the expert, tokens, first slot)) and zeroes the GEMMs' counters.
 constexpr int AL_THREADS = 1024;
 constexpr int AL_WH = 33;  // per-expert row of the 32 warps' counts, padded: [E][AL_WH]
 
@@ -266,7 +266,7 @@ __global__ void __launch_bounds__(AL_THREADS)
 
   for (int i = tid; i < AL_WH * E; i += AL_THREADS) whist[i] = 0;
   for (int i = tid; i <= m_max; i += AL_THREADS) size_hist[i] = 0;
-  if (tid < n_work_counters) work_counters[tid] = 0;
+  for (int i = tid; i < n_work_counters; i += AL_THREADS) work_counters[i] = 0;
   int bad = 0;
   for (int p = tid; p < N; p += AL_THREADS)
     sid[p] = static_cast<int16_t>(pair_label(ids, ids_dtype, p, E, relabel, bad));
@@ -422,11 +422,12 @@ __global__ void __launch_bounds__(AL_THREADS)
     __syncthreads();
     if (e_me < E && cnt > 0) {
       for (int j = 0; j < nfull; ++j)
-        tasks[size_hist[m_max] + fpre + j] = make_int4(e_me, j * m_max, m_max, 0);
+        tasks[size_hist[m_max] + fpre + j] = make_int4(e_me, j * m_max, m_max, off + j * m_max);
       if (rem > 0) {
         int before_same = rank_w;
         for (int w2 = 0; w2 < warp; ++w2) before_same += rhist[w2 * RH + rem];
-        tasks[size_hist[rem] + before_same] = make_int4(e_me, nfull * m_max, rem, 0);
+        tasks[size_hist[rem] + before_same] =
+            make_int4(e_me, nfull * m_max, rem, off + nfull * m_max);
       }
     }
   }
@@ -434,10 +435,10 @@ __global__ void __launch_bounds__(AL_THREADS)
 
 // Task list (expert token chunks of at most m) from per-expert slot offsets, largest chunks first
 // (full chunks in expert order, then remainders by size, in expert order within a size), plus the
-// task count and two zeroed work counters: the same list the align kernel builds.  One CTA.
+// task count and n_counters zeroed counters: the same list the align kernel builds.  One CTA.
 __global__ void tasks_from_offsets_kernel(const int32_t* __restrict__ offsets, int E, int m,
                                           int4* __restrict__ tasks, int32_t* __restrict__ ntasks,
-                                          int32_t* __restrict__ counters) {
+                                          int32_t* __restrict__ counters, int n_counters) {
   pdl_wait_trigger();
   __shared__ int full_pre[257];
   __shared__ int rem_of[256];
@@ -445,6 +446,7 @@ __global__ void tasks_from_offsets_kernel(const int32_t* __restrict__ offsets, i
   __shared__ int rem_start[MAX_TASK_TOKENS + 1];
   const int tid = threadIdx.x;
   for (int r = tid; r <= m; r += blockDim.x) rem_cnt[r] = 0;
+  for (int i = tid; i < n_counters; i += blockDim.x) counters[i] = 0;
   __syncthreads();
   if (tid < E) {
     const int rem = (offsets[tid + 1] - offsets[tid]) % m;
@@ -464,18 +466,18 @@ __global__ void tasks_from_offsets_kernel(const int32_t* __restrict__ offsets, i
       acc += rem_cnt[r];
     }
     *ntasks = acc;
-    counters[0] = 0;
-    counters[1] = 0;
   }
   __syncthreads();
   if (tid < E) {
     const int cnt = offsets[tid + 1] - offsets[tid];
     const int nfull = cnt / m, rem = cnt % m;
-    for (int j = 0; j < nfull; ++j) tasks[full_pre[tid] + j] = make_int4(tid, j * m, m, 0);
+    const int first = offsets[tid];
+    for (int j = 0; j < nfull; ++j)
+      tasks[full_pre[tid] + j] = make_int4(tid, j * m, m, first + j * m);
     if (rem > 0) {
       int before = 0;
       for (int e = 0; e < tid; ++e) before += rem_of[e] == rem;
-      tasks[rem_start[rem] + before] = make_int4(tid, nfull * m, rem, 0);
+      tasks[rem_start[rem] + before] = make_int4(tid, nfull * m, rem, first + nfull * m);
     }
   }
 }
@@ -683,9 +685,10 @@ int launch_align_large(const void* ids, int ids_dtype, int64_t N, int E, int32_t
 }
 
 int launch_tasks_from_offsets(const int32_t* offsets, int E, int m, int4* tasks, int32_t* ntasks,
-                              int32_t* counters, cudaStream_t s) {
-  if (E > 256 || m < 1 || m > MAX_TASK_TOKENS) return KNX_E_UNSUPPORTED;
-  (void)launch_pdl(tasks_from_offsets_kernel, 1, 256, 0, s, offsets, E, m, tasks, ntasks, counters);
+                              int32_t* counters, int n_counters, cudaStream_t s) {
+  if (E > 256 || m < 1 || m > MAX_TASK_TOKENS || n_counters < 0) return KNX_E_UNSUPPORTED;
+  (void)launch_pdl(tasks_from_offsets_kernel, 1, 256, 0, s, offsets, E, m, tasks, ntasks, counters,
+                   n_counters);
   return launch_status();
 }
 

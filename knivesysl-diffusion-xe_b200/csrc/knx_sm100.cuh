@@ -79,6 +79,28 @@ KNX_DEVINL void cp_async_mbar_arrive_noinc(uint64_t* bar) {
 KNX_DEVINL void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Orders this thread's view of global memory (generic proxy) with its later bulk / TMA copies.
+KNX_DEVINL void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// ---- counters written by other CTAs --------------------------------------------------------
+KNX_DEVINL int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Wait (acquire) until *cnt >= target; false after `limit_ns`.
+KNX_DEVINL bool wait_count_geq(const int* cnt, int target, uint64_t limit_ns = 2000000000ull,
+                               uint32_t backoff_ns = 128) {
+  if (ld_acquire_gpu(cnt) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  while (ld_acquire_gpu(cnt) < target) {
+    __nanosleep(backoff_ns);
+    if (globaltimer() - t0 > limit_ns) return false;
+  }
+  return true;
+}
 
 // ---- TMA ----------------------------------------------------------------------------------
 KNX_DEVINL void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
