@@ -24,6 +24,10 @@
 //     output columns per token in a private shared area and writes 16-byte chunks, so the math
 //     warps never wait for one another; the gated output is written in the K-interleave the
 //     down GEMM reads.
+//   * gate_up -> down by task: gate_up's weight producer counts each finished item of a task
+//     (after every math warp has released the slot, one GPU-scope fence), and the down kernel,
+//     which does not wait for gate_up to finish, gathers a task's rows once its count is
+//     complete.  Down's CTAs thus run on the SMs that gate_up's last items leave idle.
 // All waits are bounded (2 s): on a timeout the kernel sets KNX_DEV_TIMEOUT and every role
 // leaves at the next work-item boundary (each math warp decides by a warp vote); the producers
 // wait (bounded) for their copies in flight before the CTA exits.
