@@ -23,6 +23,19 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) == set(_knx.exported_symbols())
 
 
+def test_integration_stubs_match_the_signature_table():
+    """The ctypes stubs a maintainer of the reference would copy from INTEGRATION.md declare the
+    same argument types as the library's own binding table."""
+    types = {"vp": ctypes.c_void_p, "i64": ctypes.c_int64, "i32": ctypes.c_int,
+             "f32": ctypes.c_float, "sz": ctypes.c_size_t}
+    text = (REPO / "INTEGRATION.md").read_text()
+    stubs = re.findall(r"lib\.(knx_\w+)\.argtypes = \[([^\]]*)\]", text)
+    assert len(stubs) >= 15
+    for name, args in stubs:
+        got = [types[a.strip()] for a in args.replace("\n", " ").split(",") if a.strip()]
+        assert got == list(_knx._SIGS[name][1]), name
+
+
 def test_status_strings_and_version():
     lib = _knx.load()
     assert lib.knx_version() > 0
