@@ -20,11 +20,14 @@ import torch
 from _knx import (KNX_DEV_BAD_EXPERT_ID, KNX_DEV_TIMEOUT, KNX_W4_INT_ZEROS, check, dtype_code, engine_flags, load,
                   ptr, require_device, stream_of, workspace, zero_flags)
 
-# Tile constants of the sm_100a kernels (reported for parity with the reference's module globals;
-# the kernels do not use BM-padded blocks: tasks are expert token chunks of at most 32).
+# Module globals named as in the reference (which tunes its Triton launches with them).  Here they
+# describe the plain mma.sync engine (engine="mma") only; the default engines take other tiles:
+# "ws" 128 gate + 128 up (gate_up) or 256 (down) weight rows per work item and 256 k per stage,
+# "tc" 128 tokens x 256 weight rows per MMA.  No engine uses BM-padded blocks: tasks are expert
+# token chunks (at most 32 tokens for "ws" and "mma", 128 for "tc").
 BM_V2 = 32
-G1 = dict(BN=64, BK=256, stages=4)   # gate_up+GELU: 64 gate + 64 up rows per CTA tile
-G2 = dict(BN=128, BK=128, stages=5)  # down: 128 output rows per CTA tile
+G1 = dict(BN=64, BK=256, stages=4)   # mma gate_up+GELU: 64 gate + 64 up rows per CTA tile
+G2 = dict(BN=128, BK=128, stages=5)  # mma down: 128 output rows per CTA tile
 
 _TANH_GELU_NAMES = ("gelu_pytorch_tanh", "gelu_new", "gelu_tanh", "quick_gelu_tanh")
 
