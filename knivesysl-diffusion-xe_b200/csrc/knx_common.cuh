@@ -33,6 +33,8 @@ inline int launch_status() {
 // completed and its writes are visible (at once when the previous launch was an ordinary one),
 // then allows the next kernel to start launching in turn.  The next kernel is only scheduled once
 // every CTA of this one has started, so an early start never takes an SM this kernel still needs.
+// (The ws down GEMM with per-task readiness skips the wait: it synchronises with gate_up through
+// per-task counters instead; knx_moe_hw.cu.)
 template <typename... KArgs, typename... Args>
 inline int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
                       Args&&... args) {
